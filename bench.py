@@ -1,0 +1,425 @@
+"""Benchmark of the d3 prefill hot path on B200 (one JSON line on rank 0).
+
+Headline workload (BASELINE config 3a, "question-blocks/s at 4k state"): the
+question pass of one full-attention layer — 16 question blocks of 64 tokens
+attending to a 4096-token state plus their own block, 32 query heads, 4 KV
+heads, head_dim 128, bf16 — through the sm_100a prefix-bidirectional kernel.
+A step = one such pass; value = question blocks per second over all ranks.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+* value / ms_per_step: device time of the attention kernel (CUDA events on its
+  stream), inputs resident in HBM, L2 flushed (a 256 MiB write) before every
+  timed step; max over ranks.
+* e2e: the same metric through the public API ``prefix_bidir_attention`` with
+  the step's question inputs (q, k_q, v_q) copied from pinned host memory and
+  the output copied back inside the timed region; the state K/V is the
+  resident snapshot (computed once per request in the state-once design).
+* extra: state pass, config 3b (16384-token state + 255 blocks of 48), the
+  W8A8 GEMM at config 2 (e4m3 and int8) with the act-quant kernel, and the
+  readout, each timed the same way and reported in TFLOP/s or GB/s.
+* cpu_baseline: the CPU oracle's question pass (a restatement of
+  ops.sdpa_questions in fp32) on all host threads, over a bounded sample.
+
+Multi-GPU (torchrun, NCCL): rank 0 builds the state K/V and broadcasts it to
+every rank (the one exchange step, reported separately); each rank then runs
+its own 16 question blocks per step (weak scaling, no collective per step).
+``--impl reference`` times the reference algorithm's CPU path (the oracle port)
+on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CFG3A = dict(B=16, H=32, Hkv=4, L=64, D=128, S=4096)
+CFG3B = dict(B=255, H=32, Hkv=4, L=48, D=128, S=16384)
+METRIC = "question-blocks/s at 4k state"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def attn_flops(B, H, L, D, S, **_):
+    """4*H*D*sum_b Lq*(S+Lq) (matmul FLOPs of QK^T and PV)."""
+    return 4.0 * H * D * B * L * (S + L)
+
+
+def load_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        d["source"] = "measured"
+        return d
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def profile_traffic(name: str) -> float | None:
+    """dram_bytes_per_launch recorded from an ncu capture in profiles/<name>."""
+    p = ROOT / "profiles" / name
+    if not p.exists():
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_question_inputs(cfg, seed, device, with_state=True):
+    g = torch.Generator().manual_seed(seed)
+    B, H, Hkv, L, D, S = (cfg[k] for k in ("B", "H", "Hkv", "L", "D", "S"))
+    # model layout: q/k/v come out of the projections as [B, L, heads, D]
+    q = torch.randn(B, L, H, D, generator=g).to(torch.bfloat16).permute(0, 2, 1, 3)
+    kq = torch.randn(B, L, Hkv, D, generator=g).to(torch.bfloat16).permute(0, 2, 1, 3)
+    vq = torch.randn(B, L, Hkv, D, generator=g).to(torch.bfloat16).permute(0, 2, 1, 3)
+    out = {"q": q, "kq": kq, "vq": vq}
+    if with_state:
+        out["ks"] = torch.randn(S, Hkv, D, generator=g).to(torch.bfloat16).permute(1, 0, 2)
+        out["vs"] = torch.randn(S, Hkv, D, generator=g).to(torch.bfloat16).permute(1, 0, 2)
+    if device is not None:
+        out = {k: v.to(device) for k, v in out.items()}
+    return out
+
+
+def time_steps(fn, steps, warmup, stream, flush):
+    """Per-step device time (ms) of fn() with an L2 flush before every step."""
+    for _ in range(warmup):
+        flush()
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(steps):
+        flush()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        fn()
+        b.record(stream)
+        times.append((a, b))
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in times]
+
+
+def cpu_baseline_questions(cfg, target_s=10.0):
+    """The oracle's fp32 question pass on all host threads; blocks/s over a bounded sample."""
+    from oracle import attention as oattn
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    one = dict(cfg, B=1)
+    inp = make_question_inputs(one, 99, None)
+    fn = lambda: oattn.questions(inp["q"], inp["ks"], inp["vs"], inp["kq"], inp["vq"], [one["L"]], one["D"] ** -0.5,
+                                 dtype=torch.float32)
+    fn()  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= target_s or n >= 64:
+            break
+    return {"value": n / el, "unit": "question-blocks/s", "cores": threads, "kind": "port",
+            "sample": f"{n} question blocks of config 3a ({one['L']} tokens vs a {one['S']}-token state, "
+                      f"H{one['H']}/Hkv{one['Hkv']}/D{one['D']}), oracle fp32 torch CPU, {el:.1f} s"}
+
+
+def run_reference(args):
+    """--impl reference: the reference algorithm's CPU path (oracle port) on rank 0."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import attention as oattn
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    sample = 2  # question blocks per step: keeps K steps within a few minutes on the host
+    one = dict(CFG3A, B=sample)
+    inp = make_question_inputs(one, 7, None)
+    fn = lambda: oattn.questions(inp["q"], inp["ks"], inp["vs"], inp["kq"], inp["vq"], [one["L"]] * sample,
+                                 one["D"] ** -0.5, dtype=torch.float32)
+    for _ in range(args.warmup):
+        fn()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        fn()
+    el = time.perf_counter() - t0
+    value = sample * args.steps / el
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "question-blocks/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "cfg3a question pass (4096-token state + 16 x 64-token blocks, H32/Hkv4/D128)",
+                   "sample_blocks_per_step": sample, "l2": "n/a (CPU)"},
+        "cpu_baseline": {"value": value, "unit": "question-blocks/s", "cores": threads, "kind": "port",
+                         "sample": f"{sample} blocks per step, oracle restatement of ops.sdpa_questions, fp32 torch CPU"},
+        "e2e": {"value": value, "unit": "question-blocks/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-extra", action="store_true", help="skip the secondary workloads")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch.distributed as dist
+    import d3_turbo_trt_b200 as d3b
+    from d3_turbo_trt_b200 import _lib, dist as d3dist
+    from d3_turbo_trt_b200.kernels import prefix_bidir as pb
+    from d3_turbo_trt_b200.model import quant
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    stream = torch.cuda.current_stream(dev)
+    flush_buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush = lambda: flush_buf.fill_(1)
+    peaks = load_peaks()
+    cfg = CFG3A
+    scale = cfg["D"] ** -0.5
+
+    # ---- state K/V: built on rank 0, broadcast over NCCL (the exchange step) ----
+    state = make_question_inputs(cfg, 1, dev if rank == 0 else None, with_state=True)
+    ks = torch.empty(cfg["S"], cfg["Hkv"], cfg["D"], dtype=torch.bfloat16, device=dev)
+    vs = torch.empty_like(ks)
+    if rank == 0:
+        ks.copy_(state["ks"].permute(1, 0, 2))
+        vs.copy_(state["vs"].permute(1, 0, 2))
+    bcast_ms = None
+    if world > 1:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        t0.record(stream)
+        d3dist.broadcast_state_kv([(ks, vs)], src=0)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        bcast_ms = t0.elapsed_time(t1)
+    ks_v, vs_v = ks.permute(1, 0, 2), vs.permute(1, 0, 2)  # [Hkv, S, D] token-major views
+
+    # ---- this rank's question blocks ----
+    inp = make_question_inputs(cfg, 100 + rank, dev, with_state=False)
+    lens = [cfg["L"]] * cfg["B"]
+    out = torch.empty(cfg["B"], cfg["H"], cfg["L"], cfg["D"], dtype=torch.bfloat16, device=dev)
+    step = lambda: pb.prefix_bidir_attention(inp["q"], ks_v, vs_v, inp["kq"], inp["vq"], lens, scale=scale, out=out)
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        times = time_steps(step, args.steps, max(args.warmup, 3), stream, flush)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+    total_ms = sum(times)
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    value = cfg["B"] * world / (ms_per_step / 1e3)
+    flops = attn_flops(**cfg)
+    achieved_tflops = flops / (ms_per_step / 1e3) / 1e12  # per GPU (each rank runs one launch per step)
+
+    # ---- e2e through the public API with host buffers ----
+    host = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in
+            (("q", inp["q"].contiguous()), ("kq", inp["kq"].contiguous()), ("vq", inp["vq"].contiguous()))}
+    for k in host:
+        host[k].copy_(inp[k].contiguous().cpu())
+    host_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    dev_in = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
+
+    def e2e_step():
+        for k in host:
+            dev_in[k].copy_(host[k], non_blocking=True)
+        o = pb.prefix_bidir_attention(dev_in["q"], ks_v, vs_v, dev_in["kq"], dev_in["vq"], lens, scale=scale)
+        host_out.copy_(o, non_blocking=True)
+
+    e2e_times = time_steps(e2e_step, args.steps, max(args.warmup, 3), stream, flush)
+    e2e_ms = sum(e2e_times) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = host_out.numel() * host_out.element_size()
+
+    extra = {}
+    if not args.no_extra:
+        extra = secondary(dev, stream, flush, peaks, quant, pb, d3b)
+    if world > 1:
+        dist.barrier()
+
+    if rank == 0:
+        cpu = None if args.no_cpu else cpu_baseline_questions(cfg)
+        traffic = profile_traffic("prefix_bidir_cfg3a.md")
+        peak = peaks["bf16_tflops"]
+        line = {
+            "metric": METRIC, "value": value, "unit": "question-blocks/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) q/k/v)",
+            "config": {"workload": "cfg3a question pass: 16 blocks x 64 tokens over a 4096-token state, "
+                                   "H32/Hkv4/D128 bf16, one layer, per rank",
+                       "question_blocks_per_rank": cfg["B"], "state_tokens": cfg["S"], "block_tokens": cfg["L"],
+                       "parallelism": f"dp{world} (question-block sharding, state KV broadcast once)",
+                       "l2": "flushed before every timed step (256 MiB write)"},
+            "roofline": {"bound": "tensor", "achieved": achieved_tflops, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved_tflops / peak, "traffic": traffic,
+                         "kernel": "prefix_bidir_kernel<128,128,bf16>",
+                         "algorithmic_flops_per_launch": flops,
+                         "peak_source": f"{peaks['source']} bf16 dense (burst)"},
+            "e2e": {"value": cfg["B"] * world / (e2e_ms / 1e3), "unit": "question-blocks/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                    "api": "d3_turbo_trt_b200.kernels.prefix_bidir.prefix_bidir_attention"},
+            "gpu_launches": args.steps,
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+            "state_kv_broadcast_ms": bcast_ms,
+            "extra": extra,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def secondary(dev, stream, flush, peaks, quant, pb, d3b):
+    """State pass, config 3b, W8A8 GEMM (config 2), act quant and readout."""
+    res = {}
+    bf16_peak = peaks["bf16_tflops"]
+    # state pass of config 3a: [1, 32, 4096, 128] over [1, 4, 4096, 128]
+    g = torch.Generator().manual_seed(3)
+    S, H, Hkv, D = 4096, 32, 4, 128
+    q = torch.randn(1, S, H, D, generator=g).to(torch.bfloat16).to(dev).permute(0, 2, 1, 3)
+    k = torch.randn(1, S, Hkv, D, generator=g).to(torch.bfloat16).to(dev).permute(0, 2, 1, 3)
+    v = torch.randn(1, S, Hkv, D, generator=g).to(torch.bfloat16).to(dev).permute(0, 2, 1, 3)
+    t = statistics.median(time_steps(lambda: pb.state_attention(q, k, v, scale=D ** -0.5), 10, 3, stream, flush))
+    fl = 4.0 * H * D * S * S
+    res["state_pass_4k"] = {"ms": t, "tflops": fl / t / 1e9, "frac_bf16_peak": fl / t / 1e9 / bf16_peak}
+    del q, k, v
+    # config 3b: 16384-token state + 255 blocks of 48
+    inp = make_question_inputs(CFG3B, 4, dev)
+    lens = [48] * 255
+    t = statistics.median(time_steps(lambda: pb.prefix_bidir_attention(
+        inp["q"], inp["ks"], inp["vs"], inp["kq"], inp["vq"], lens, scale=D ** -0.5), 5, 3, stream, flush))
+    fl = attn_flops(**CFG3B)
+    res["cfg3b_question_pass"] = {"ms": t, "blocks_per_s": 255 / (t / 1e3), "tflops": fl / t / 1e9,
+                                  "frac_bf16_peak": fl / t / 1e9 / bf16_peak}
+    del inp
+    # config 2: W8A8 [4096, 5120] x [13824, 5120]^T
+    M, K, N = 4096, 5120, 13824
+    x = torch.randn(M, K, generator=g)
+    cols = torch.randperm(K, generator=g)[: K // 100]
+    x[:, cols] *= 20.0
+    x = x.to(torch.bfloat16).to(dev)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+    gemm_flops = 2.0 * M * N * K
+    fp8_peak = 2 * bf16_peak  # dense e4m3 / int8 rate is twice bf16 on B200
+    for mode in ("fp8", "int8"):
+        layer = quant.QuantLinear(K, N, mode=mode, dtype=torch.bfloat16, device=dev)
+        layer.load_full(w)
+        qa, sa = quant.quantize_rows(x, mode)
+        tg = statistics.median(time_steps(lambda: quant.scaled_mm(qa, layer.weight, sa, layer.weight_scale,
+                                                                   out_dtype=torch.bfloat16), 10, 3, stream, flush))
+        tq = statistics.median(time_steps(lambda: quant.quantize_rows(x, mode), 10, 3, stream, flush))
+        tl = statistics.median(time_steps(lambda: layer(x), 10, 3, stream, flush))
+        qbytes = M * K * 2 + M * K + M * 4
+        res[f"w8a8_{mode}_cfg2"] = {
+            "gemm_ms": tg, "gemm_tflops": gemm_flops / tg / 1e9, "frac_dense_peak": gemm_flops / tg / 1e9 / fp8_peak,
+            "act_quant_ms": tq, "act_quant_gbs": qbytes / tq / 1e6, "act_quant_frac_hbm": qbytes / tq / 1e6 / peaks["hbm_gbs"],
+            "quant_linear_ms": tl}
+        if mode == "fp8":
+            ts = statistics.median(time_steps(lambda: torch._scaled_mm(
+                qa, layer.weight.t(), scale_a=sa, scale_b=layer.weight_scale[None, :], out_dtype=torch.bfloat16),
+                10, 3, stream, flush))
+            res["w8a8_fp8_cfg2"]["torch_scaled_mm_ms"] = ts
+        else:
+            ti = statistics.median(time_steps(lambda: torch._int_mm(qa, layer.weight.t()), 10, 3, stream, flush))
+            res["w8a8_int8_cfg2"]["torch_int_mm_ms"] = ti
+        del layer, qa, sa
+    res["fp8_int8_peak_tflops"] = fp8_peak
+    del x, w
+    # readout: 255 blocks x 5120 x 255 options
+    hidden = torch.randn(255, 5120, generator=g).to(torch.bfloat16).to(dev)
+    ro = (torch.randn(255, 5120, generator=g) * 0.02).to(dev)
+    counts = torch.full((255,), 255, dtype=torch.int32, device=dev)
+    t = statistics.median(time_steps(lambda: d3b.probabilities_tensor(hidden, ro, counts, temperature=1.0), 10, 3,
+                                     stream, flush))
+    res["readout_255x5120x255"] = {"ms": t}
+    return res
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,96 @@
+"""Multi-GPU question-block sharding (one process per GPU, torch.distributed).
+
+The state-once design has one exchange step: rank 0 runs the state pass and
+broadcasts each full-attention layer's state K/V (and, end to end, the GDN
+state) to every rank; the question blocks of the request are then split into
+contiguous, length-sorted shards (the order of d3trt/backends/trtllm.py:149),
+each rank runs its shard with no further communication, and the per-block
+readout probabilities are gathered back. Independent requests are spread
+data-parallel with no communication at all.
+
+Collectives go through torch.distributed (NCCL over NVLink/NVSwitch on GPUs,
+gloo on CPU for the tests). Every rank takes the same collective steps in the
+same order. Received K/V lands in each rank's own HBM before any kernel reads
+it; no kernel reads a peer's memory.
+"""
+
+from __future__ import annotations
+
+from typing import Callable, Sequence
+
+import torch
+import torch.distributed as dist
+
+
+def shard_bounds(n_blocks: int, world_size: int, rank: int) -> tuple[int, int]:
+    """Contiguous split of n_blocks into world_size shards of ceil/floor sizes.
+
+    The first ``n_blocks % world_size`` ranks take one extra block, so shard
+    sizes differ by at most one and every block is owned exactly once.
+    """
+    if world_size <= 0 or not 0 <= rank < world_size:
+        raise ValueError(f"rank {rank} outside world of {world_size}")
+    base, extra = divmod(n_blocks, world_size)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def length_order(lengths: Sequence[int]) -> list[int]:
+    """Block indices sorted by length, longest first (stable): shards get similar work."""
+    return sorted(range(len(lengths)), key=lambda i: (-int(lengths[i]), i))
+
+
+def broadcast_state_kv(entries: Sequence[tuple[torch.Tensor, torch.Tensor]], *, src: int = 0, group=None) -> None:
+    """Broadcast every (keys, values) pair in place from ``src`` to all ranks.
+
+    Non-source ranks pass preallocated tensors of the same shape/dtype; each
+    tensor must be contiguous (NCCL moves flat buffers).
+    """
+    for k, v in entries:
+        for t in (k, v):
+            if not t.is_contiguous():
+                raise ValueError("broadcast buffers must be contiguous")
+            dist.broadcast(t, src=src, group=group)
+
+
+def gather_rows(local: torch.Tensor, n_total: int, world_size: int, *, group=None) -> torch.Tensor:
+    """All-gather per-rank row blocks (split by :func:`shard_bounds`) into [n_total, ...].
+
+    Rows are padded to the largest shard for the collective and trimmed after.
+    """
+    biggest = -(-n_total // world_size)
+    pad = torch.zeros((biggest, *local.shape[1:]), dtype=local.dtype, device=local.device)
+    pad[: local.shape[0]] = local
+    parts = [torch.empty_like(pad) for _ in range(world_size)]
+    dist.all_gather(parts, pad, group=group)
+    out = []
+    for r in range(world_size):
+        a, b = shard_bounds(n_total, world_size, r)
+        out.append(parts[r][: b - a])
+    return torch.cat(out, 0)
+
+
+def sharded_question_pass(
+    lengths: Sequence[int],
+    run_blocks: Callable[[list[int]], torch.Tensor],
+    *,
+    rank: int,
+    world_size: int,
+    group=None,
+) -> torch.Tensor:
+    """Run this rank's shard of the (length-sorted) question blocks and gather.
+
+    ``run_blocks(block_ids)`` returns one row per block in the given order
+    (e.g. the readout probabilities). The result has one row per block in the
+    original block order, identical on every rank.
+    """
+    order = length_order(lengths)
+    a, b = shard_bounds(len(order), world_size, rank)
+    mine = order[a:b]
+    local = run_blocks(mine)
+    if local.shape[0] != len(mine):
+        raise RuntimeError(f"run_blocks returned {local.shape[0]} rows for {len(mine)} blocks")
+    gathered = gather_rows(local, len(order), world_size, group=group) if world_size > 1 else local
+    result = torch.empty_like(gathered)
+    result[torch.tensor(order, device=gathered.device)] = gathered
+    return result

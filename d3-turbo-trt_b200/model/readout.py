@@ -1,0 +1,105 @@
+"""255-way fp32 readout softmax on sm_100a (drop-in for the ``probabilities`` method of
+d3trt/model/trtllm_stack.py:451-468, identical to hf_stack.py:67-84).
+
+    logits = hidden.float() @ readout.T
+    logits[b, j >= counts[b]] = -inf
+    probs  = softmax(logits / temperature)
+    return [row[:count] for row, count in zip(probs.tolist(), counts)]
+
+One kernel launch computes the fp32 dot products, the mask, the temperature
+and the softmax (libd3b200 ``d3b_readout``); the only host work left is the
+device-to-host copy of the result, as in the reference (``.cpu().tolist()``).
+"""
+
+from __future__ import annotations
+
+from typing import Sequence
+
+import torch
+
+from .. import _lib
+
+KERNEL_NAME = "sm100a"
+_WORKSPACES: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    """A zero-filled scratch buffer per (device, stream); calls on one stream never overlap."""
+    key = (device.index or 0, stream)
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = ws
+    return ws
+
+
+def probabilities_tensor(
+    hidden: torch.Tensor,
+    readout: torch.Tensor,
+    counts: Sequence[int] | torch.Tensor,
+    *,
+    temperature: float,
+) -> torch.Tensor:
+    """[B, K] hidden, [n_opt, K] fp32 readout -> [B, n_opt] fp32 probabilities on the device."""
+    _lib.require_cuda(hidden, "probabilities")
+    if hidden.dim() != 2 or readout.dim() != 2 or hidden.shape[1] != readout.shape[1]:
+        raise ValueError(f"hidden {tuple(hidden.shape)} and readout {tuple(readout.shape)} do not match")
+    if hidden.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+        hidden = hidden.float()
+    hidden = hidden.contiguous()
+    readout = readout.to(device=hidden.device, dtype=torch.float32).contiguous()
+    rows, k = hidden.shape
+    n_opt = readout.shape[0]
+    if isinstance(counts, torch.Tensor):
+        counts_t = counts.to(device=hidden.device, dtype=torch.int32).contiguous()
+    else:
+        counts_t = torch.tensor([int(c) for c in counts], dtype=torch.int32).to(hidden.device)
+    if counts_t.numel() != rows:
+        raise ValueError(f"{counts_t.numel()} counts for {rows} rows")
+    probs = torch.empty((rows, n_opt), dtype=torch.float32, device=hidden.device)
+    if rows == 0:
+        return probs
+    lib = _lib.lib()
+    stream = _lib.stream_of(hidden)
+    nbytes = int(lib.d3b_readout_workspace_size(rows, n_opt))
+    ws = _workspace(hidden.device, int(stream.value or 0), nbytes)
+    status = lib.d3b_readout(
+        _lib.ptr(hidden), _lib.dtype_code(hidden.dtype), _lib.ptr(readout), _lib.ptr(counts_t), float(temperature),
+        _lib.ptr(probs), rows, k, n_opt, _lib.ptr(ws), ws.numel(), stream,
+    )
+    _lib.check(status, "d3b_readout")
+    return probs
+
+
+def probabilities(
+    hidden: torch.Tensor,
+    readout: torch.Tensor,
+    counts: Sequence[int],
+    *,
+    temperature: float,
+    readout_dtype: str = "float32",
+) -> list[list[float]]:
+    """Per-answer probabilities, rows cut to ``count`` (trtllm_stack.py:451-468)."""
+    if readout_dtype != "float32":
+        raise ValueError("the sm_100a readout computes in float32 only (readout_dtype='float32')")
+    counts = [int(c) for c in counts]
+    values = probabilities_tensor(hidden, readout, counts, temperature=temperature).cpu().tolist()
+    return [row[:count] for row, count in zip(values, counts)]
+
+
+class ReadoutHead:
+    """The ``probabilities`` method of the reference stacks, bound to a readout matrix."""
+
+    def __init__(self, readout: torch.Tensor):
+        self.readout = readout.float().contiguous()
+        self.max_options = int(readout.shape[0])
+
+    def probabilities(
+        self,
+        hidden: torch.Tensor,
+        counts: Sequence[int],
+        *,
+        temperature: float,
+        readout_dtype: str = "float32",
+    ) -> list[list[float]]:
+        return probabilities(hidden, self.readout, counts, temperature=temperature, readout_dtype=readout_dtype)

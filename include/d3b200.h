@@ -1,0 +1,142 @@
+/*
+ * libd3b200 — C ABI of the B200 (sm_100a) kernels for d3's prefill hot path.
+ *
+ * Every entry point takes raw device pointers, element strides and sizes, and
+ * a CUDA stream (passed as an opaque pointer; 0 = legacy default stream). All
+ * work is enqueued on that stream; nothing synchronises the device. The caller
+ * owns every buffer. Each function returns D3B_OK (0) or a negative status;
+ * d3b_error_string() turns a status into text. Argument problems (shape,
+ * stride, alignment, unsupported dtype) are reported before any launch and
+ * never reach the GPU. A device-side wait that runs past its wall-clock limit
+ * records a site code that d3b_device_error() returns after the stream is
+ * synchronised.
+ *
+ * Dtype codes (x_dtype, dtype, h_dtype, out_kind):
+ *   D3B_F32 = 0, D3B_F16 = 1, D3B_BF16 = 2, D3B_I32 = 3
+ * Quantisation modes (mode):
+ *   D3B_MODE_FP8 = 0  (e4m3fn, max 448)
+ *   D3B_MODE_INT8 = 1 (symmetric int8, max 127)
+ */
+#ifndef D3B200_H_
+#define D3B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define D3B_API __attribute__((visibility("default")))
+#else
+#define D3B_API
+#endif
+
+typedef void* d3b_stream_t;
+
+enum {
+  D3B_OK = 0,
+  D3B_EINVAL = -1,       /* bad shape, size or argument */
+  D3B_EALIGN = -2,       /* pointer or stride not aligned as the kernel needs */
+  D3B_EUNSUPPORTED = -3, /* dtype / head_dim / group size the kernels do not cover */
+  D3B_ECUDA = -4,        /* a CUDA runtime or driver call failed */
+  D3B_ETIMEOUT = -5,     /* a device-side wait ran past its limit */
+  D3B_ENOSPACE = -6      /* workspace or fixed scratch too small for the request */
+};
+
+enum { D3B_F32 = 0, D3B_F16 = 1, D3B_BF16 = 2, D3B_I32 = 3 };
+enum { D3B_MODE_FP8 = 0, D3B_MODE_INT8 = 1 };
+
+/* Library version (major*10000 + minor*100 + patch). */
+D3B_API int d3b_version(void);
+
+/* Static text for a status code. */
+D3B_API const char* d3b_error_string(int status);
+
+/* Returns the device error word of the current device (0 = none) after
+ * synchronising `stream`; clears it when `reset` is non-zero. A non-zero
+ * value is the site code of the wait that gave up. */
+D3B_API int d3b_device_error(d3b_stream_t stream, int reset);
+
+/*
+ * Per-token (per-row) dynamic activation quantisation.
+ * Replaces d3trt/model/quant.py:92-100 (quantize_rows) and, applied to a
+ * weight matrix, quant.py:77-89 (quantize_weight).
+ *   x     [M, K] rows of `ldx` elements, dtype x_dtype (f32, f16 or bf16)
+ *   q     [M, K] contiguous, e4m3fn bytes (mode FP8) or int8 (mode INT8)
+ *   scale [M] float32: max(max|x_row|, 1e-12) / 448 (or / 127)
+ * q = e4m3_rn_satfinite(clamp(x / scale, ±448)) or int8(clamp(rint(x / scale), ±127)),
+ * IEEE division, bit-identical to the reference on the same input.
+ */
+D3B_API int d3b_act_quant(const void* x, int x_dtype, int64_t ldx, void* q, float* scale, int64_t M, int64_t K,
+                  int mode, d3b_stream_t stream);
+
+/*
+ * W8A8 scaled GEMM: y[m, n] = (sum_k qa[m,k] * qw[n,k]) * sa[m] * sw[n].
+ * Replaces the torch._scaled_mm rowwise call in quant.py:164-179 (mode FP8)
+ * and torch._int_mm plus its dequant chain in quant.py:190-197 (mode INT8).
+ *   qa [M, K] row-major 8-bit, qw [N, K] row-major 8-bit (K-major both)
+ *   sa [M] f32, sw [N] f32
+ *   y  [M, N] with row stride ldy elements; out_kind D3B_BF16 / D3B_F16 /
+ *      D3B_F32 (dequantised) or D3B_I32 (raw int32 accumulator, INT8 only,
+ *      scales ignored and may be NULL)
+ * Requires K % 16 == 0, N % 16 == 0, 16-byte aligned qa/qw/y.
+ */
+D3B_API int d3b_w8a8_gemm(const void* qa, const void* qw, const float* sa, const float* sw, void* y, int64_t ldy,
+                  int64_t M, int64_t N, int64_t K, int mode, int out_kind, d3b_stream_t stream);
+
+/*
+ * Prefix-bidirectional GQA attention (question pass), one launch.
+ * Replaces d3trt/kernels/prefix_bidir.py:187-260 (prefix_bidir_attention and
+ * the Triton _prefix_bidir_fwd kernel at :47-131, without the pack/unpack
+ * gathers). For block b, head h, token i < lengths[b]:
+ *   out[b,h,i] = softmax_j(scale * q[b,h,i] . key_j) . value_j over
+ *   j in {state keys 0..S-1 of kv head h/(H/Hkv)} U {own keys 0..lengths[b]-1}
+ * Tokens i >= lengths[b] get zero rows. S == 0 gives plain bidirectional
+ * attention within each block (the state pass, ops.py:107-124 / :174-193).
+ *   q        [B, H, L, D]   strides q_strides   = {b, h, l} in elements, d contiguous
+ *   k_state  [Hkv, S, D]    strides kv_strides  = {h, s}
+ *   v_state  [Hkv, S, D]    same strides as k_state
+ *   k_q, v_q [B, Hkv, L, D] strides kq_strides  = {b, h, l}
+ *   lengths  [B] int32 on the device (the block-offset table)
+ *   out      [B, H, L, D]   strides out_strides = {b, h, l}
+ * dtype: D3B_F16 or D3B_BF16 for all of q/k/v/out. D in {32, 64, 128, 256};
+ * H % Hkv == 0 and H/Hkv <= 128. Strides must be multiples of 8 elements.
+ */
+D3B_API int d3b_prefix_bidir(const void* q, const int64_t* q_strides, const void* k_state, const void* v_state,
+                     const int64_t* kv_strides, const void* k_q, const void* v_q, const int64_t* kq_strides,
+                     const int32_t* lengths, int B, int H, int Hkv, int S, int L, int D, int dtype, float scale,
+                     void* out, const int64_t* out_strides, d3b_stream_t stream);
+
+/*
+ * 255-way (any n_opt <= 1024) fp32 readout softmax at the selected positions.
+ * Replaces the probabilities body of d3trt/model/trtllm_stack.py:451-468
+ * (= hf_stack.py:67-84): logits = f32(hidden) @ readout^T; logits[b, j] = -inf
+ * for j >= counts[b]; probs = softmax(logits / temperature).
+ *   hidden  [B, K] contiguous, dtype h_dtype (f32, f16, bf16)
+ *   readout [n_opt, K] f32 contiguous
+ *   counts  [B] int32 device
+ *   probs   [B, n_opt] f32 contiguous
+ *   workspace: device scratch of d3b_readout_workspace_size(B, n_opt) bytes,
+ *   zero-filled before its first use; the kernel leaves it ready for the next
+ *   call. Calls that share a workspace must not overlap on the GPU.
+ */
+D3B_API size_t d3b_readout_workspace_size(int B, int n_opt);
+D3B_API int d3b_readout(const void* hidden, int h_dtype, const float* readout, const int32_t* counts, float temperature,
+                float* probs, int B, int K, int n_opt, void* workspace, size_t workspace_bytes,
+                d3b_stream_t stream);
+
+/*
+ * Self-test of the device wait limit: launches one CTA that waits on an
+ * mbarrier nothing arrives on, with a limit of `limit_ms` milliseconds; the
+ * kernel gives up, records its site code and returns. After synchronising,
+ * d3b_device_error() returns that code. Used by the failure-detection test.
+ */
+D3B_API int d3b_selftest_wait_timeout(int limit_ms, d3b_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* D3B200_H_ */

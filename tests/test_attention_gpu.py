@@ -1,0 +1,139 @@
+"""GPU parity of the prefix-bidirectional attention against the oracle
+(ops.sdpa_questions / sdpa_state restated) and the golden vectors recorded from
+the reference: within 2e-2 max-abs (the BASELINE tolerance), and in practice
+near bf16 output rounding."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import bf16_from_bits, load_golden
+from oracle import attention as oattn
+
+from d3_turbo_trt_b200 import _lib
+from d3_turbo_trt_b200.kernels import prefix_bidir as pb
+from d3_turbo_trt_b200.model import ops
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+TOL = 2e-2
+
+
+def _rand(shape, g, dtype=torch.bfloat16):
+    return torch.randn(*shape, generator=g).to(dtype)
+
+
+def test_cfg1_golden_strided_views():
+    """BASELINE config 1 ([768, 8, 64] over a 512-token state + 8 x 32), read
+    through strided views of the token-major sequence: no copies."""
+    g = load_golden("attn_cfg1.npz")
+    state, nb, lq, heads, kv_heads, dim = (int(v) for v in g["meta"])
+    scale = float(g["scale"])
+    Q = bf16_from_bits(g["Q"]).to(DEV)
+    K = bf16_from_bits(g["K"]).to(DEV)
+    V = bf16_from_bits(g["V"]).to(DEV)
+    ks, vs = K[:state].transpose(0, 1), V[:state].transpose(0, 1)  # [Hkv, S, D], token-major
+    qq = Q[state:].view(nb, lq, heads, dim).permute(0, 2, 1, 3)
+    kq = K[state:].view(nb, lq, kv_heads, dim).permute(0, 2, 1, 3)
+    vq = V[state:].view(nb, lq, kv_heads, dim).permute(0, 2, 1, 3)
+    out_q, kernel = ops.question_attention(qq, ks, vs, kq, vq, [lq] * nb, scale=scale, return_kernel=True)
+    assert kernel == "sm100a"
+    out_s = ops.flash_state(Q[:state].transpose(0, 1)[None], ks[None], vs[None], scale=scale)
+    out = torch.cat([out_s[0].transpose(0, 1), out_q.permute(0, 2, 1, 3).reshape(nb * lq, heads, dim)], 0)
+    err = np.abs(out.float().cpu().numpy() - g["out"]).max()
+    assert err <= TOL, err
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("case", ["d32_g2", "d64_g3", "d256_g1", "d128_g8"])
+def test_ragged_golden(case):
+    g = load_golden("attn_ragged.npz")
+    t = {k: bf16_from_bits(g[f"{case}_{k}"]).to(DEV) for k in ("q", "ks", "vs", "kq", "vq")}
+    lens = g[f"{case}_lens"].tolist()
+    out = pb.prefix_bidir_attention(t["q"], t["ks"], t["vs"], t["kq"], t["vq"], lens, scale=float(g[f"{case}_scale"]))
+    got = out.float().cpu().numpy()
+    ref = g[f"{case}_out"]
+    assert np.abs(got - ref).max() <= TOL
+    for b, n in enumerate(lens):
+        assert np.all(got[b, :, n:] == 0)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_cfg3a_shape_against_oracle(dtype):
+    """BASELINE config 3a shapes: 4096-token state + 16 blocks x 64, H32/Hkv4/D128;
+    the oracle checks three blocks (one ragged)."""
+    g = torch.Generator().manual_seed(11)
+    B, H, Hkv, L, D, S = 16, 32, 4, 64, 128, 4096
+    q = _rand((B, L, H, D), g, dtype).permute(0, 2, 1, 3)  # model layout: [B, L, H, D] memory
+    ks = _rand((S, Hkv, D), g, dtype).permute(1, 0, 2)      # token-major state
+    vs = _rand((S, Hkv, D), g, dtype).permute(1, 0, 2)
+    kq = _rand((B, L, Hkv, D), g, dtype).permute(0, 2, 1, 3)
+    vq = _rand((B, L, Hkv, D), g, dtype).permute(0, 2, 1, 3)
+    lens = [64] * B
+    lens[5] = 37
+    lens[9] = 1
+    out = pb.prefix_bidir_attention(q.to(DEV), ks.to(DEV), vs.to(DEV), kq.to(DEV), vq.to(DEV), lens, scale=D**-0.5)
+    got = out.float().cpu()
+    for b in (0, 5, 9):
+        ref = oattn.questions(q[b : b + 1], ks, vs, kq[b : b + 1], vq[b : b + 1], [lens[b]], D**-0.5,
+                              dtype=torch.float32)
+        assert float((got[b : b + 1] - ref).abs().max()) <= TOL
+    assert torch.all(got[5, :, 37:] == 0) and torch.all(got[9, :, 1:] == 0)
+
+
+def test_head_major_state_and_empty_blocks():
+    g = torch.Generator().manual_seed(12)
+    B, H, Hkv, L, D, S = 4, 16, 2, 48, 128, 300
+    q = _rand((B, H, L, D), g)
+    ks, vs = _rand((Hkv, S, D), g), _rand((Hkv, S, D), g)  # head-major contiguous
+    kq, vq = _rand((B, Hkv, L, D), g), _rand((B, Hkv, L, D), g)
+    lens = [48, 0, 17, 48]
+    out = pb.prefix_bidir_attention(q.to(DEV), ks.to(DEV), vs.to(DEV), kq.to(DEV), vq.to(DEV), lens, scale=0.09)
+    ref = oattn.questions(q, ks, vs, kq, vq, lens, 0.09, dtype=torch.float32)
+    assert float((out.float().cpu() - ref).abs().max()) <= TOL
+    assert torch.all(out[1] == 0)
+    z = pb.prefix_bidir_attention(q.to(DEV), ks.to(DEV), vs.to(DEV), kq.to(DEV), vq.to(DEV), [0] * B, scale=0.09)
+    assert torch.all(z == 0)
+
+
+@pytest.mark.parametrize("tokens,heads,kv_heads,dim", [(1000, 16, 2, 128), (257, 8, 8, 64), (130, 4, 1, 256)])
+def test_state_pass_against_oracle(tokens, heads, kv_heads, dim):
+    g = torch.Generator().manual_seed(13)
+    q = _rand((1, heads, tokens, dim), g)
+    k = _rand((1, kv_heads, tokens, dim), g)
+    v = _rand((1, kv_heads, tokens, dim), g)
+    out = ops.flash_state(q.to(DEV), k.to(DEV), v.to(DEV), scale=dim**-0.5)
+    ref = oattn.state(q, k, v, dim**-0.5, dtype=torch.float32)
+    assert float((out.float().cpu() - ref).abs().max()) <= TOL
+
+
+def test_large_logits_stay_finite():
+    """Scores far from zero exercise the lazy rescale (max jumps by > 2^8)."""
+    g = torch.Generator().manual_seed(14)
+    B, H, Hkv, L, D, S = 2, 8, 1, 32, 64, 512
+    q = _rand((B, H, L, D), g) * 4
+    ks = _rand((Hkv, S, D), g) * 4
+    ks[:, 300:] *= 3  # later keys dominate: the running max grows mid-stream
+    vs = _rand((Hkv, S, D), g)
+    kq, vq = _rand((B, Hkv, L, D), g) * 4, _rand((B, Hkv, L, D), g)
+    out = pb.prefix_bidir_attention(q.to(DEV), ks.to(DEV), vs.to(DEV), kq.to(DEV), vq.to(DEV), [32, 20], scale=0.5)
+    ref = oattn.questions(q, ks, vs, kq, vq, [32, 20], 0.5, dtype=torch.float64)
+    got = out.float().cpu()
+    assert torch.isfinite(got).all()
+    assert float((got - ref).abs().max()) <= TOL
+
+
+def test_preallocated_strided_output_and_tensor_lengths():
+    g = torch.Generator().manual_seed(15)
+    B, H, Hkv, L, D, S = 3, 8, 2, 16, 64, 128
+    q = _rand((B, H, L, D), g).to(DEV)
+    ks, vs = _rand((Hkv, S, D), g).to(DEV), _rand((Hkv, S, D), g).to(DEV)
+    kq, vq = _rand((B, Hkv, L, D), g).to(DEV), _rand((B, Hkv, L, D), g).to(DEV)
+    lens = torch.tensor([16, 3, 9], dtype=torch.int32, device=DEV)
+    buf = torch.full((B, L, H, D), 7.0, dtype=torch.bfloat16, device=DEV)
+    out = buf.permute(0, 2, 1, 3)
+    pb.prefix_bidir_attention(q, ks, vs, kq, vq, lens, scale=0.125, out=out)
+    ref = oattn.questions(q.cpu(), ks.cpu(), vs.cpu(), kq.cpu(), vq.cpu(), [16, 3, 9], 0.125, dtype=torch.float32)
+    assert float((out.float().cpu() - ref).abs().max()) <= TOL

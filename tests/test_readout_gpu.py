@@ -1,0 +1,53 @@
+"""GPU parity of the 255-way readout against the golden vectors recorded from
+TrtllmStack.probabilities (trtllm_stack.py:451-468) and the oracle."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import bf16_from_bits, load_golden
+from oracle import readout as oread
+
+import d3_turbo_trt_b200 as d3b
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.mark.parametrize("tag", ["t1", "t07"])
+def test_readout_golden(tag):
+    g = load_golden("readout.npz")
+    hidden = bf16_from_bits(g["hidden_bf16"]).to(DEV)
+    readout = torch.from_numpy(g["readout"]).to(DEV)
+    counts = g["counts"].tolist()
+    temp = float(g[f"temp_{tag}"])
+    lists = d3b.probabilities(hidden, readout, counts, temperature=temp)
+    assert [len(r) for r in lists] == counts
+    for row, ref in zip(lists, g[f"probs_{tag}"]):
+        assert np.abs(np.array(row) - ref[: len(row)]).max() <= 1e-5
+
+
+def test_readout_cfg4_shape_twice():
+    """255 blocks x hidden 5120 x 255 options; two calls in a row reuse the workspace."""
+    g = torch.Generator().manual_seed(21)
+    hidden = torch.randn(255, 5120, generator=g).to(torch.bfloat16)
+    readout = torch.randn(255, 5120, generator=g) * 0.02
+    counts = [1 + (i * 37) % 255 for i in range(255)]
+    ref = oread.probabilities(hidden.float().numpy(), readout.numpy(), counts, 1.0)
+    for _ in range(2):
+        probs = d3b.probabilities_tensor(hidden.to(DEV), readout.to(DEV), counts, temperature=1.0).cpu().numpy()
+        assert np.abs(probs - ref).max() <= 1e-5
+        assert np.argmax(probs, 1).tolist() == np.argmax(ref, 1).tolist()
+
+
+def test_readout_odd_sizes():
+    g = torch.Generator().manual_seed(22)
+    for rows, k, n_opt in ((1, 100, 3), (9, 777, 40), (33, 512, 1000)):
+        hidden = torch.randn(rows, k, generator=g)
+        readout = torch.randn(n_opt, k, generator=g) * 0.05
+        counts = [(i % n_opt) + 1 for i in range(rows)]
+        ref = oread.probabilities(hidden.numpy(), readout.numpy(), counts, 0.5)
+        got = d3b.probabilities_tensor(hidden.to(DEV), readout.to(DEV), counts, temperature=0.5).cpu().numpy()
+        assert np.abs(got - ref).max() <= 1e-5
