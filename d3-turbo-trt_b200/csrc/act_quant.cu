@@ -1,17 +1,24 @@
 // Per-token activation quantisation (d3trt/model/quant.py:92-100) and, on a
 // weight matrix, per-output-channel weight quantisation (quant.py:77-89).
 //
-// One warp owns one row. Pass 1 reads the row with 16-byte loads and reduces
-// max|x| with warp shuffles; pass 2 re-reads the row (an L1/L2 hit: the row was
-// just streamed) and writes the 8-bit codes. HBM traffic is the algorithmic
-// minimum: read x once (2 B/elem for bf16), write q (1 B/elem) and the scale.
+// One warp owns one row. Rows up to 32 lanes x 8 x kMaxVec elements are read
+// once into registers with 16-byte loads (all in flight together), reduced to
+// max|x| with warp shuffles and quantised from registers: HBM traffic is the
+// algorithmic minimum (read x once, write q and the scale). Longer rows use a
+// two-pass variant whose second read hits L2.
 //
 // Bit-exactness with the reference formulas:
 //   amax  = max(max_k |x|, 1e-12f)                (fp32, order independent)
 //   scale = amax / 448 (fp8) or amax / 127 (int8)   (IEEE fp32 division)
 //   fp8 : q = e4m3fn(clamp(x / scale, -448, 448))   cvt.rn.satfinite = RNE
 //   int8: q = int8(clamp(rint(x / scale), -127, 127))  rint = half-to-even
-// x / scale uses __fdiv_rn (IEEE), never a reciprocal multiply.
+// x / scale must be the IEEE quotient RN(x / scale). Per element the kernel
+// first forms v = RN(x * RN(1 / scale)), which is within 1.5 ulp of x / scale.
+// The code only depends on which side of a rounding boundary of the target
+// format (an e4m3 midpoint, or k + 1/2 for int8) the quotient lies; when v is
+// 4 ulp or more away from every boundary, v and RN(x / scale) give the same
+// code. Otherwise the element is recomputed with __fdiv_rn (IEEE). So the
+// codes equal those of the reference's IEEE division in every case.
 #include "common.cuh"
 
 namespace {
@@ -23,16 +30,17 @@ struct Vec;  // 16-byte vector of T converted to fp32
 template <>
 struct Vec<float> {
   static constexpr int N = 4;
-  __device__ static void load(const float* p, float (&v)[8]) {
-    float4 a = __ldg(reinterpret_cast<const float4*>(p));
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  __device__ static void unpack(uint4 a, float (&v)[8]) {
+    v[0] = __uint_as_float(a.x); v[1] = __uint_as_float(a.y); v[2] = __uint_as_float(a.z);
+    v[3] = __uint_as_float(a.w);
   }
+  __device__ static void load(const float* p, float (&v)[8]) { unpack(__ldg(reinterpret_cast<const uint4*>(p)), v); }
 };
 template <>
 struct Vec<__nv_bfloat16> {
   static constexpr int N = 8;
-  __device__ static void load(const __nv_bfloat16* p, float (&v)[8]) {
-    uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+  __device__ static void load(const __nv_bfloat16* p, float (&v)[8]) { unpack(__ldg(reinterpret_cast<const uint4*>(p)), v); }
+  __device__ static void unpack(uint4 a, float (&v)[8]) {
     const uint32_t w[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -44,8 +52,8 @@ struct Vec<__nv_bfloat16> {
 template <>
 struct Vec<__half> {
   static constexpr int N = 8;
-  __device__ static void load(const __half* p, float (&v)[8]) {
-    uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+  __device__ static void load(const __half* p, float (&v)[8]) { unpack(__ldg(reinterpret_cast<const uint4*>(p)), v); }
+  __device__ static void unpack(uint4 a, float (&v)[8]) {
     const uint32_t w[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -68,15 +76,103 @@ __device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
   return r;
 }
 
+// True when v may lie within 4 fp32 ulp of a rounding boundary of the target
+// format (then RN(x/s) must be computed exactly). |v| <= 448 (fp8) or 127.
 template <int MODE>
-__device__ __forceinline__ uint32_t quant1(float x, float scale) {
+__device__ __forceinline__ bool near_boundary(float v) {
+  const float a = fabsf(v);
   if (MODE == D3B_MODE_FP8) {
-    float v = fminf(fmaxf(__fdiv_rn(x, scale), -448.f), 448.f);
-    return e4m3x2(v, 0.f) & 0xFFu;
+    if (a >= 0.015625f) {  // e4m3 normal range: 3 mantissa bits, tie at dropped bits == 0x80000
+      const int dropped = static_cast<int>(__float_as_uint(a) & 0xFFFFFu);
+      return abs(dropped - 0x80000) <= 4;
+    }
+    const float t = a * 512.f;  // subnormal quantum 2^-9 (exact scaling)
+    return fabsf(t - floorf(t) - 0.5f) <= 1.0f / 32768.f;
+  }
+  return fabsf(a - floorf(a) - 0.5f) <= 1.0f / 32768.f;  // 4 ulp at |v| < 128
+}
+
+template <int MODE>
+__device__ __forceinline__ float quotient(float x, float scale, float rcp) {
+  float v = __fmul_rn(x, rcp);
+  const float lim = MODE == D3B_MODE_FP8 ? 448.f : 127.f;
+  if (near_boundary<MODE>(fminf(fmaxf(v, -lim), lim))) v = __fdiv_rn(x, scale);
+  return v;
+}
+
+// Two elements -> two codes in the low 16 bits (element 0 in bits 0..7).
+template <int MODE>
+__device__ __forceinline__ uint32_t quant2(float x0, float x1, float scale, float rcp) {
+  const float v0 = quotient<MODE>(x0, scale, rcp), v1 = quotient<MODE>(x1, scale, rcp);
+  if (MODE == D3B_MODE_FP8) {
+    return e4m3x2(fminf(fmaxf(v0, -448.f), 448.f), fminf(fmaxf(v1, -448.f), 448.f));
   } else {
-    int i = __float2int_rn(__fdiv_rn(x, scale));
-    i = min(max(i, -127), 127);
-    return static_cast<uint32_t>(i) & 0xFFu;
+    const int i0 = min(max(__float2int_rn(v0), -127), 127);
+    const int i1 = min(max(__float2int_rn(v1), -127), 127);
+    return (static_cast<uint32_t>(i0) & 0xFFu) | ((static_cast<uint32_t>(i1) & 0xFFu) << 8);
+  }
+}
+
+template <int MODE>
+__device__ __forceinline__ uint32_t quant1(float x, float scale, float rcp) {
+  return quant2<MODE>(x, 0.f, scale, rcp) & 0xFFu;
+}
+
+__device__ __forceinline__ float row_scale(float amax, int mode) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  amax = fmaxf(amax, 1e-12f);
+  return __fdiv_rn(amax, mode == D3B_MODE_FP8 ? 448.f : 127.f);
+}
+
+// Single pass: the row lives in registers (nvec 16-byte vectors per lane).
+constexpr int kMaxVec = 24;
+constexpr int kCachedWarps = 4;
+
+template <typename T, int MODE>
+__global__ void __launch_bounds__(kCachedWarps * 32) act_quant_cached_kernel(const T* __restrict__ x, int64_t ldx,
+                                                                              uint8_t* __restrict__ q,
+                                                                              float* __restrict__ scale_out,
+                                                                              int64_t M, int64_t K) {
+  constexpr int VN = Vec<T>::N;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kCachedWarps + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const T* xr = x + row * ldx;
+  uint8_t* qr = q + row * K;
+  const int nvec = static_cast<int>(K / (VN * 32));  // full vectors per lane (K % (VN*32) == 0 here)
+  uint4 raw[kMaxVec];
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i)
+    if (i < nvec) raw[i] = __ldg(reinterpret_cast<const uint4*>(xr + (int64_t)(i * 32 + lane) * VN));
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    if (i < nvec) {
+      float v[8];
+      Vec<T>::unpack(raw[i], v);
+#pragma unroll
+      for (int e = 0; e < VN; ++e) amax = fmaxf(amax, fabsf(v[e]));
+    }
+  }
+  const float scale = row_scale(amax, MODE);
+  const float rcp = __frcp_rn(scale);
+  if (lane == 0) scale_out[row] = scale;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    if (i < nvec) {
+      float v[8];
+      Vec<T>::unpack(raw[i], v);
+      uint8_t* dst = qr + (int64_t)(i * 32 + lane) * VN;
+      if (VN == 8) {
+        const uint32_t w0 = quant2<MODE>(v[0], v[1], scale, rcp) | (quant2<MODE>(v[2], v[3], scale, rcp) << 16);
+        const uint32_t w1 = quant2<MODE>(v[4], v[5], scale, rcp) | (quant2<MODE>(v[6], v[7], scale, rcp) << 16);
+        *reinterpret_cast<uint2*>(dst) = make_uint2(w0, w1);
+      } else {
+        *reinterpret_cast<uint32_t*>(dst) =
+            quant2<MODE>(v[0], v[1], scale, rcp) | (quant2<MODE>(v[2], v[3], scale, rcp) << 16);
+      }
+    }
   }
 }
 
@@ -106,10 +202,8 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) act_quant_kernel(const T* _
     }
   }
   for (int64_t k = k_vec_end + lane; k < K; k += 32) amax = fmaxf(amax, fabsf(to_f32(xr[k])));
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  amax = fmaxf(amax, 1e-12f);
-  const float scale = __fdiv_rn(amax, MODE == D3B_MODE_FP8 ? 448.f : 127.f);
+  const float scale = row_scale(amax, MODE);
+  const float rcp = __frcp_rn(scale);
   if (lane == 0) scale_out[row] = scale;
 
   // ---- pass 2: codes ----
@@ -119,21 +213,17 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) act_quant_kernel(const T* _
       float v[8];
       Vec<T>::load(xr + k, v);
       if (VN == 8) {
-        uint32_t w0 = 0, w1 = 0;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) w0 |= quant1<MODE>(v[i], scale) << (8 * i);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) w1 |= quant1<MODE>(v[4 + i], scale) << (8 * i);
+        const uint32_t w0 = quant2<MODE>(v[0], v[1], scale, rcp) | (quant2<MODE>(v[2], v[3], scale, rcp) << 16);
+        const uint32_t w1 = quant2<MODE>(v[4], v[5], scale, rcp) | (quant2<MODE>(v[6], v[7], scale, rcp) << 16);
         *reinterpret_cast<uint2*>(qr + k) = make_uint2(w0, w1);
       } else {
-        uint32_t w0 = 0;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) w0 |= quant1<MODE>(v[i], scale) << (8 * i);
+        const uint32_t w0 = quant2<MODE>(v[0], v[1], scale, rcp) | (quant2<MODE>(v[2], v[3], scale, rcp) << 16);
         *reinterpret_cast<uint32_t*>(qr + k) = w0;
       }
     }
   }
-  for (int64_t k = k_vec_end + lane; k < K; k += 32) qr[k] = static_cast<uint8_t>(quant1<MODE>(to_f32(xr[k]), scale));
+  for (int64_t k = k_vec_end + lane; k < K; k += 32)
+    qr[k] = static_cast<uint8_t>(quant1<MODE>(to_f32(xr[k]), scale, rcp));
 }
 
 template <typename T>
@@ -144,6 +234,18 @@ int launch_typed(const void* x, int64_t ldx, void* q, float* scale, int64_t M, i
   // need K to keep every row start aligned.
   const int vec_ok = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((ldx * elem) % 16 == 0) &&
                      (reinterpret_cast<uintptr_t>(q) % 16 == 0) && (K % 8 == 0);
+  constexpr int VN = Vec<T>::N;
+  if (vec_ok && K % (VN * 32) == 0 && K / (VN * 32) <= kMaxVec) {
+    const int64_t blocks = (M + kCachedWarps - 1) / kCachedWarps;
+    if (blocks > 0x7FFFFFFF) return D3B_EINVAL;
+    if (mode == D3B_MODE_FP8)
+      act_quant_cached_kernel<T, D3B_MODE_FP8><<<(unsigned)blocks, kCachedWarps * 32, 0, stream>>>(
+          static_cast<const T*>(x), ldx, static_cast<uint8_t*>(q), scale, M, K);
+    else
+      act_quant_cached_kernel<T, D3B_MODE_INT8><<<(unsigned)blocks, kCachedWarps * 32, 0, stream>>>(
+          static_cast<const T*>(x), ldx, static_cast<uint8_t*>(q), scale, M, K);
+    return d3b_host::check_launch();
+  }
   const int64_t blocks = (M + kWarpsPerCta - 1) / kWarpsPerCta;
   if (blocks > 0x7FFFFFFF) return D3B_EINVAL;
   dim3 grid((unsigned)blocks), block(kWarpsPerCta * 32);

@@ -88,12 +88,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(addr, parity)) return true;
     if (*abort_flag) return false;
+    // Another CTA (of this or an earlier launch) already gave up: the results
+    // are void until the host reads and clears the error word, so stop early
+    // instead of letting every CTA wait out its own limit.
+    if (err && *reinterpret_cast<volatile int*>(err) != 0) {
+      *abort_flag = 1;
+      return false;
+    }
     if (globaltimer_ns() - t0 > D3B_WAIT_LIMIT_NS) {
       *abort_flag = 1;
       record_device_error(err, site);
       return false;
     }
   }
+}
+
+// Warp-collective form: every lane of the (converged) warp waits and the result
+// is the AND over lanes, so code after it that uses .sync.aligned tcgen05
+// instructions is entered by all 32 lanes or by none.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                          int site) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, err, site);
+  return __all_sync(0xffffffffu, ok);
 }
 
 // ---------------------------------------------------------------------------

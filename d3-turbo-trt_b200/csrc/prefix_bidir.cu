@@ -291,7 +291,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int j = 0; j < n; ++j) {
       const int sb = j & 1;
       const uint32_t u = (uint32_t)(j >> 1);
-      if (!d3b::mbar_wait(&bars.s_full[sb], u & 1, abort_flag, p.err, kSiteSFull)) { ok = false; break; }
+      if (!d3b::warp_wait(&bars.s_full[sb], u & 1, abort_flag, p.err, kSiteSFull)) { ok = false; break; }
       d3b::tc_fence_after();
       float s[BN];
 #pragma unroll
@@ -311,8 +311,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
       for (int c = 1; c < BN; ++c) mx = fmaxf(mx, s[c]);
       const float m_tile = mx * sl2;
-      const bool rescale = m_tile > m_ref + kRescaleThreshold;
-      const float m_new = rescale ? m_tile : m_ref;
+      // Lazy rescale, decided per warp: tcgen05.ld/st are warp-collective, so
+      // if any row of the warp needs a new reference max, every row of the
+      // warp moves to its exact running max (alpha = 1 where it is unchanged).
+      const bool rescale = __any_sync(0xffffffffu, m_tile > m_ref + kRescaleThreshold);
+      const float m_new = rescale ? fmaxf(m_ref, m_tile) : m_ref;
       const float alpha = rescale ? d3b::ex2_approx(m_ref - m_new) : 1.f;
       float rowsum = 0.f;
       uint32_t pk[BN / 2];
@@ -324,7 +327,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         pk[c / 2] = pack2<FP16>(p0, p1);
       }
       // P[sb] is free once PV_{j-2} (its previous reader) has completed.
-      if (!d3b::mbar_wait(&bars.p_free[sb], (u & 1) ^ 1, abort_flag, p.err, kSitePFree)) { ok = false; break; }
+      if (!d3b::warp_wait(&bars.p_free[sb], (u & 1) ^ 1, abort_flag, p.err, kSitePFree)) { ok = false; break; }
       d3b::tc_fence_after();
 #pragma unroll
       for (int c = 0; c < BN / 64; ++c)
@@ -335,7 +338,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // O must hold every PV up to j-1: wait for PV_{j-1}'s commit.
         const int pb1 = (j - 1) & 1;
         const uint32_t u1 = (uint32_t)((j - 1) >> 1);
-        if (!d3b::mbar_wait(&bars.p_free[pb1], u1 & 1, abort_flag, p.err, kSitePFree)) { ok = false; break; }
+        if (!d3b::warp_wait(&bars.p_free[pb1], u1 & 1, abort_flag, p.err, kSitePFree)) { ok = false; break; }
         d3b::tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
@@ -355,7 +358,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     if (ok) {
       const int jl = n - 1;
-      ok = d3b::mbar_wait(&bars.p_free[jl & 1], (uint32_t)(jl >> 1) & 1, abort_flag, p.err, kSiteFinal);
+      ok = d3b::warp_wait(&bars.p_free[jl & 1], (uint32_t)(jl >> 1) & 1, abort_flag, p.err, kSiteFinal);
     }
     if (ok) {
       d3b::tc_fence_after();

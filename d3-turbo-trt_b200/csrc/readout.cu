@@ -4,12 +4,17 @@
 //   probs  = softmax(logits / T)
 //
 // One launch. The grid is (row groups of 8) x (option groups of 32). A CTA
-// stages K-chunks of its 8 hidden rows in shared memory (as fp32), each warp
+// stages K-chunks of its 8 hidden rows in shared memory (as fp32); each warp
 // computes 4 options x 8 rows of dot products with fp32 FMAs (the reference
-// computes in fp32, so no tensor-core rounding is introduced), and writes its
-// logits to the workspace. The last CTA of a row group to finish (an atomic
-// ticket per row group) runs the masked softmax with one warp per row and
-// resets the ticket to zero, so the workspace is ready for the next call.
+// computes in fp32, so no tensor-core rounding is introduced), streaming R
+// with 16-byte loads, 16 of them in flight per lane. Logits go to the
+// workspace. The last CTA of a row group to finish (an atomic ticket per row
+// group) runs the masked softmax with one warp per row and resets the ticket,
+// so the workspace is ready for the next call.
+//
+// Workspace layout: [tickets: kMaxGroups x u32 at offset 0][logits: B x n_opt f32].
+// The ticket region never moves, so one zero-filled workspace serves calls of
+// any shape (B <= 8 * kMaxGroups).
 #include "common.cuh"
 
 namespace {
@@ -17,14 +22,17 @@ namespace {
 constexpr int kRows = 8;        // hidden rows per CTA (= warps per CTA)
 constexpr int kOpts = 32;       // options per CTA
 constexpr int kOptsPerWarp = kOpts / kRows;
-constexpr int kChunk = 512;     // K elements staged per step
+constexpr int kChunk = 1024;    // K elements staged per step (8 rows x 4 KB)
+constexpr int kUnroll = 4;      // float4 steps per lane kept in flight, per option
 constexpr int kMaxOpts = 1024;  // softmax keeps n_opt/32 logits per lane
+constexpr int kMaxGroups = 4096;
+constexpr size_t kTicketBytes = kMaxGroups * sizeof(unsigned int);
 
 __device__ __forceinline__ float load_h(const float* p) { return __ldg(p); }
 __device__ __forceinline__ float load_h(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 __device__ __forceinline__ float load_h(const __half* p) { return __half2float(*p); }
 
-template <typename T>
+template <typename T, bool VEC>
 __global__ void __launch_bounds__(kRows * 32) readout_kernel(const T* __restrict__ hidden,
                                                               const float* __restrict__ R,
                                                               const int32_t* __restrict__ counts, float temperature,
@@ -42,6 +50,9 @@ __global__ void __launch_bounds__(kRows * 32) readout_kernel(const T* __restrict
   for (int o = 0; o < kOptsPerWarp; ++o)
 #pragma unroll
     for (int r = 0; r < kRows; ++r) acc[o][r] = 0.f;
+  const float* rrow[kOptsPerWarp];
+#pragma unroll
+  for (int o = 0; o < kOptsPerWarp; ++o) rrow[o] = R + (int64_t)min(o0 + o, n_opt - 1) * K;
 
   for (int kc = 0; kc < K; kc += kChunk) {
     const int kn = min(kChunk, K - kc);
@@ -52,16 +63,42 @@ __global__ void __launch_bounds__(kRows * 32) readout_kernel(const T* __restrict
       hs[r][k] = (row < B && k < kn) ? load_h(hidden + (int64_t)row * K + kc + k) : 0.f;
     }
     __syncthreads();
-    for (int k = lane; k < kn; k += 32) {
-      float h[kRows];
+    if (VEC) {
+      // kn is a multiple of 4; lanes cover 128 consecutive k per step
+      for (int k0 = lane * 4; k0 < kn; k0 += 128 * kUnroll) {
+        float4 w[kUnroll][kOptsPerWarp];
 #pragma unroll
-      for (int r = 0; r < kRows; ++r) h[r] = hs[r][k];
+        for (int u = 0; u < kUnroll; ++u)
 #pragma unroll
-      for (int o = 0; o < kOptsPerWarp; ++o) {
-        const int opt = o0 + o;
-        const float w = opt < n_opt ? __ldg(R + (int64_t)opt * K + kc + k) : 0.f;
+          for (int o = 0; o < kOptsPerWarp; ++o) {
+            const int k = k0 + u * 128;
+            w[u][o] = k < kn ? __ldg(reinterpret_cast<const float4*>(rrow[o] + kc + k)) : make_float4(0, 0, 0, 0);
+          }
 #pragma unroll
-        for (int r = 0; r < kRows; ++r) acc[o][r] = fmaf(h[r], w, acc[o][r]);
+        for (int u = 0; u < kUnroll; ++u) {
+          const int k = k0 + u * 128;
+          if (k >= kn) break;
+#pragma unroll
+          for (int r = 0; r < kRows; ++r) {
+            const float4 h = *reinterpret_cast<const float4*>(&hs[r][k]);
+#pragma unroll
+            for (int o = 0; o < kOptsPerWarp; ++o) {
+              acc[o][r] = fmaf(h.x, w[u][o].x, acc[o][r]);
+              acc[o][r] = fmaf(h.y, w[u][o].y, acc[o][r]);
+              acc[o][r] = fmaf(h.z, w[u][o].z, acc[o][r]);
+              acc[o][r] = fmaf(h.w, w[u][o].w, acc[o][r]);
+            }
+          }
+        }
+      }
+    } else {
+      for (int k = lane; k < kn; k += 32) {
+#pragma unroll
+        for (int o = 0; o < kOptsPerWarp; ++o) {
+          const float w = __ldg(rrow[o] + kc + k);
+#pragma unroll
+          for (int r = 0; r < kRows; ++r) acc[o][r] = fmaf(hs[r][k], w, acc[o][r]);
+        }
       }
     }
   }
@@ -130,47 +167,44 @@ __global__ void __launch_bounds__(kRows * 32) readout_kernel(const T* __restrict
   if (threadIdx.x == 0) tickets[blockIdx.x] = 0u;
 }
 
-size_t ws_layout(int B, int n_opt, size_t* tickets_off) {
-  const size_t logits = ((size_t)B * n_opt * sizeof(float) + 255) & ~(size_t)255;
-  const size_t groups = (size_t)(B + kRows - 1) / kRows;
-  *tickets_off = logits;
-  return logits + ((groups * sizeof(unsigned int) + 255) & ~(size_t)255);
+template <typename T>
+void launch_typed(const void* hidden, const float* readout, const int32_t* counts, float temperature, float* probs,
+                  int B, int K, int n_opt, float* logits, unsigned int* tickets, cudaStream_t s) {
+  dim3 grid((B + kRows - 1) / kRows, (n_opt + kOpts - 1) / kOpts), block(kRows * 32);
+  const bool vec = (K % 4 == 0) && (reinterpret_cast<uintptr_t>(readout) % 16 == 0);
+  if (vec)
+    readout_kernel<T, true><<<grid, block, 0, s>>>(static_cast<const T*>(hidden), readout, counts, temperature,
+                                                   probs, B, K, n_opt, logits, tickets);
+  else
+    readout_kernel<T, false><<<grid, block, 0, s>>>(static_cast<const T*>(hidden), readout, counts, temperature,
+                                                    probs, B, K, n_opt, logits, tickets);
 }
 
 }  // namespace
 
 extern "C" size_t d3b_readout_workspace_size(int B, int n_opt) {
   if (B <= 0 || n_opt <= 0) return 0;
-  size_t off;
-  return ws_layout(B, n_opt, &off);
+  return kTicketBytes + (((size_t)B * n_opt * sizeof(float) + 255) & ~(size_t)255);
 }
 
 extern "C" int d3b_readout(const void* hidden, int h_dtype, const float* readout, const int32_t* counts,
                            float temperature, float* probs, int B, int K, int n_opt, void* workspace,
                            size_t workspace_bytes, d3b_stream_t stream) {
   if (B < 0 || K <= 0 || n_opt <= 0 || n_opt > kMaxOpts) return D3B_EINVAL;
+  if (B > kRows * kMaxGroups) return D3B_EINVAL;
   if (!(temperature > 0.f)) return D3B_EINVAL;
   if (B == 0) return D3B_OK;
   if (!hidden || !readout || !counts || !probs || !workspace) return D3B_EINVAL;
-  size_t tickets_off;
-  const size_t need = ws_layout(B, n_opt, &tickets_off);
-  if (workspace_bytes < need) return D3B_ENOSPACE;
-  float* logits = static_cast<float*>(workspace);
-  unsigned int* tickets = reinterpret_cast<unsigned int*>(static_cast<char*>(workspace) + tickets_off);
-  dim3 grid((B + kRows - 1) / kRows, (n_opt + kOpts - 1) / kOpts), block(kRows * 32);
+  if (workspace_bytes < d3b_readout_workspace_size(B, n_opt)) return D3B_ENOSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) % 16) return D3B_EALIGN;
+  unsigned int* tickets = static_cast<unsigned int*>(workspace);
+  float* logits = reinterpret_cast<float*>(static_cast<char*>(workspace) + kTicketBytes);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (h_dtype) {
-    case D3B_F32:
-      readout_kernel<float><<<grid, block, 0, s>>>(static_cast<const float*>(hidden), readout, counts, temperature,
-                                                   probs, B, K, n_opt, logits, tickets);
-      break;
-    case D3B_F16:
-      readout_kernel<__half><<<grid, block, 0, s>>>(static_cast<const __half*>(hidden), readout, counts,
-                                                    temperature, probs, B, K, n_opt, logits, tickets);
-      break;
+    case D3B_F32: launch_typed<float>(hidden, readout, counts, temperature, probs, B, K, n_opt, logits, tickets, s); break;
+    case D3B_F16: launch_typed<__half>(hidden, readout, counts, temperature, probs, B, K, n_opt, logits, tickets, s); break;
     case D3B_BF16:
-      readout_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(static_cast<const __nv_bfloat16*>(hidden), readout,
-                                                           counts, temperature, probs, B, K, n_opt, logits, tickets);
+      launch_typed<__nv_bfloat16>(hidden, readout, counts, temperature, probs, B, K, n_opt, logits, tickets, s);
       break;
     default: return D3B_EUNSUPPORTED;
   }

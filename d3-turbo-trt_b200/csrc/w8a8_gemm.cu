@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int m0 = (t % num_m) * BM, n0 = (t / num_m) * BN;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!d3b::mbar_wait(&bars.tfull[acc], acc_phase, abort_flag, err, kSiteEpi)) break;
+      if (!d3b::warp_wait(&bars.tfull[acc], acc_phase, abort_flag, err, kSiteEpi)) break;
       d3b::tc_fence_after();
       const int row = m0 + row_in_tile;
       const float sa_row = (out_kind != D3B_I32 && row < M) ? __ldg(sa + row) : 0.f;

@@ -1,0 +1,131 @@
+"""Run one hot-path kernel on one configuration a fixed number of times.
+
+    python -m d3_turbo_trt_b200.profile --kernel attention --config cfg3a --launches 3
+
+Meant as the target of an ``ncu`` capture (one kernel, a few launches, a small
+device footprint) and as a quick device-time probe: it prints the median
+CUDA-event time per launch and the algorithmic work per launch. Configs follow
+cfg3a (4096-token state + 16 x 64-token blocks), cfg3b (16384 +
+255 x 48), state4k (the state pass of cfg3a), cfg2 (W8A8 4096 x 5120 x 13824),
+cfg4 (readout 255 x 5120 x 255). Inputs are seeded synthetic tensors.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import statistics
+
+import torch
+
+from .kernels import prefix_bidir as pb
+from .model import quant
+from .model.readout import probabilities_tensor
+
+ATTN = {
+    "cfg3a": dict(B=16, H=32, Hkv=4, L=64, D=128, S=4096),
+    "cfg3b": dict(B=255, H=32, Hkv=4, L=48, D=128, S=16384),
+    "cfg1": dict(B=8, H=8, Hkv=2, L=32, D=64, S=512),
+}
+
+
+def _attention(cfg: str, dev: torch.device):
+    c = ATTN[cfg]
+    g = torch.Generator().manual_seed(0)
+    B, H, Hkv, L, D, S = (c[k] for k in ("B", "H", "Hkv", "L", "D", "S"))
+    q = torch.randn(B, L, H, D, generator=g).to(torch.bfloat16).to(dev).permute(0, 2, 1, 3)
+    kq = torch.randn(B, L, Hkv, D, generator=g).to(torch.bfloat16).to(dev).permute(0, 2, 1, 3)
+    vq = torch.randn(B, L, Hkv, D, generator=g).to(torch.bfloat16).to(dev).permute(0, 2, 1, 3)
+    ks = torch.randn(S, Hkv, D, generator=g).to(torch.bfloat16).to(dev).permute(1, 0, 2)
+    vs = torch.randn(S, Hkv, D, generator=g).to(torch.bfloat16).to(dev).permute(1, 0, 2)
+    out = torch.empty(B, H, L, D, dtype=torch.bfloat16, device=dev)
+    lens = [L] * B
+    flops = 4.0 * H * D * B * L * (S + L)
+    return (lambda: pb.prefix_bidir_attention(q, ks, vs, kq, vq, lens, scale=D ** -0.5, out=out)), {"flops": flops}
+
+
+def _state(dev: torch.device, tokens: int = 4096):
+    g = torch.Generator().manual_seed(1)
+    H, Hkv, D = 32, 4, 128
+    q = torch.randn(1, tokens, H, D, generator=g).to(torch.bfloat16).to(dev).permute(0, 2, 1, 3)
+    k = torch.randn(1, tokens, Hkv, D, generator=g).to(torch.bfloat16).to(dev).permute(0, 2, 1, 3)
+    v = torch.randn(1, tokens, Hkv, D, generator=g).to(torch.bfloat16).to(dev).permute(0, 2, 1, 3)
+    return (lambda: pb.state_attention(q, k, v, scale=D ** -0.5)), {"flops": 4.0 * H * D * tokens * tokens}
+
+
+def _gemm(mode: str, dev: torch.device, M=4096, K=5120, N=13824):
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(dev)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+    layer = quant.QuantLinear(K, N, mode=mode, dtype=torch.bfloat16, device=dev)
+    layer.load_full(w)
+    qa, sa = quant.quantize_rows(x, mode)
+    fn = lambda: quant.scaled_mm(qa, layer.weight, sa, layer.weight_scale, out_dtype=torch.bfloat16)
+    return fn, {"flops": 2.0 * M * N * K, "bytes": M * K + N * K + M * N * 2}
+
+
+def _act_quant(mode: str, dev: torch.device, M=4096, K=5120):
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(dev)
+    return (lambda: quant.quantize_rows(x, mode)), {"bytes": M * K * 3 + M * 4}
+
+
+def _readout(dev: torch.device, B=255, K=5120, n_opt=255):
+    g = torch.Generator().manual_seed(4)
+    h = torch.randn(B, K, generator=g).to(torch.bfloat16).to(dev)
+    r = (torch.randn(n_opt, K, generator=g) * 0.02).to(dev)
+    counts = torch.full((B,), n_opt, dtype=torch.int32, device=dev)
+    return (lambda: probabilities_tensor(h, r, counts, temperature=1.0)), {
+        "flops": 2.0 * B * K * n_opt, "bytes": B * K * 2 + n_opt * K * 4 + B * n_opt * 4}
+
+
+def build(kernel: str, config: str, dev: torch.device):
+    if kernel == "attention":
+        return _state(dev) if config == "state4k" else _attention(config, dev)
+    if kernel == "gemm_fp8":
+        return _gemm("fp8", dev)
+    if kernel == "gemm_int8":
+        return _gemm("int8", dev)
+    if kernel == "act_quant_fp8":
+        return _act_quant("fp8", dev)
+    if kernel == "act_quant_int8":
+        return _act_quant("int8", dev)
+    if kernel == "readout":
+        return _readout(dev)
+    raise SystemExit(f"unknown kernel {kernel!r}")
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel", required=True,
+                    choices=["attention", "gemm_fp8", "gemm_int8", "act_quant_fp8", "act_quant_int8", "readout"])
+    ap.add_argument("--config", default="cfg3a", choices=[*ATTN, "state4k", "cfg2", "cfg4"])
+    ap.add_argument("--launches", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=1)
+    args = ap.parse_args()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    fn, work = build(args.kernel, args.config, dev)
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(args.launches):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(1_000_000)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    ms = statistics.median(times)
+    rep = {"kernel": args.kernel, "config": args.config, "ms": ms}
+    if "flops" in work:
+        rep["tflops"] = work["flops"] / ms / 1e9
+    if "bytes" in work:
+        rep["gbs"] = work["bytes"] / ms / 1e6
+    print(json.dumps(rep))
+
+
+if __name__ == "__main__":
+    main()

@@ -101,6 +101,7 @@ def test_readout_rejects_bad_arguments():
     assert lib.d3b_readout(a, _lib.BF16, a, a, 1.0, a, 4, 64, 2000, a, need, None) == _lib.EINVAL
     assert lib.d3b_readout(a, 7, a, a, 1.0, a, 4, 64, 255, a, need, None) == _lib.EUNSUPPORTED
     assert lib.d3b_readout_workspace_size(0, 255) == 0
+    assert lib.d3b_readout(a, _lib.BF16, a, a, 1.0, a, 8 * 4096 + 1, 64, 255, a, 1 << 40, None) == _lib.EINVAL
 
 
 def test_wait_selftest_rejects_bad_limit():

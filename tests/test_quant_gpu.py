@@ -191,7 +191,7 @@ def test_cfg2_full_size(mode):
     assert torch.equal(y, y32.to(torch.bfloat16))
     # the kernel against torch._scaled_mm (the reference's GPU call), fp8 only
     if mode == "fp8":
-        ts = torch._scaled_mm(qa, layer.weight.t(), scale_a=sa[:, None], scale_b=layer.weight_scale[None, :],
+        ts = torch._scaled_mm(qa, layer.weight.t(), scale_a=sa, scale_b=layer.weight_scale[None, :],
                               out_dtype=torch.float32)
         assert float((ts - y32).abs().max()) <= 2e-2
     assert _lib.device_error() == 0
