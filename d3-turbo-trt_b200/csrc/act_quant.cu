@@ -1,11 +1,11 @@
 // Per-token activation quantisation (d3trt/model/quant.py:92-100) and, on a
 // weight matrix, per-output-channel weight quantisation (quant.py:77-89).
 //
-// One warp owns one row. Rows up to 32 lanes x 8 x kMaxVec elements are read
-// once into registers with 16-byte loads (all in flight together), reduced to
-// max|x| with warp shuffles and quantised from registers: HBM traffic is the
-// algorithmic minimum (read x once, write q and the scale). Longer rows use a
-// two-pass variant whose second read hits L2.
+// One warp owns one row (8 warps per CTA, so many rows per SM are in flight).
+// Pass 1 reads the row with 16-byte loads (batches of 8 per lane in flight) and reduces max|x| with warp shuffles; pass 2 re-reads the
+// row, which the first pass has just brought into L2, and writes the 8-bit
+// codes with 8-byte stores. HBM traffic is the algorithmic minimum: read x
+// once, write q and the scale.
 //
 // Bit-exactness with the reference formulas:
 //   amax  = max(max_k |x|, 1e-12f)                (fp32, order independent)
@@ -17,8 +17,9 @@
 // The code only depends on which side of a rounding boundary of the target
 // format (an e4m3 midpoint, or k + 1/2 for int8) the quotient lies; when v is
 // 4 ulp or more away from every boundary, v and RN(x / scale) give the same
-// code. Otherwise the element is recomputed with __fdiv_rn (IEEE). So the
-// codes equal those of the reference's IEEE division in every case.
+// code. Otherwise (and for every |v| in the e4m3 subnormal range) the element
+// is recomputed with __fdiv_rn (IEEE). So the codes equal those of the
+// reference's IEEE division in every case.
 #include "common.cuh"
 
 namespace {
@@ -26,7 +27,7 @@ namespace {
 constexpr int kWarpsPerCta = 8;
 
 template <typename T>
-struct Vec;  // 16-byte vector of T converted to fp32
+struct Vec;  // 16-byte vector of T as fp32
 template <>
 struct Vec<float> {
   static constexpr int N = 4;
@@ -34,12 +35,10 @@ struct Vec<float> {
     v[0] = __uint_as_float(a.x); v[1] = __uint_as_float(a.y); v[2] = __uint_as_float(a.z);
     v[3] = __uint_as_float(a.w);
   }
-  __device__ static void load(const float* p, float (&v)[8]) { unpack(__ldg(reinterpret_cast<const uint4*>(p)), v); }
 };
 template <>
 struct Vec<__nv_bfloat16> {
   static constexpr int N = 8;
-  __device__ static void load(const __nv_bfloat16* p, float (&v)[8]) { unpack(__ldg(reinterpret_cast<const uint4*>(p)), v); }
   __device__ static void unpack(uint4 a, float (&v)[8]) {
     const uint32_t w[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
@@ -52,13 +51,11 @@ struct Vec<__nv_bfloat16> {
 template <>
 struct Vec<__half> {
   static constexpr int N = 8;
-  __device__ static void load(const __half* p, float (&v)[8]) { unpack(__ldg(reinterpret_cast<const uint4*>(p)), v); }
   __device__ static void unpack(uint4 a, float (&v)[8]) {
     const uint32_t w[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
-      float2 f = __half22float2(h);
+      float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
       v[2 * i] = f.x;
       v[2 * i + 1] = f.y;
     }
@@ -76,31 +73,30 @@ __device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
   return r;
 }
 
-// True when v may lie within 4 fp32 ulp of a rounding boundary of the target
-// format (then RN(x/s) must be computed exactly). |v| <= 448 (fp8) or 127.
-template <int MODE>
-__device__ __forceinline__ bool near_boundary(float v) {
-  const float a = fabsf(v);
-  if (MODE == D3B_MODE_FP8) {
-    if (a >= 0.015625f) {  // e4m3 normal range: 3 mantissa bits, tie at dropped bits == 0x80000
-      const int dropped = static_cast<int>(__float_as_uint(a) & 0xFFFFFu);
-      return abs(dropped - 0x80000) <= 4;
-    }
-    const float t = a * 512.f;  // subnormal quantum 2^-9 (exact scaling)
-    return fabsf(t - floorf(t) - 0.5f) <= 1.0f / 32768.f;
-  }
-  return fabsf(a - floorf(a) - 0.5f) <= 1.0f / 32768.f;  // 4 ulp at |v| < 128
-}
+// The exact IEEE quotient, out of line so the compiler cannot evaluate it
+// speculatively for every element: it runs only for the rare elements whose
+// fast quotient lies next to a rounding boundary.
+__device__ __noinline__ float exact_quotient(float x, float scale) { return __fdiv_rn(x, scale); }
 
+// RN(x / scale), given rcp = RN(1 / scale): the fast product unless it may sit
+// within 4 ulp of a rounding boundary of the target format.
 template <int MODE>
 __device__ __forceinline__ float quotient(float x, float scale, float rcp) {
-  float v = __fmul_rn(x, rcp);
-  const float lim = MODE == D3B_MODE_FP8 ? 448.f : 127.f;
-  if (near_boundary<MODE>(fminf(fmaxf(v, -lim), lim))) v = __fdiv_rn(x, scale);
+  const float v = __fmul_rn(x, rcp);
+  bool near;
+  if (MODE == D3B_MODE_FP8) {
+    const float a = fminf(fabsf(v), 448.f);
+    // e4m3 normals keep 3 mantissa bits: a tie has dropped bits == 0x80000
+    const int dropped = static_cast<int>(__float_as_uint(a) & 0xFFFFFu);
+    near = (a < 0.015625f) || (abs(dropped - 0x80000) <= 4);
+  } else {
+    const float a = fminf(fabsf(v), 127.f);
+    near = fabsf(a - floorf(a) - 0.5f) <= 1.0f / 32768.f;  // 4 ulp at |v| < 128
+  }
+  if (__builtin_expect(near, 0)) return exact_quotient(x, scale);
   return v;
 }
 
-// Two elements -> two codes in the low 16 bits (element 0 in bits 0..7).
 template <int MODE>
 __device__ __forceinline__ uint32_t quant2(float x0, float x1, float scale, float rcp) {
   const float v0 = quotient<MODE>(x0, scale, rcp), v1 = quotient<MODE>(x1, scale, rcp);
@@ -113,11 +109,6 @@ __device__ __forceinline__ uint32_t quant2(float x0, float x1, float scale, floa
   }
 }
 
-template <int MODE>
-__device__ __forceinline__ uint32_t quant1(float x, float scale, float rcp) {
-  return quant2<MODE>(x, 0.f, scale, rcp) & 0xFFu;
-}
-
 __device__ __forceinline__ float row_scale(float amax, int mode) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -125,136 +116,94 @@ __device__ __forceinline__ float row_scale(float amax, int mode) {
   return __fdiv_rn(amax, mode == D3B_MODE_FP8 ? 448.f : 127.f);
 }
 
-// Single pass: the row lives in registers (nvec 16-byte vectors per lane).
-constexpr int kMaxVec = 24;
-constexpr int kCachedWarps = 4;
-
+// 8 (bf16/f16) or 4 (f32) codes from one 16-byte vector -> one 8- or 4-byte store.
 template <typename T, int MODE>
-__global__ void __launch_bounds__(kCachedWarps * 32) act_quant_cached_kernel(const T* __restrict__ x, int64_t ldx,
-                                                                              uint8_t* __restrict__ q,
-                                                                              float* __restrict__ scale_out,
-                                                                              int64_t M, int64_t K) {
-  constexpr int VN = Vec<T>::N;
-  const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * kCachedWarps + (threadIdx.x >> 5);
-  if (row >= M) return;
-  const T* xr = x + row * ldx;
-  uint8_t* qr = q + row * K;
-  const int nvec = static_cast<int>(K / (VN * 32));  // full vectors per lane (K % (VN*32) == 0 here)
-  uint4 raw[kMaxVec];
-#pragma unroll
-  for (int i = 0; i < kMaxVec; ++i)
-    if (i < nvec) raw[i] = __ldg(reinterpret_cast<const uint4*>(xr + (int64_t)(i * 32 + lane) * VN));
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < kMaxVec; ++i) {
-    if (i < nvec) {
-      float v[8];
-      Vec<T>::unpack(raw[i], v);
-#pragma unroll
-      for (int e = 0; e < VN; ++e) amax = fmaxf(amax, fabsf(v[e]));
-    }
-  }
-  const float scale = row_scale(amax, MODE);
-  const float rcp = __frcp_rn(scale);
-  if (lane == 0) scale_out[row] = scale;
-#pragma unroll
-  for (int i = 0; i < kMaxVec; ++i) {
-    if (i < nvec) {
-      float v[8];
-      Vec<T>::unpack(raw[i], v);
-      uint8_t* dst = qr + (int64_t)(i * 32 + lane) * VN;
-      if (VN == 8) {
-        const uint32_t w0 = quant2<MODE>(v[0], v[1], scale, rcp) | (quant2<MODE>(v[2], v[3], scale, rcp) << 16);
-        const uint32_t w1 = quant2<MODE>(v[4], v[5], scale, rcp) | (quant2<MODE>(v[6], v[7], scale, rcp) << 16);
-        *reinterpret_cast<uint2*>(dst) = make_uint2(w0, w1);
-      } else {
-        *reinterpret_cast<uint32_t*>(dst) =
-            quant2<MODE>(v[0], v[1], scale, rcp) | (quant2<MODE>(v[2], v[3], scale, rcp) << 16);
-      }
-    }
+__device__ __forceinline__ void quant_vec(uint4 raw, float scale, float rcp, uint8_t* dst) {
+  float v[8];
+  Vec<T>::unpack(raw, v);
+  if (Vec<T>::N == 8) {
+    const uint32_t w0 = quant2<MODE>(v[0], v[1], scale, rcp) | (quant2<MODE>(v[2], v[3], scale, rcp) << 16);
+    const uint32_t w1 = quant2<MODE>(v[4], v[5], scale, rcp) | (quant2<MODE>(v[6], v[7], scale, rcp) << 16);
+    *reinterpret_cast<uint2*>(dst) = make_uint2(w0, w1);
+  } else {
+    *reinterpret_cast<uint32_t*>(dst) =
+        quant2<MODE>(v[0], v[1], scale, rcp) | (quant2<MODE>(v[2], v[3], scale, rcp) << 16);
   }
 }
 
-template <typename T, int MODE>
+// ---------------------------------------------------------------------------
+// two-pass warp-per-row kernel; VEC: 16-byte aligned rows with K % 8 == 0
+// ---------------------------------------------------------------------------
+template <typename T, int MODE, bool VEC>
 __global__ void __launch_bounds__(kWarpsPerCta * 32) act_quant_kernel(const T* __restrict__ x, int64_t ldx,
                                                                        uint8_t* __restrict__ q,
                                                                        float* __restrict__ scale_out, int64_t M,
-                                                                       int64_t K, int vec_ok) {
+                                                                       int64_t K) {
+  constexpr int VN = Vec<T>::N;
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
   if (row >= M) return;
   const T* xr = x + row * ldx;
   uint8_t* qr = q + row * K;
-  constexpr int VN = Vec<T>::N;
-
-  // ---- pass 1: max |x| ----
   float amax = 0.f;
-  int64_t k_vec_end = 0;
-  if (vec_ok) {
-    k_vec_end = (K / (VN * 32)) * (VN * 32);
-#pragma unroll 4
-    for (int64_t k = (int64_t)lane * VN; k < k_vec_end; k += 32 * VN) {
-      float v[8];
-      Vec<T>::load(xr + k, v);
+  if (VEC) {
+    // batches of kBatch 16-byte loads per lane, all issued before any use
+    constexpr int kBatch = 8;
+    const uint4* src = reinterpret_cast<const uint4*>(xr);
+    const int nvec = static_cast<int>(K / VN);
+    for (int k0 = lane; k0 < nvec; k0 += 32 * kBatch) {
+      uint4 raw[kBatch];
 #pragma unroll
-      for (int i = 0; i < VN; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    }
-  }
-  for (int64_t k = k_vec_end + lane; k < K; k += 32) amax = fmaxf(amax, fabsf(to_f32(xr[k])));
-  const float scale = row_scale(amax, MODE);
-  const float rcp = __frcp_rn(scale);
-  if (lane == 0) scale_out[row] = scale;
-
-  // ---- pass 2: codes ----
-  if (vec_ok) {
-#pragma unroll 4
-    for (int64_t k = (int64_t)lane * VN; k < k_vec_end; k += 32 * VN) {
-      float v[8];
-      Vec<T>::load(xr + k, v);
-      if (VN == 8) {
-        const uint32_t w0 = quant2<MODE>(v[0], v[1], scale, rcp) | (quant2<MODE>(v[2], v[3], scale, rcp) << 16);
-        const uint32_t w1 = quant2<MODE>(v[4], v[5], scale, rcp) | (quant2<MODE>(v[6], v[7], scale, rcp) << 16);
-        *reinterpret_cast<uint2*>(qr + k) = make_uint2(w0, w1);
-      } else {
-        const uint32_t w0 = quant2<MODE>(v[0], v[1], scale, rcp) | (quant2<MODE>(v[2], v[3], scale, rcp) << 16);
-        *reinterpret_cast<uint32_t*>(qr + k) = w0;
+      for (int u = 0; u < kBatch; ++u)
+        raw[u] = k0 + 32 * u < nvec ? __ldg(src + k0 + 32 * u) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        float v[8];
+        Vec<T>::unpack(raw[u], v);
+#pragma unroll
+        for (int e = 0; e < VN; ++e) amax = fmaxf(amax, fabsf(v[e]));
       }
     }
+    const float scale = row_scale(amax, MODE);
+    const float rcp = __frcp_rn(scale);
+    if (lane == 0) scale_out[row] = scale;
+    for (int k0 = lane; k0 < nvec; k0 += 32 * kBatch) {
+      uint4 raw[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u)
+        if (k0 + 32 * u < nvec) raw[u] = __ldg(src + k0 + 32 * u);
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u)
+        if (k0 + 32 * u < nvec) quant_vec<T, MODE>(raw[u], scale, rcp, qr + (int64_t)(k0 + 32 * u) * VN);
+    }
+  } else {
+    for (int64_t k = lane; k < K; k += 32) amax = fmaxf(amax, fabsf(to_f32(xr[k])));
+    const float scale = row_scale(amax, MODE);
+    const float rcp = __frcp_rn(scale);
+    if (lane == 0) scale_out[row] = scale;
+    for (int64_t k = lane; k < K; k += 32)
+      qr[k] = static_cast<uint8_t>(quant2<MODE>(to_f32(xr[k]), 0.f, scale, rcp) & 0xFFu);
   }
-  for (int64_t k = k_vec_end + lane; k < K; k += 32)
-    qr[k] = static_cast<uint8_t>(quant1<MODE>(to_f32(xr[k]), scale, rcp));
 }
 
 template <typename T>
 int launch_typed(const void* x, int64_t ldx, void* q, float* scale, int64_t M, int64_t K, int mode,
                  cudaStream_t stream) {
-  const int elem = sizeof(T);
-  // 16-byte vector loads need an aligned base and row pitch; 4/8-byte stores
-  // need K to keep every row start aligned.
-  const int vec_ok = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((ldx * elem) % 16 == 0) &&
-                     (reinterpret_cast<uintptr_t>(q) % 16 == 0) && (K % 8 == 0);
-  constexpr int VN = Vec<T>::N;
-  if (vec_ok && K % (VN * 32) == 0 && K / (VN * 32) <= kMaxVec) {
-    const int64_t blocks = (M + kCachedWarps - 1) / kCachedWarps;
-    if (blocks > 0x7FFFFFFF) return D3B_EINVAL;
-    if (mode == D3B_MODE_FP8)
-      act_quant_cached_kernel<T, D3B_MODE_FP8><<<(unsigned)blocks, kCachedWarps * 32, 0, stream>>>(
-          static_cast<const T*>(x), ldx, static_cast<uint8_t*>(q), scale, M, K);
-    else
-      act_quant_cached_kernel<T, D3B_MODE_INT8><<<(unsigned)blocks, kCachedWarps * 32, 0, stream>>>(
-          static_cast<const T*>(x), ldx, static_cast<uint8_t*>(q), scale, M, K);
-    return d3b_host::check_launch();
-  }
+  const int64_t elem = sizeof(T);
+  const bool vec = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((ldx * elem) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(q) % 16 == 0) && (K % 8 == 0);
   const int64_t blocks = (M + kWarpsPerCta - 1) / kWarpsPerCta;
   if (blocks > 0x7FFFFFFF) return D3B_EINVAL;
-  dim3 grid((unsigned)blocks), block(kWarpsPerCta * 32);
-  if (mode == D3B_MODE_FP8)
-    act_quant_kernel<T, D3B_MODE_FP8><<<grid, block, 0, stream>>>(static_cast<const T*>(x), ldx,
-                                                                   static_cast<uint8_t*>(q), scale, M, K, vec_ok);
-  else
-    act_quant_kernel<T, D3B_MODE_INT8><<<grid, block, 0, stream>>>(static_cast<const T*>(x), ldx,
-                                                                    static_cast<uint8_t*>(q), scale, M, K, vec_ok);
+  const dim3 grid((unsigned)blocks), block(kWarpsPerCta * 32);
+  const T* xt = static_cast<const T*>(x);
+  uint8_t* qt = static_cast<uint8_t*>(q);
+  if (mode == D3B_MODE_FP8) {
+    if (vec) act_quant_kernel<T, D3B_MODE_FP8, true><<<grid, block, 0, stream>>>(xt, ldx, qt, scale, M, K);
+    else act_quant_kernel<T, D3B_MODE_FP8, false><<<grid, block, 0, stream>>>(xt, ldx, qt, scale, M, K);
+  } else {
+    if (vec) act_quant_kernel<T, D3B_MODE_INT8, true><<<grid, block, 0, stream>>>(xt, ldx, qt, scale, M, K);
+    else act_quant_kernel<T, D3B_MODE_INT8, false><<<grid, block, 0, stream>>>(xt, ldx, qt, scale, M, K);
+  }
   return d3b_host::check_launch();
 }
 

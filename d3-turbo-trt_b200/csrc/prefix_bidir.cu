@@ -109,6 +109,91 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return FP16 ? d3b::pack_f16x2(lo, hi) : d3b::pack_bf16x2(lo, hi);
 }
 
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Max of N values: three-input max, 8 independent accumulators (short
+// dependency chains; N/2 + 4 instructions).
+template <int N>
+__device__ __forceinline__ float max_n(const float* v) {
+  float a[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) a[k] = v[k];
+#pragma unroll
+  for (int c = 8; c < N; c += 16)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[k] = max3(a[k], v[c + k], v[c + 8 + k]);
+  return max3(max3(a[0], a[1], a[2]), max3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
+}
+
+// (d0, d1) = (a0, a1) * (b, b) + (c, c) as one packed fp32x2 FMA.
+__device__ __forceinline__ void fma2_bc(float& d0, float& d1, float a0, float a1, float b, float c) {
+  asm("{.reg .b64 x, y, z; mov.b64 x, {%2, %3}; mov.b64 y, {%4, %4}; mov.b64 z, {%5, %5};"
+      " fma.rn.f32x2 x, x, y, z; mov.b64 {%0, %1}, x;}"
+      : "=f"(d0), "=f"(d1) : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+// (d0, d1) = (a0, a1) * (b0, b1) + (c, c)
+__device__ __forceinline__ void fma2_c(float& d0, float& d1, float a0, float a1, float b0, float b1, float c) {
+  asm("{.reg .b64 x, y, z; mov.b64 x, {%2, %3}; mov.b64 y, {%4, %5}; mov.b64 z, {%6, %6};"
+      " fma.rn.f32x2 x, x, y, z; mov.b64 {%0, %1}, x;}"
+      : "=f"(d0), "=f"(d1) : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c));
+}
+// (a0, a1) += (b0, b1)
+__device__ __forceinline__ void add2(float& a0, float& a1, float b0, float b1) {
+  asm("{.reg .b64 x, y; mov.b64 x, {%0, %1}; mov.b64 y, {%2, %3}; add.rn.f32x2 x, x, y; mov.b64 {%0, %1}, x;}"
+      : "+f"(a0), "+f"(a1) : "f"(b0), "f"(b1));
+}
+
+// 2^x for a pair on the FMA pipe (x <= 8): Cody-Waite range reduction
+// x = r + f with r = round(x) (the 1.5 * 2^23 shifter puts r in the low
+// mantissa bits of t), f in [-1/2, 1/2], 2^f from a degree-3 polynomial
+// (least-squares fit of 2^f on Chebyshev nodes of [-1/2, 1/2], max relative
+// error 7.8e-5, well below the bf16 rounding of P), and 2^r added to the
+// exponent field. Inputs below -126 are clamped: 2^-126 stands for 0.
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& p0, float& p1) {
+  constexpr float kShift = 12582912.f;  // 1.5 * 2^23
+  x0 = fmaxf(x0, -126.f);
+  x1 = fmaxf(x1, -126.f);
+  float t0, t1, r0, r1, f0, f1;
+  fma2_bc(t0, t1, x0, x1, 1.f, kShift);      // t = x + shift (round to nearest integer)
+  fma2_bc(r0, r1, t0, t1, 1.f, -kShift);     // r = round(x)
+  fma2_c(f0, f1, r0, r1, -1.f, -1.f, 0.f);   // -r
+  add2(f0, f1, x0, x1);                      // f = x - r
+  float q0, q1;
+  fma2_bc(q0, q1, f0, f1, 0.05508868396282196f, 0.24260404706001282f);
+  fma2_c(q0, q1, q0, q1, f0, f1, 0.6932762265205383f);
+  fma2_c(q0, q1, q0, q1, f0, f1, 0.9999289512634277f);
+  p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+  p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
+}
+
+// P = 2^(s * sl2 - m) for one row of N scores: packed pairs into pk (bf16 or
+// f16), returns the row sum of the fp32 values. One pair in four goes through
+// the FMA-pipe exponential, the rest through MUFU ex2, so neither unit alone
+// bounds the softmax.
+template <int N, int FP16>
+__device__ __forceinline__ float exp_row(const float* s, float sl2, float m, uint32_t* pk) {
+  float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int c = 0; c < N; c += 2) {
+    float x0, x1, p0, p1;
+    fma2_bc(x0, x1, s[c], s[c + 1], sl2, -m);
+    if (((c >> 1) & 3) == 3) {
+      exp2_poly2(x0, x1, p0, p1);
+    } else {
+      p0 = d3b::ex2_approx(x0);
+      p1 = d3b::ex2_approx(x1);
+    }
+    const int k = ((c >> 1) & 3) * 2;
+    add2(part[k], part[k + 1], p0, p1);
+    pk[c / 2] = pack2<FP16>(p0, p1);
+  }
+  return ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
+}
+
 template <int D, int BN, int FP16>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     prefix_bidir_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapKs,
@@ -307,25 +392,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int c = 0; c < BN; ++c)
           if (c >= valid) s[c] = -INFINITY;
       }
-      float mx = s[0];
-#pragma unroll
-      for (int c = 1; c < BN; ++c) mx = fmaxf(mx, s[c]);
-      const float m_tile = mx * sl2;
+      const float m_tile = max_n<BN>(s) * sl2;
       // Lazy rescale, decided per warp: tcgen05.ld/st are warp-collective, so
       // if any row of the warp needs a new reference max, every row of the
       // warp moves to its exact running max (alpha = 1 where it is unchanged).
       const bool rescale = __any_sync(0xffffffffu, m_tile > m_ref + kRescaleThreshold);
       const float m_new = rescale ? fmaxf(m_ref, m_tile) : m_ref;
       const float alpha = rescale ? d3b::ex2_approx(m_ref - m_new) : 1.f;
-      float rowsum = 0.f;
       uint32_t pk[BN / 2];
-#pragma unroll
-      for (int c = 0; c < BN; c += 2) {
-        const float p0 = d3b::ex2_approx(fmaf(s[c], sl2, -m_new));
-        const float p1 = d3b::ex2_approx(fmaf(s[c + 1], sl2, -m_new));
-        rowsum += p0 + p1;
-        pk[c / 2] = pack2<FP16>(p0, p1);
-      }
+      const float rowsum = exp_row<BN, FP16>(s, sl2, m_new, pk);
       // P[sb] is free once PV_{j-2} (its previous reader) has completed.
       if (!d3b::warp_wait(&bars.p_free[sb], (u & 1) ^ 1, abort_flag, p.err, kSitePFree)) { ok = false; break; }
       d3b::tc_fence_after();
@@ -392,6 +467,430 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 1) d3b::tmem_dealloc(tmem_base, C::TMEM_COLS);
 }
 
+// ===========================================================================
+// Two Q tiles per CTA (D <= 128): ping-pong between two softmax warpgroups.
+//
+//   warps 0-3  softmax + epilogue of Q tile A     warps 4-7  same for tile B
+//   warp 8     TMA producer (K_0, V_0, K_1, V_1, ... into a slot ring)
+//   warp 9     TMEM owner + tcgen05.mma issuer   (warps 10-11 idle)
+// Registers: launched at 168 per thread (384 threads = 64512); the producer/MMA
+// warpgroup drops to 104 and the softmax warpgroups rise to 200 (setmaxnreg:
+// 128 * 104 + 256 * 200 = 64512, the launch budget), so a softmax thread holds
+// a whole S row without spilling.
+// TMEM (512 columns): O_A | O_B (D each) | S_A | S_B (128 each). P_X (bf16/f16,
+// 64 columns) is written into the upper half of S_X once S_X has been read.
+// P is published in two halves (keys 0-63, then 64-127, separate barriers):
+// the first four PV MMAs start while the softmax still exponentiates the
+// second half.
+// MMA order per key tile j:  QK_A(j)  PV_B(j-1)  QK_B(j)  PV_A(j)
+// so while the tensor core works on one tile, the other tile's softmax runs.
+// A CTA whose second tile has no real token (e.g. the third tile of a 48-token
+// block) runs tile A alone with S double-buffered in S_A / S_B instead:
+// QK(j+1) then overlaps the softmax of S(j), PV(j) reads P from S[j % 2].
+// QK_X(j+1) overwrites S_X, whose upper half still holds P_X(j) for PV_X(j).
+// Both are issued by the same thread in that order, and tcgen05.mma
+// operations of one issuing thread execute in issue order on the SM's tensor
+// core, so QK_X(j+1) cannot write S_X before PV_X(j) has read P_X(j). This is
+// an observed property of the hardware, not one of the PTX ISA's guaranteed
+// "pipelined" pairs (those cover MMAs on the same accumulator). Building with
+// -DD3B_STRICT_MMA_ORDER=1 instead waits for PV_X(j)'s commit before issuing
+// QK_X(j+1) (slower: the tensor pipe drains twice per key tile); the parity
+// tests pass in both builds. Either way, s_full_X(j+1) is a tcgen05.commit
+// after PV_X(j), so O_X is complete when the softmax sees S_X(j+1) and may
+// rescale O_X without further synchronisation.
+// ===========================================================================
+constexpr int PP_THREADS = 384;
+#ifndef D3B_STRICT_MMA_ORDER
+#define D3B_STRICT_MMA_ORDER 0
+#endif
+
+template <int D>
+struct CfgPP {
+  static constexpr int BN = 128;
+  static constexpr int CH = D >= 64 ? 64 : D;
+  static constexpr int ROWB = CH * 2;
+  static constexpr int NCH = D / CH;
+  static constexpr uint32_t LAYOUT = ROWB == 128 ? d3b::kLayoutSW128 : d3b::kLayoutSW64;
+  static constexpr int SBO = 8 * ROWB;
+  static constexpr int Q_BYTES = BM * D * 2;
+  static constexpr int SLOT_BYTES = BN * D * 2;
+  static constexpr int Q_CHUNK = BM * ROWB;
+  static constexpr int SLOT_CHUNK = BN * ROWB;
+  static constexpr int NSLOT_RAW = (226 * 1024 - 2 * Q_BYTES - 1024) / SLOT_BYTES;
+  static constexpr int NSLOT = NSLOT_RAW > 8 ? 8 : NSLOT_RAW;
+  static constexpr int SMEM_RAW = 2 * Q_BYTES + NSLOT * SLOT_BYTES + 1024;
+  // at least 120 KB so a single CTA owns the SM and all 512 TMEM columns
+  static constexpr int SMEM_BYTES = SMEM_RAW < 120 * 1024 ? 120 * 1024 : SMEM_RAW;
+  static constexpr int COL_O = 0;      // + X * D
+  static constexpr int COL_S = 2 * D;  // + X * BN; P_X = S_X + BN / 2
+  static_assert(2 * D + 2 * BN <= 512, "TMEM budget");
+  static_assert(NSLOT >= 2, "smem budget");
+};
+
+struct __align__(8) BarsPP {
+  uint64_t q_full;
+  uint64_t slot_full[8];
+  uint64_t slot_empty[8];
+  uint64_t s_full[2];   // per S buffer
+  uint64_t p_full[2][2];  // per Q tile, per half of P (keys 0-63, 64-127)
+  uint64_t pv_done[2];  // per Q tile, one commit per PV
+  uint64_t o_final[2];  // per Q tile, one commit after its last PV
+  uint64_t drain;
+  uint32_t tmem_slot;
+  int abort_flag;
+};
+
+enum { kSitePPQ = 3001, kSitePPSlotEmpty, kSitePPSlotFull, kSitePPPv, kSitePPPFull, kSitePPSFull, kSitePPFinal,
+       kSitePPDrain };
+
+template <int D>
+__device__ __forceinline__ void zero_tile_rows(const Params& p, int b, int g, int tok0, int quarter, int lane) {
+  const int r = quarter * 32 + lane;
+  const int tok = tok0 + r / p.G, h = r % p.G;
+  if (r < p.G * p.T && tok < p.L) {
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + (int64_t)b * p.out_sb +
+                                          (int64_t)(g * p.G + h) * p.out_sh + (int64_t)tok * p.out_sl);
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) dst[i] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+template <int D, int FP16>
+__global__ void __launch_bounds__(PP_THREADS, 1)
+    prefix_bidir_pp_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapKs,
+                           const __grid_constant__ CUtensorMap mapVs, const __grid_constant__ CUtensorMap mapKq,
+                           const __grid_constant__ CUtensorMap mapVq, const Params p) {
+  using C = CfgPP<D>;
+  constexpr int BN = C::BN;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ BarsPP bars;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pair = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int G = p.G, T = p.T;
+  const int rows_used = G * T;
+  const int len_b = p.lengths[b];
+  const int tok_a = 2 * pair * T, tok_b = tok_a + T;
+  const bool act_a = tok_a < len_b, act_b = tok_b < len_b;
+
+  if (!act_a) {  // neither tile has a real token: zero-fill and leave
+    if (warp < 8) zero_tile_rows<D>(p, b, g, tok_a + (warp >> 2) * T, warp & 3, lane);
+    return;
+  }
+  const int ns = act_b ? 2 : 1;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;  // tile X at sQ + X * Q_BYTES
+  uint8_t* sKV = smem + 2 * C::Q_BYTES;
+  volatile int* abort_flag = &bars.abort_flag;
+  const int n_s = (p.S + BN - 1) / BN;
+  const int n = n_s + (len_b + BN - 1) / BN;
+
+  if (threadIdx.x == 0) {
+    d3b::mbar_init(&bars.q_full, 1);
+    for (int i = 0; i < C::NSLOT; ++i) {
+      d3b::mbar_init(&bars.slot_full[i], 1);
+      d3b::mbar_init(&bars.slot_empty[i], 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      d3b::mbar_init(&bars.s_full[x], 1);
+      d3b::mbar_init(&bars.p_full[x][0], 128);
+      d3b::mbar_init(&bars.p_full[x][1], 128);
+      d3b::mbar_init(&bars.pv_done[x], 1);
+      d3b::mbar_init(&bars.o_final[x], 1);
+    }
+    d3b::mbar_init(&bars.drain, 1);
+    bars.abort_flag = 0;
+    d3b::fence_barrier_init();
+  }
+  if (rows_used < BM) {  // rows no TMA box covers are zero for the MMA
+    const int per_chunk = (BM - rows_used) * C::ROWB / 16;
+    for (int i = threadIdx.x; i < 2 * C::NCH * per_chunk; i += PP_THREADS) {
+      const int x = i / (C::NCH * per_chunk), rem = i % (C::NCH * per_chunk);
+      const int c = rem / per_chunk, o = rem % per_chunk;
+      reinterpret_cast<uint4*>(sQ + x * C::Q_BYTES + c * C::Q_CHUNK + rows_used * C::ROWB)[o] =
+          make_uint4(0, 0, 0, 0);
+    }
+    d3b::fence_proxy_async_smem();
+  }
+  if (warp == 9) d3b::tmem_alloc(&bars.tmem_slot, 512);
+  d3b::tc_fence_before();
+  __syncthreads();
+  d3b::tc_fence_after();
+  const uint32_t tmem_base = bars.tmem_slot;
+  if (warp >= 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 104;" ::: "memory");
+   if (warp == 8) {
+    // ================= TMA producer =================
+    if (lane == 0) {
+      d3b::tma_prefetch_desc(&mapQ);
+      d3b::tma_prefetch_desc(&mapKq);
+      d3b::tma_prefetch_desc(&mapVq);
+      if (n_s) {
+        d3b::tma_prefetch_desc(&mapKs);
+        d3b::tma_prefetch_desc(&mapVs);
+      }
+      d3b::mbar_arrive_expect_tx(&bars.q_full, ns * C::NCH * rows_used * C::ROWB);
+      for (int x = 0; x < ns; ++x)
+#pragma unroll
+        for (int c = 0; c < C::NCH; ++c)
+          d3b::tma_load_4d(sQ + x * C::Q_BYTES + c * C::Q_CHUNK, &mapQ, &bars.q_full, c * C::CH, g * G,
+                           tok_a + x * T, b);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int i = 0; i < 2 * n; ++i) {
+        const int is_v = i & 1, j = i >> 1;
+        if (!d3b::mbar_wait(&bars.slot_empty[stage], phase ^ 1, abort_flag, p.err, kSitePPSlotEmpty)) break;
+        d3b::mbar_arrive_expect_tx(&bars.slot_full[stage], C::SLOT_BYTES);
+        uint8_t* dst = sKV + stage * C::SLOT_BYTES;
+        if (j < n_s) {
+          const CUtensorMap* m = is_v ? &mapVs : &mapKs;
+#pragma unroll
+          for (int c = 0; c < C::NCH; ++c)
+            d3b::tma_load_3d(dst + c * C::SLOT_CHUNK, m, &bars.slot_full[stage], c * C::CH, j * BN, g);
+        } else {
+          const CUtensorMap* m = is_v ? &mapVq : &mapKq;
+#pragma unroll
+          for (int c = 0; c < C::NCH; ++c)
+            d3b::tma_load_4d(dst + c * C::SLOT_CHUNK, m, &bars.slot_full[stage], c * C::CH, (j - n_s) * BN, g,
+                             b);
+        }
+        if (++stage == C::NSLOT) { stage = 0; phase ^= 1; }
+      }
+    }
+  } else if (warp == 9) {
+    // ================= MMA issuer =================
+    if (lane == 0) {
+      constexpr uint32_t fmt = FP16 ? 0u : 1u;
+      constexpr uint32_t idesc_qk = d3b::make_idesc(1, fmt, fmt, 0, 0, BM, BN);
+      constexpr uint32_t idesc_pv = d3b::make_idesc(1, fmt, fmt, 0, 1, BM, D);
+      // Base descriptors, built once: an operand's descriptor is the base plus
+      // (byte offset >> 4) in the start-address field (all offsets < 256 KB).
+      const uint64_t dq0 = d3b::make_smem_desc(d3b::smem_u32(sQ), 16, C::SBO, C::LAYOUT);
+      const uint64_t dk0 = d3b::make_smem_desc(d3b::smem_u32(sKV), 16, C::SBO, C::LAYOUT);
+      const uint64_t dv0 = d3b::make_smem_desc(d3b::smem_u32(sKV), C::SLOT_CHUNK, C::SBO, C::LAYOUT);
+      auto slot_of = [&](int item) { return item % C::NSLOT; };
+      auto wait_item = [&](int item) -> bool {
+        return d3b::mbar_wait(&bars.slot_full[slot_of(item)], (uint32_t)(item / C::NSLOT) & 1, abort_flag, p.err,
+                              kSitePPSlotFull);
+      };
+      // S[sb] = Q_x K^T
+      auto qk = [&](int x, int sb, int item) {
+        const uint64_t dq = dq0 + (uint64_t)((x * C::Q_BYTES) >> 4);
+        const uint64_t dk = dk0 + (uint64_t)((slot_of(item) * C::SLOT_BYTES) >> 4);
+        const uint32_t d_tmem = tmem_base + C::COL_S + sb * BN;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const int c = (k * 16) / C::CH, off = ((k * 16) % C::CH) * 2;
+          d3b::mma_f16_ss(d_tmem, dq + (uint64_t)((c * C::Q_CHUNK + off) >> 4),
+                          dk + (uint64_t)((c * C::SLOT_CHUNK + off) >> 4), idesc_qk, k > 0 ? 1u : 0u);
+        }
+        d3b::mma_commit(&bars.s_full[sb]);
+      };
+      // O_x (+)= P[sb] V   (P in the upper half of S[sb]); each half of P is
+      // used as soon as the softmax has published it (use = the phase parity).
+      auto pv = [&](int x, int sb, int item, bool accumulate, uint32_t use) -> bool {
+        const uint64_t dv = dv0 + (uint64_t)((slot_of(item) * C::SLOT_BYTES) >> 4);
+        const uint32_t d_tmem = tmem_base + C::COL_O + x * D;
+        const uint32_t a_tmem = tmem_base + C::COL_S + sb * BN + BN / 2;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (!d3b::mbar_wait(&bars.p_full[x][h], use & 1, abort_flag, p.err, kSitePPPFull)) return false;
+          d3b::tc_fence_after();
+#pragma unroll
+          for (int k = h * BN / 32; k < (h + 1) * BN / 32; ++k)
+            d3b::mma_f16_ts(d_tmem, a_tmem + k * 8, dv + (uint64_t)((k * 16 * C::ROWB) >> 4), idesc_pv,
+                            (accumulate || k > 0) ? 1u : 0u);
+        }
+        d3b::mma_commit(&bars.pv_done[x]);
+        return true;
+      };
+      bool ok = d3b::mbar_wait(&bars.q_full, 0, abort_flag, p.err, kSitePPQ);
+      if (ns == 2) {
+        for (int j = 0; j < n && ok; ++j) {
+          const int it_k = 2 * j, it_v = 2 * j + 1;
+          const uint32_t prev = (uint32_t)((j - 1) & 1);
+          // QK_A(j) (in issue order after PV_A(j-1), which read P_A from S_A)
+          if (!(ok = wait_item(it_k))) break;
+          if (D3B_STRICT_MMA_ORDER && j > 0 &&
+              !(ok = d3b::mbar_wait(&bars.pv_done[0], prev, abort_flag, p.err, kSitePPPv)))
+            break;
+          d3b::tc_fence_after();
+          qk(0, 0, it_k);
+          if (j > 0) {  // PV_B(j-1)
+            if (!(ok = pv(1, 1, it_v - 2, j - 1 > 0, prev))) break;
+            d3b::mma_commit(&bars.slot_empty[slot_of(it_v - 2)]);  // V_{j-1} done
+          }
+          // QK_B(j)
+          if (D3B_STRICT_MMA_ORDER && j > 0 &&
+              !(ok = d3b::mbar_wait(&bars.pv_done[1], prev, abort_flag, p.err, kSitePPPv)))
+            break;
+          d3b::tc_fence_after();
+          qk(1, 1, it_k);
+          d3b::mma_commit(&bars.slot_empty[slot_of(it_k)]);  // K_j done
+          // PV_A(j)
+          if (!(ok = wait_item(it_v))) break;
+          if (!(ok = pv(0, 0, it_v, j > 0, (uint32_t)j))) break;
+        }
+        if (ok) {
+          d3b::mma_commit(&bars.o_final[0]);
+          if (pv(1, 1, 2 * n - 1, n - 1 > 0, (uint32_t)(n - 1))) d3b::mma_commit(&bars.o_final[1]);
+          d3b::mma_commit(&bars.slot_empty[slot_of(2 * n - 1)]);
+        }
+      } else {
+        // one Q tile, S double-buffered in S_A / S_B
+        if (ok && (ok = wait_item(0))) {
+          d3b::tc_fence_after();
+          qk(0, 0, 0);
+          d3b::mma_commit(&bars.slot_empty[slot_of(0)]);
+        }
+        for (int j = 0; j < n && ok; ++j) {
+          if (j + 1 < n) {  // QK(j+1) into S[(j+1)%2] (after PV(j-1), which read that buffer's P)
+            const int it_k = 2 * (j + 1);
+            if (!(ok = wait_item(it_k))) break;
+            d3b::tc_fence_after();
+            qk(0, (j + 1) & 1, it_k);
+            d3b::mma_commit(&bars.slot_empty[slot_of(it_k)]);
+          }
+          const int it_v = 2 * j + 1;
+          if (!(ok = wait_item(it_v))) break;
+          if (!(ok = pv(0, j & 1, it_v, j > 0, (uint32_t)j))) break;
+          d3b::mma_commit(&bars.slot_empty[slot_of(it_v)]);
+        }
+        if (ok) d3b::mma_commit(&bars.o_final[0]);
+      }
+      d3b::mma_commit(&bars.drain);
+      const uint32_t addr = d3b::smem_u32(&bars.drain);
+      const uint64_t t0 = d3b::globaltimer_ns();
+      while (!d3b::mbar_try_wait(addr, 0)) {
+        if (d3b::globaltimer_ns() - t0 > D3B_WAIT_LIMIT_NS) {
+          d3b::record_device_error(p.err, kSitePPDrain);
+          break;
+        }
+      }
+    }
+   }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 200;" ::: "memory");
+    // ================= softmax + epilogue (warps 0-7) =================
+    const int x = warp >> 2;  // Q tile of this warpgroup
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    if (x >= ns) {
+      zero_tile_rows<D>(p, b, g, tok_b, quarter, lane);
+    } else {
+      const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
+      const uint32_t col_o = C::COL_O + x * D;
+      const float sl2 = p.scale_log2;
+      float m_ref = -INFINITY, l_sum = 0.f;
+      bool ok = true;
+      for (int j = 0; j < n; ++j) {
+        // S buffer and its use count: own buffer with two tiles, alternating with one
+        const int sb = ns == 2 ? x : (j & 1);
+        const uint32_t s_use = ns == 2 ? (uint32_t)j : (uint32_t)(j >> 1);
+        const uint32_t col_s = C::COL_S + sb * BN, col_p = col_s + BN / 2;
+        if (!d3b::warp_wait(&bars.s_full[sb], s_use & 1, abort_flag, p.err, kSitePPSFull)) { ok = false; break; }
+        d3b::tc_fence_after();
+        const int valid = j < n_s ? p.S - j * BN : len_b - (j - n_s) * BN;
+        float s[BN];
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c)
+          d3b::tmem_ld32(lane_addr + col_s + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
+        d3b::tmem_wait_ld();
+        if (valid < BN) {
+#pragma unroll
+          for (int c = 0; c < BN; ++c)
+            if (c >= valid) s[c] = -INFINITY;
+        }
+        const float m_tile = max_n<BN>(s) * sl2;
+        const bool rescale = __any_sync(0xffffffffu, m_tile > m_ref + kRescaleThreshold);
+        const float m_new = rescale ? fmaxf(m_ref, m_tile) : m_ref;
+        const float alpha = rescale ? d3b::ex2_approx(m_ref - m_new) : 1.f;
+        // P (BN/2 columns, into the upper half of S whose values are in registers),
+        // published in two halves. A rescale of O must land before the first.
+        if (rescale && j > 0) {
+          // O_x must hold PV(j-1). With two tiles that is already implied by
+          // s_full (QK_x(j) was committed after PV_x(j-1)); with one tile, QK(j)
+          // was issued before PV(j-1), so wait for PV(j-1)'s commit (the barrier
+          // is at most one phase ahead here, so the parity wait is exact).
+          if (!d3b::warp_wait(&bars.pv_done[x], (uint32_t)((j - 1) & 1), abort_flag, p.err, kSitePPPv)) {
+            ok = false;
+            break;
+          }
+          d3b::tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            d3b::tmem_ld32(lane_addr + col_o + c * 32, o);
+            d3b::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            d3b::tmem_st32(lane_addr + col_o + c * 32, o);
+          }
+        }
+        float rowsum = 0.f;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t pk[BN / 4];
+          rowsum += exp_row<BN / 2, FP16>(s + h * (BN / 2), sl2, m_new, pk);
+          d3b::tmem_st32(lane_addr + col_p + h * 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
+          d3b::tmem_wait_st();
+          d3b::tc_fence_before();
+          d3b::mbar_arrive(&bars.p_full[x][h]);
+        }
+        l_sum = l_sum * alpha + rowsum;
+        m_ref = m_new;
+      }
+      if (ok) ok = d3b::warp_wait(&bars.o_final[x], 0, abort_flag, p.err, kSitePPFinal);
+      if (ok) {
+        d3b::tc_fence_after();
+        const int tok = tok_a + x * T + r / G, h = r % G;
+        const bool in_tensor = r < rows_used && tok < p.L;
+        const bool real = tok < len_b;
+        const float inv_l = 1.f / l_sum;
+        uint16_t* dst_row = static_cast<uint16_t*>(p.out) + (int64_t)b * p.out_sb +
+                            (int64_t)(g * G + h) * p.out_sh + (int64_t)tok * p.out_sl;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          d3b::tmem_ld32(lane_addr + col_o + c * 32, o);
+          d3b::tmem_wait_ld();
+          if (in_tensor) {
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              w[i] = real ? pack2<FP16>(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l)
+                          : 0u;
+            uint4* dst = reinterpret_cast<uint4*>(dst_row + c * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          }
+        }
+      }
+    }
+  }
+
+  d3b::tc_fence_before();
+  __syncthreads();
+  d3b::tc_fence_after();
+  if (warp == 9) d3b::tmem_dealloc(tmem_base, 512);
+}
+
+template <int D, int FP16>
+int launch_pp(const CUtensorMap* maps, const Params& prm, int tiles, int Hkv, int B, cudaStream_t stream) {
+  using C = CfgPP<D>;
+  static int attr_set[64] = {0};
+  const int dev = d3b_host::current_device();
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(prefix_bidir_pp_kernel<D, FP16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::SMEM_BYTES) != cudaSuccess)
+      return D3B_ECUDA;
+    attr_set[dev] = 1;
+  }
+  dim3 grid((tiles + 1) / 2, Hkv, B);
+  prefix_bidir_pp_kernel<D, FP16><<<grid, PP_THREADS, C::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3],
+                                                                              maps[4], prm);
+  return d3b_host::check_launch();
+}
+
 template <int D, int BN, int FP16>
 int launch(const CUtensorMap* maps, const Params& prm, dim3 grid, cudaStream_t stream) {
   using C = Cfg<D, BN>;
@@ -410,10 +909,11 @@ int launch(const CUtensorMap* maps, const Params& prm, dim3 grid, cudaStream_t s
 
 template <int FP16>
 int dispatch(int D, const CUtensorMap* maps, const Params& prm, dim3 grid, cudaStream_t s) {
+  // D <= 128: two Q tiles per CTA; D = 256 (O needs 256 TMEM columns): one.
   switch (D) {
-    case 32: return launch<32, 128, FP16>(maps, prm, grid, s);
-    case 64: return launch<64, 128, FP16>(maps, prm, grid, s);
-    case 128: return launch<128, 128, FP16>(maps, prm, grid, s);
+    case 32: return launch_pp<32, FP16>(maps, prm, grid.x, grid.y, grid.z, s);
+    case 64: return launch_pp<64, FP16>(maps, prm, grid.x, grid.y, grid.z, s);
+    case 128: return launch_pp<128, FP16>(maps, prm, grid.x, grid.y, grid.z, s);
     case 256: return launch<256, 64, FP16>(maps, prm, grid, s);
     default: return D3B_EUNSUPPORTED;
   }

@@ -7,7 +7,8 @@
 // stages K-chunks of its 8 hidden rows in shared memory (as fp32); each warp
 // computes 4 options x 8 rows of dot products with fp32 FMAs (the reference
 // computes in fp32, so no tensor-core rounding is introduced), streaming R
-// with 16-byte loads, 16 of them in flight per lane. Logits go to the
+// with 16-byte loads, 16 of them in flight per lane; the hidden chunk is staged
+// with 16-byte loads that are all issued before the first store. Logits go to the
 // workspace. The last CTA of a row group to finish (an atomic ticket per row
 // group) runs the masked softmax with one warp per row and resets the ticket,
 // so the workspace is ready for the next call.
@@ -27,6 +28,31 @@ constexpr int kUnroll = 4;      // float4 steps per lane kept in flight, per opt
 constexpr int kMaxOpts = 1024;  // softmax keeps n_opt/32 logits per lane
 constexpr int kMaxGroups = 4096;
 constexpr size_t kTicketBytes = kMaxGroups * sizeof(unsigned int);
+
+// 16 bytes of hidden as fp32 (8 bf16/f16 or 4 f32 values)
+__device__ __forceinline__ int unpack16(uint4 a, const float*, float (&v)[8]) {
+  v[0] = __uint_as_float(a.x); v[1] = __uint_as_float(a.y); v[2] = __uint_as_float(a.z); v[3] = __uint_as_float(a.w);
+  return 4;
+}
+__device__ __forceinline__ int unpack16(uint4 a, const __nv_bfloat16*, float (&v)[8]) {
+  const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+  return 8;
+}
+__device__ __forceinline__ int unpack16(uint4 a, const __half*, float (&v)[8]) {
+  const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+  return 8;
+}
 
 __device__ __forceinline__ float load_h(const float* p) { return __ldg(p); }
 __device__ __forceinline__ float load_h(const __nv_bfloat16* p) { return __bfloat162float(*p); }
@@ -57,10 +83,34 @@ __global__ void __launch_bounds__(kRows * 32) readout_kernel(const T* __restrict
   for (int kc = 0; kc < K; kc += kChunk) {
     const int kn = min(kChunk, K - kc);
     __syncthreads();
-    for (int i = threadIdx.x; i < kRows * kChunk; i += blockDim.x) {
-      const int r = i / kChunk, k = i % kChunk;
-      const int row = r0 + r;
-      hs[r][k] = (row < B && k < kn) ? load_h(hidden + (int64_t)row * K + kc + k) : 0.f;
+    if (VEC) {
+      // 16-byte loads, all issued before any store: kRows * kChunk / (per * 256) per thread
+      constexpr int per = 16 / sizeof(T);
+      constexpr int kLoads = kRows * kChunk / per / (kRows * 32);
+      uint4 raw[kLoads];
+#pragma unroll
+      for (int i = 0; i < kLoads; ++i) {
+        const int e = (threadIdx.x + i * kRows * 32) * per;  // element index in the [kRows][kChunk] tile
+        const int r = e / kChunk, k = e % kChunk;
+        const int row = r0 + r;
+        raw[i] = (row < B && k < kn) ? __ldg(reinterpret_cast<const uint4*>(hidden + (int64_t)row * K + kc + k))
+                                     : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int i = 0; i < kLoads; ++i) {
+        const int e = (threadIdx.x + i * kRows * 32) * per;
+        const int r = e / kChunk, k = e % kChunk;
+        float v[8];
+        unpack16(raw[i], static_cast<const T*>(nullptr), v);
+        *reinterpret_cast<float4*>(&hs[r][k]) = make_float4(v[0], v[1], v[2], v[3]);
+        if (per == 8) *reinterpret_cast<float4*>(&hs[r][k + 4]) = make_float4(v[4], v[5], v[6], v[7]);
+      }
+    } else {
+      for (int i = threadIdx.x; i < kRows * kChunk; i += blockDim.x) {
+        const int r = i / kChunk, k = i % kChunk;
+        const int row = r0 + r;
+        hs[r][k] = (row < B && k < kn) ? load_h(hidden + (int64_t)row * K + kc + k) : 0.f;
+      }
     }
     __syncthreads();
     if (VEC) {
@@ -171,7 +221,9 @@ template <typename T>
 void launch_typed(const void* hidden, const float* readout, const int32_t* counts, float temperature, float* probs,
                   int B, int K, int n_opt, float* logits, unsigned int* tickets, cudaStream_t s) {
   dim3 grid((B + kRows - 1) / kRows, (n_opt + kOpts - 1) / kOpts), block(kRows * 32);
-  const bool vec = (K % 4 == 0) && (reinterpret_cast<uintptr_t>(readout) % 16 == 0);
+  // vector path: 16-byte aligned rows of hidden and readout (K * sizeof(T) and K * 4 multiples of 16)
+  const bool vec = (K % 8 == 0) && (reinterpret_cast<uintptr_t>(readout) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(hidden) % 16 == 0);
   if (vec)
     readout_kernel<T, true><<<grid, block, 0, s>>>(static_cast<const T*>(hidden), readout, counts, temperature,
                                                    probs, B, K, n_opt, logits, tickets);
