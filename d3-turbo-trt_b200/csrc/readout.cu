@@ -16,6 +16,8 @@
 // Workspace layout: [tickets: kMaxGroups x u32 at offset 0][logits: B x n_opt f32].
 // The ticket region never moves, so one zero-filled workspace serves calls of
 // any shape (B <= 8 * kMaxGroups).
+#include <mutex>
+
 #include "common.cuh"
 
 namespace {
@@ -259,6 +261,85 @@ extern "C" int d3b_readout(const void* hidden, int h_dtype, const float* readout
       launch_typed<__nv_bfloat16>(hidden, readout, counts, temperature, probs, B, K, n_opt, logits, tickets, s);
       break;
     default: return D3B_EUNSUPPORTED;
+  }
+  return d3b_host::check_launch();
+}
+
+// ===========================================================================
+// Readout without any allocation.
+//
+// Some callers cannot allocate device memory at call time: code that runs
+// while a CUDA graph is being captured, host runtimes that hand the library
+// only input and output buffers, or processes whose allocator is owned by
+// someone else. For them this entry point keeps the readout's scratch (the
+// ticket counters and the logits) in one fixed array that lives in the
+// library itself. Every GPU that loads the library holds these bytes until
+// the process exits.
+//
+// Limits: B * n_opt * 4 bytes of logits plus the ticket region must fit in
+// kNoAllocScratchBytes (1 MiB), i.e. up to 258048 logits (B = 255 questions
+// at 255 options needs 65025); larger requests return D3B_ENOSPACE before any
+// work is enqueued.
+//
+// All calls on a device share the array and it keeps the last call's
+// contents. Each call clears the ticket counters it uses on its own stream
+// before the kernel runs; the logits need no clearing (every logit is written
+// before it is read). Two calls whose work overlaps on the GPU (different
+// streams, no ordering between them) race on the array and give wrong results.
+//
+// Set-up: the first call on a device looks up the array's device address
+// (cudaGetSymbolAddress) with that device current and caches it. Make that
+// first call before any stream capture begins.
+// ===========================================================================
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 1u << 20;
+static __device__ __align__(256) unsigned char g_readout_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {nullptr};
+
+// Device address of g_readout_scratch on the current device (the symbol's
+// name in host code is only a stand-in, never a device address).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return D3B_ECUDA;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_readout_scratch) != cudaSuccess || !p) return D3B_ECUDA;
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return D3B_OK;
+}
+
+}  // namespace
+
+extern "C" int d3b_readout_noalloc(const void* hidden, int h_dtype, const float* readout, const int32_t* counts,
+                                   float temperature, float* probs, int B, int K, int n_opt, d3b_stream_t stream) {
+  if (B < 0 || K <= 0 || n_opt <= 0 || n_opt > kMaxOpts) return D3B_EINVAL;
+  if (B > kRows * kMaxGroups) return D3B_EINVAL;
+  if (!(temperature > 0.f)) return D3B_EINVAL;
+  if (B == 0) return D3B_OK;
+  if (!hidden || !readout || !counts || !probs) return D3B_EINVAL;
+  if (h_dtype != D3B_F32 && h_dtype != D3B_F16 && h_dtype != D3B_BF16) return D3B_EUNSUPPORTED;
+  if (d3b_readout_workspace_size(B, n_opt) > kNoAllocScratchBytes) return D3B_ENOSPACE;
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != D3B_OK) return rc;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // the ticket counters must start at zero: clear the ones this launch uses
+  const size_t groups = (size_t)(B + kRows - 1) / kRows;
+  if (cudaMemsetAsync(scratch, 0, groups * sizeof(unsigned int), s) != cudaSuccess) return D3B_ECUDA;
+  unsigned int* tickets = static_cast<unsigned int*>(scratch);
+  float* logits = reinterpret_cast<float*>(static_cast<char*>(scratch) + kTicketBytes);
+  switch (h_dtype) {
+    case D3B_F32: launch_typed<float>(hidden, readout, counts, temperature, probs, B, K, n_opt, logits, tickets, s); break;
+    case D3B_F16: launch_typed<__half>(hidden, readout, counts, temperature, probs, B, K, n_opt, logits, tickets, s); break;
+    default:
+      launch_typed<__nv_bfloat16>(hidden, readout, counts, temperature, probs, B, K, n_opt, logits, tickets, s);
+      break;
   }
   return d3b_host::check_launch();
 }

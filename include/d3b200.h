@@ -128,6 +128,24 @@ D3B_API int d3b_readout(const void* hidden, int h_dtype, const float* readout, c
                 d3b_stream_t stream);
 
 /*
+ * The readout above for callers that cannot allocate device memory when they
+ * call (for example code that runs during CUDA graph capture, or a host
+ * runtime that only hands over its input and output buffers). It has no
+ * counterpart in the reference. Same arguments and results as d3b_readout,
+ * without the workspace: the scratch is one fixed 1 MiB array inside the
+ * library, held by every GPU that loads it until the process exits.
+ *   Limit: d3b_readout_workspace_size(B, n_opt) <= 1 MiB (B * n_opt up to
+ *   258048 logits), otherwise D3B_ENOSPACE and nothing is enqueued.
+ *   Calls on one device share the array: calls whose work overlaps on the
+ *   GPU (unordered streams) race and give wrong results.
+ *   The first call on a device looks up the array's device address; make it
+ *   before any stream capture begins.
+ * Calls no allocating routine (no cudaMalloc / cudaFree).
+ */
+D3B_API int d3b_readout_noalloc(const void* hidden, int h_dtype, const float* readout, const int32_t* counts,
+                                float temperature, float* probs, int B, int K, int n_opt, d3b_stream_t stream);
+
+/*
  * Self-test of the device wait limit: launches one CTA that waits on an
  * mbarrier nothing arrives on, with a limit of `limit_ms` milliseconds; the
  * kernel gives up, records its site code and returns. After synchronising,
