@@ -75,53 +75,78 @@ def profile_traffic(name: str) -> float | None:
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during a region."""
+    """SM clock and throttle reasons sampled every 2 ms (NVML) during a region.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    Falls back to `nvidia-smi -lms 200` when NVML is unavailable.
+    """
+
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
+        self.samples: list[tuple[float, float, int]] = []  # (sm_mhz, max_mhz, reasons bitmask)
+        self._stop = None
+        self._thread = None
+        self._proc = None
 
     def __enter__(self):
+        import threading
+
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            mx = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            self._stop = threading.Event()
+
+            def run():
+                while not self._stop.is_set():
+                    try:
+                        sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                        rs = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
+                        self.samples.append((sm, mx, rs))
+                    except Exception:  # noqa: BLE001
+                        pass
+                    time.sleep(0.002)
+
+            self._thread = threading.Thread(target=run, daemon=True)
+            self._thread.start()
+        except Exception:  # noqa: BLE001 - no NVML: nvidia-smi at its minimum period
+            try:
+                self._proc = subprocess.Popen(
+                    ["nvidia-smi", "-i", str(self.index), "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active",
+                     "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                    text=True)
+            except OSError:
+                self._proc = None
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+        if self._proc is not None:
+            self._proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                out, _ = self._proc.communicate(timeout=5)
             except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+                self._proc.kill()
+                out, _ = self._proc.communicate()
+            for line in out.splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                try:
+                    self.samples.append((float(parts[0]), float(parts[1]), int(parts[2], 16)))
+                except (ValueError, IndexError):
+                    continue
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in getattr(self, "lines", []):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = max(mx, float(parts[2]))
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        reasons = sorted(name for name, bit in self.REASONS.items() if any(r & bit for _, _, r in self.samples))
+        return {"sm_mhz": statistics.median(s for s, _, _ in self.samples),
+                "sm_max_mhz": max(m for _, m, _ in self.samples), "reasons": reasons,
+                "samples": len(self.samples), "source": "nvml" if self._thread is not None else "nvidia-smi"}
 
 
 def make_question_inputs(cfg, seed, device, with_state=True):
@@ -230,7 +255,7 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extra", action="store_true", help="skip the secondary workloads")
@@ -335,7 +360,7 @@ def main():
 
     if rank == 0:
         cpu = None if args.no_cpu else cpu_baseline_questions(cfg)
-        traffic = profile_traffic("prefix_bidir_cfg3a.md")
+        traffic = profile_traffic("prefix_bidir_cfg3a.md")  # per launch, from the committed ncu summary
         peak = peaks["bf16_tflops"]
         line = {
             "metric": METRIC, "value": value, "unit": "question-blocks/s", "n_gpus": world, "steps": args.steps,
