@@ -295,11 +295,13 @@ def main():
         vs.copy_(state["vs"].permute(1, 0, 2))
     bcast_ms = None
     if world > 1:
+        d3dist.broadcast_state_kv([(ks, vs)], src=0)  # first call also sets up the NCCL communicator
+        torch.cuda.synchronize()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         dist.barrier()
         t0.record(stream)
-        d3dist.broadcast_state_kv([(ks, vs)], src=0)
+        d3dist.broadcast_state_kv([(ks, vs)], src=0)  # timed: the per-request exchange (8 MiB K+V)
         t1.record(stream)
         torch.cuda.synchronize()
         bcast_ms = t0.elapsed_time(t1)
@@ -359,7 +361,8 @@ def main():
         dist.barrier()
 
     if rank == 0:
-        cpu = None if args.no_cpu else cpu_baseline_questions(cfg)
+        # the CPU baseline is a single-process figure: measured at N = 1 only
+        cpu = None if (args.no_cpu or world > 1) else cpu_baseline_questions(cfg)
         traffic = profile_traffic("prefix_bidir_cfg3a.md")  # per launch, from the committed ncu summary
         peak = peaks["bf16_tflops"]
         line = {
@@ -373,7 +376,7 @@ def main():
                        "l2": "flushed before every timed step (256 MiB write)"},
             "roofline": {"bound": "tensor", "achieved": achieved_tflops, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved_tflops / peak, "traffic": traffic,
-                         "kernel": "prefix_bidir_kernel<128,128,bf16>",
+                         "kernel": "prefix_bidir_2c_kernel<128,bf16>",
                          "algorithmic_flops_per_launch": flops,
                          "peak_source": f"{peaks['source']} bf16 dense (burst)"},
             "e2e": {"value": cfg["B"] * world / (e2e_ms / 1e3), "unit": "question-blocks/s",

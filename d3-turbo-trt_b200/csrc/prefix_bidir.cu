@@ -20,16 +20,24 @@
 // then ceil(len_b/BN) own-block tiles; only the last state tile and the own
 // tiles carry a key mask. Nothing outside [state | own block] is touched.
 //
-// Roles (6 warps):
+// Two kernels share this work unit, the key schedule and the softmax:
+//   D <= 128  prefix_bidir_2c_kernel: one Q tile per CTA, two CTAs per SM
+//             (the tensor core alternates between the two CTAs' chains).
+//   D == 256  prefix_bidir_kernel: one Q tile per CTA, one CTA per SM, S
+//             double-buffered in TMEM (O alone takes 256 columns).
+// Both use one thread per Q row for the softmax: tcgen05.ld of the S row,
+// online softmax in the log2 domain, P as bf16/f16 written back to TMEM for
+// the TS-form PV MMA (V read MN-major from shared memory), O rescaled in TMEM
+// only when the running max grows by more than 2^8 (otherwise the stale max
+// is kept), final O / l in the epilogue.
+//
+// D == 256 kernel roles (6 warps):
 //   warp 0      TMA producer: Q once, then K/V tiles into a ring of slots in
 //               the order the MMA issuer consumes them (K0, K1, V0, K2, V1, ..)
 //   warp 1      TMEM owner + tcgen05.mma issuer (one thread)
 //                 S[j%2] = Q K_j^T              (SS form, both K-major, fp32)
 //                 O     += P[j%2] V_j            (TS form: P from TMEM, V MN-major)
-//   warps 2..5  softmax + epilogue, one thread per row: tcgen05.ld the S row,
-//               online softmax in the log2 domain, P as bf16/f16 written back
-//               to TMEM, O rescaled in TMEM only when the running max grows by
-//               more than 2^8 (otherwise the stale max is kept), final O / l.
+//   warps 2..5  softmax + epilogue
 // TMEM (512 columns): O [0,D) | S0 | S1 (BN each) | P0 | P1 (BN/2 each).
 #include "common.cuh"
 
@@ -468,44 +476,41 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 }
 
 // ===========================================================================
-// Two Q tiles per CTA (D <= 128): ping-pong between two softmax warpgroups.
+// One Q tile per CTA, two CTAs per SM (D <= 128).
 //
-//   warps 0-3  softmax + epilogue of Q tile A     warps 4-7  same for tile B
-//   warp 8     TMA producer (K_0, V_0, K_1, V_1, ... into a slot ring)
-//   warp 9     TMEM owner + tcgen05.mma issuer   (warps 10-11 idle)
-// Registers: launched at 168 per thread (384 threads = 64512); the producer/MMA
-// warpgroup drops to 104 and the softmax warpgroups rise to 200 (setmaxnreg:
-// 128 * 104 + 256 * 200 = 64512, the launch budget), so a softmax thread holds
-// a whole S row without spilling.
-// TMEM (512 columns): O_A | O_B (D each) | S_A | S_B (128 each). P_X (bf16/f16,
-// 64 columns) is written into the upper half of S_X once S_X has been read.
-// P is published in two halves (keys 0-63, then 64-127, separate barriers):
-// the first four PV MMAs start while the softmax still exponentiates the
-// second half.
-// MMA order per key tile j:  QK_A(j)  PV_B(j-1)  QK_B(j)  PV_A(j)
-// so while the tensor core works on one tile, the other tile's softmax runs.
-// A CTA whose second tile has no real token (e.g. the third tile of a 48-token
-// block) runs tile A alone with S double-buffered in S_A / S_B instead:
-// QK(j+1) then overlaps the softmax of S(j), PV(j) reads P from S[j % 2].
-// QK_X(j+1) overwrites S_X, whose upper half still holds P_X(j) for PV_X(j).
-// Both are issued by the same thread in that order, and tcgen05.mma
-// operations of one issuing thread execute in issue order on the SM's tensor
-// core, so QK_X(j+1) cannot write S_X before PV_X(j) has read P_X(j). This is
-// an observed property of the hardware, not one of the PTX ISA's guaranteed
-// "pipelined" pairs (those cover MMAs on the same accumulator). Building with
-// -DD3B_STRICT_MMA_ORDER=1 instead waits for PV_X(j)'s commit before issuing
-// QK_X(j+1) (slower: the tensor pipe drains twice per key tile); the parity
-// tests pass in both builds. Either way, s_full_X(j+1) is a tcgen05.commit
-// after PV_X(j), so O_X is complete when the softmax sees S_X(j+1) and may
-// rescale O_X without further synchronisation.
+// 256 TMEM columns per CTA: O (D) | S (128 keys); P (bf16/f16) goes into the
+// upper half of S once S has been read. Two co-resident CTAs share the SM's
+// tensor core, so while one CTA's softmax runs, the other's QK^T / PV execute;
+// each CTA's chain QK(j) -> softmax(j) -> PV(j) -> QK(j+1) needs no
+// cross-CTA ordering. Shared memory stays under half an SM (Q + two 32 KB K/V
+// slots at D = 128).
+// Warps 0-3 softmax + epilogue, warp 4 TMA producer, warp 5 TMEM + MMA. At
+// 128 registers per thread a softmax thread holds 64 scores at a time: it
+// reduces keys 0-63, then 64-127, turns the second half into P, reloads the
+// first half and turns it into P. P is published in those two halves
+// (separate barriers), so the first four PV MMAs run while the softmax still
+// exponentiates keys 0-63. (An 8-warp variant that lends the softmax 200
+// registers through setmaxnreg, to keep all 128 scores in registers,
+// measured slower.)
+// QK(j+1) overwrites S, whose upper half still holds P(j) for PV(j). Both are
+// issued by the same thread in that order, and tcgen05.mma operations of one
+// issuing thread execute in issue order on the SM's tensor core, so QK(j+1)
+// cannot write S before PV(j) has read P(j). This is an observed property of
+// the hardware, not one of the PTX ISA's guaranteed "pipelined" pairs (those
+// cover MMAs on the same accumulator). Building with -DD3B_STRICT_MMA_ORDER=1
+// instead waits for PV(j)'s commit before issuing QK(j+1) (slower: the tensor
+// pipe drains once per key tile); the parity tests pass in both builds.
+// Either way, s_full(j+1) is a tcgen05.commit after PV(j), so O is complete
+// when the softmax sees S(j+1) and may rescale O without further
+// synchronisation.
 // ===========================================================================
-constexpr int PP_THREADS = 384;
 #ifndef D3B_STRICT_MMA_ORDER
 #define D3B_STRICT_MMA_ORDER 0
 #endif
+constexpr int C2_THREADS = 192;
 
 template <int D>
-struct CfgPP {
+struct Cfg2C {
   static constexpr int BN = 128;
   static constexpr int CH = D >= 64 ? 64 : D;
   static constexpr int ROWB = CH * 2;
@@ -516,33 +521,37 @@ struct CfgPP {
   static constexpr int SLOT_BYTES = BN * D * 2;
   static constexpr int Q_CHUNK = BM * ROWB;
   static constexpr int SLOT_CHUNK = BN * ROWB;
-  static constexpr int NSLOT_RAW = (226 * 1024 - 2 * Q_BYTES - 1024) / SLOT_BYTES;
+  static constexpr int NSLOT_RAW = (110 * 1024 - Q_BYTES - 1024) / SLOT_BYTES;
   static constexpr int NSLOT = NSLOT_RAW > 8 ? 8 : NSLOT_RAW;
-  static constexpr int SMEM_RAW = 2 * Q_BYTES + NSLOT * SLOT_BYTES + 1024;
-  // at least 120 KB so a single CTA owns the SM and all 512 TMEM columns
-  static constexpr int SMEM_BYTES = SMEM_RAW < 120 * 1024 ? 120 * 1024 : SMEM_RAW;
-  static constexpr int COL_O = 0;      // + X * D
-  static constexpr int COL_S = 2 * D;  // + X * BN; P_X = S_X + BN / 2
-  static_assert(2 * D + 2 * BN <= 512, "TMEM budget");
+  static constexpr int SMEM_BYTES = Q_BYTES + NSLOT * SLOT_BYTES + 1024;
+  static constexpr int COL_O = 0;
+  static constexpr int COL_S = D;
+  static constexpr uint32_t TMEM_COLS = 256;
+  static_assert(D + BN <= 256, "TMEM budget");
   static_assert(NSLOT >= 2, "smem budget");
+  static_assert(SMEM_BYTES <= 113 * 1024, "two CTAs per SM");
 };
 
-struct __align__(8) BarsPP {
+struct __align__(8) Bars2C {
   uint64_t q_full;
   uint64_t slot_full[8];
   uint64_t slot_empty[8];
-  uint64_t s_full[2];   // per S buffer
-  uint64_t p_full[2][2];  // per Q tile, per half of P (keys 0-63, 64-127)
-  uint64_t pv_done[2];  // per Q tile, one commit per PV
-  uint64_t o_final[2];  // per Q tile, one commit after its last PV
+  uint64_t s_full;
+  uint64_t p_full[2];  // halves of P: [0] keys 0-63, [1] keys 64-127
+  uint64_t o_final;
+  uint64_t pv_done;  // only with D3B_STRICT_MMA_ORDER
   uint64_t drain;
   uint32_t tmem_slot;
   int abort_flag;
 };
 
-enum { kSitePPQ = 3001, kSitePPSlotEmpty, kSitePPSlotFull, kSitePPPv, kSitePPPFull, kSitePPSFull, kSitePPFinal,
-       kSitePPDrain };
+enum {
+  kSite2CQ = 5001, kSite2CSlotEmpty, kSite2CSlotFull, kSite2CPFull, kSite2CSFull, kSite2CFinal, kSite2CDrain,
+  kSite2CPvDone
+};
 
+// Zero the output rows of a Q tile that holds no real token (rows past the
+// tensor's L are skipped).
 template <int D>
 __device__ __forceinline__ void zero_tile_rows(const Params& p, int b, int g, int tok0, int quarter, int lane) {
   const int r = quarter * 32 + lane;
@@ -555,31 +564,40 @@ __device__ __forceinline__ void zero_tile_rows(const Params& p, int b, int g, in
   }
 }
 
+// 64 columns of this thread's TMEM row into registers, keys >= valid masked.
+__device__ __forceinline__ void load64(uint32_t addr, int key0, int valid, float (&s)[64]) {
+  d3b::tmem_ld32(addr, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+  d3b::tmem_ld32(addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+  d3b::tmem_wait_ld();
+  if (valid - key0 < 64) {
+#pragma unroll
+    for (int c = 0; c < 64; ++c)
+      if (key0 + c >= valid) s[c] = -INFINITY;
+  }
+}
+
 template <int D, int FP16>
-__global__ void __launch_bounds__(PP_THREADS, 1)
-    prefix_bidir_pp_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapKs,
+__global__ void __launch_bounds__(C2_THREADS, 2)
+    prefix_bidir_2c_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapKs,
                            const __grid_constant__ CUtensorMap mapVs, const __grid_constant__ CUtensorMap mapKq,
                            const __grid_constant__ CUtensorMap mapVq, const Params p) {
-  using C = CfgPP<D>;
+  using C = Cfg2C<D>;
   constexpr int BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ BarsPP bars;
+  __shared__ Bars2C bars;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int pair = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int tile = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int G = p.G, T = p.T;
   const int rows_used = G * T;
   const int len_b = p.lengths[b];
-  const int tok_a = 2 * pair * T, tok_b = tok_a + T;
-  const bool act_a = tok_a < len_b, act_b = tok_b < len_b;
-
-  if (!act_a) {  // neither tile has a real token: zero-fill and leave
-    if (warp < 8) zero_tile_rows<D>(p, b, g, tok_a + (warp >> 2) * T, warp & 3, lane);
+  const int tok0 = tile * T;
+  if (tok0 >= len_b) {  // no real token in this tile: zero-fill and leave
+    if (warp < 4) zero_tile_rows<D>(p, b, g, tok0, warp, lane);
     return;
   }
-  const int ns = act_b ? 2 : 1;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;  // tile X at sQ + X * Q_BYTES
-  uint8_t* sKV = smem + 2 * C::Q_BYTES;
+  uint8_t* sQ = smem;
+  uint8_t* sKV = smem + C::Q_BYTES;
   volatile int* abort_flag = &bars.abort_flag;
   const int n_s = (p.S + BN - 1) / BN;
   const int n = n_s + (len_b + BN - 1) / BN;
@@ -590,36 +608,31 @@ __global__ void __launch_bounds__(PP_THREADS, 1)
       d3b::mbar_init(&bars.slot_full[i], 1);
       d3b::mbar_init(&bars.slot_empty[i], 1);
     }
-    for (int x = 0; x < 2; ++x) {
-      d3b::mbar_init(&bars.s_full[x], 1);
-      d3b::mbar_init(&bars.p_full[x][0], 128);
-      d3b::mbar_init(&bars.p_full[x][1], 128);
-      d3b::mbar_init(&bars.pv_done[x], 1);
-      d3b::mbar_init(&bars.o_final[x], 1);
-    }
+    d3b::mbar_init(&bars.s_full, 1);
+    d3b::mbar_init(&bars.p_full[0], 128);
+    d3b::mbar_init(&bars.p_full[1], 128);
+    d3b::mbar_init(&bars.o_final, 1);
+    d3b::mbar_init(&bars.pv_done, 1);
     d3b::mbar_init(&bars.drain, 1);
     bars.abort_flag = 0;
     d3b::fence_barrier_init();
   }
-  if (rows_used < BM) {  // rows no TMA box covers are zero for the MMA
+  if (rows_used < BM) {
     const int per_chunk = (BM - rows_used) * C::ROWB / 16;
-    for (int i = threadIdx.x; i < 2 * C::NCH * per_chunk; i += PP_THREADS) {
-      const int x = i / (C::NCH * per_chunk), rem = i % (C::NCH * per_chunk);
-      const int c = rem / per_chunk, o = rem % per_chunk;
-      reinterpret_cast<uint4*>(sQ + x * C::Q_BYTES + c * C::Q_CHUNK + rows_used * C::ROWB)[o] =
-          make_uint4(0, 0, 0, 0);
+    for (int i = threadIdx.x; i < C::NCH * per_chunk; i += C2_THREADS) {
+      const int c = i / per_chunk, o = i % per_chunk;
+      reinterpret_cast<uint4*>(sQ + c * C::Q_CHUNK + rows_used * C::ROWB)[o] = make_uint4(0, 0, 0, 0);
     }
     d3b::fence_proxy_async_smem();
   }
-  if (warp == 9) d3b::tmem_alloc(&bars.tmem_slot, 512);
+  if (warp == 5) d3b::tmem_alloc(&bars.tmem_slot, C::TMEM_COLS);
   d3b::tc_fence_before();
   __syncthreads();
   d3b::tc_fence_after();
   const uint32_t tmem_base = bars.tmem_slot;
-  if (warp >= 8) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 104;" ::: "memory");
-   if (warp == 8) {
-    // ================= TMA producer =================
+
+  if (warp == 4) {
+    // ================= TMA producer: Q, then K_0, V_0, K_1, V_1, ... =================
     if (lane == 0) {
       d3b::tma_prefetch_desc(&mapQ);
       d3b::tma_prefetch_desc(&mapKq);
@@ -628,17 +641,15 @@ __global__ void __launch_bounds__(PP_THREADS, 1)
         d3b::tma_prefetch_desc(&mapKs);
         d3b::tma_prefetch_desc(&mapVs);
       }
-      d3b::mbar_arrive_expect_tx(&bars.q_full, ns * C::NCH * rows_used * C::ROWB);
-      for (int x = 0; x < ns; ++x)
+      d3b::mbar_arrive_expect_tx(&bars.q_full, C::NCH * rows_used * C::ROWB);
 #pragma unroll
-        for (int c = 0; c < C::NCH; ++c)
-          d3b::tma_load_4d(sQ + x * C::Q_BYTES + c * C::Q_CHUNK, &mapQ, &bars.q_full, c * C::CH, g * G,
-                           tok_a + x * T, b);
+      for (int c = 0; c < C::NCH; ++c)
+        d3b::tma_load_4d(sQ + c * C::Q_CHUNK, &mapQ, &bars.q_full, c * C::CH, g * G, tok0, b);
       int stage = 0;
       uint32_t phase = 0;
       for (int i = 0; i < 2 * n; ++i) {
         const int is_v = i & 1, j = i >> 1;
-        if (!d3b::mbar_wait(&bars.slot_empty[stage], phase ^ 1, abort_flag, p.err, kSitePPSlotEmpty)) break;
+        if (!d3b::mbar_wait(&bars.slot_empty[stage], phase ^ 1, abort_flag, p.err, kSite2CSlotEmpty)) break;
         d3b::mbar_arrive_expect_tx(&bars.slot_full[stage], C::SLOT_BYTES);
         uint8_t* dst = sKV + stage * C::SLOT_BYTES;
         if (j < n_s) {
@@ -656,213 +667,157 @@ __global__ void __launch_bounds__(PP_THREADS, 1)
         if (++stage == C::NSLOT) { stage = 0; phase ^= 1; }
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == 5) {
     // ================= MMA issuer =================
     if (lane == 0) {
       constexpr uint32_t fmt = FP16 ? 0u : 1u;
       constexpr uint32_t idesc_qk = d3b::make_idesc(1, fmt, fmt, 0, 0, BM, BN);
       constexpr uint32_t idesc_pv = d3b::make_idesc(1, fmt, fmt, 0, 1, BM, D);
-      // Base descriptors, built once: an operand's descriptor is the base plus
-      // (byte offset >> 4) in the start-address field (all offsets < 256 KB).
       const uint64_t dq0 = d3b::make_smem_desc(d3b::smem_u32(sQ), 16, C::SBO, C::LAYOUT);
       const uint64_t dk0 = d3b::make_smem_desc(d3b::smem_u32(sKV), 16, C::SBO, C::LAYOUT);
       const uint64_t dv0 = d3b::make_smem_desc(d3b::smem_u32(sKV), C::SLOT_CHUNK, C::SBO, C::LAYOUT);
       auto slot_of = [&](int item) { return item % C::NSLOT; };
       auto wait_item = [&](int item) -> bool {
         return d3b::mbar_wait(&bars.slot_full[slot_of(item)], (uint32_t)(item / C::NSLOT) & 1, abort_flag, p.err,
-                              kSitePPSlotFull);
+                              kSite2CSlotFull);
       };
-      // S[sb] = Q_x K^T
-      auto qk = [&](int x, int sb, int item) {
-        const uint64_t dq = dq0 + (uint64_t)((x * C::Q_BYTES) >> 4);
+      auto qk = [&](int item) {
         const uint64_t dk = dk0 + (uint64_t)((slot_of(item) * C::SLOT_BYTES) >> 4);
-        const uint32_t d_tmem = tmem_base + C::COL_S + sb * BN;
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
           const int c = (k * 16) / C::CH, off = ((k * 16) % C::CH) * 2;
-          d3b::mma_f16_ss(d_tmem, dq + (uint64_t)((c * C::Q_CHUNK + off) >> 4),
+          d3b::mma_f16_ss(tmem_base + C::COL_S, dq0 + (uint64_t)((c * C::Q_CHUNK + off) >> 4),
                           dk + (uint64_t)((c * C::SLOT_CHUNK + off) >> 4), idesc_qk, k > 0 ? 1u : 0u);
         }
-        d3b::mma_commit(&bars.s_full[sb]);
+        d3b::mma_commit(&bars.s_full);
       };
-      // O_x (+)= P[sb] V   (P in the upper half of S[sb]); each half of P is
-      // used as soon as the softmax has published it (use = the phase parity).
-      auto pv = [&](int x, int sb, int item, bool accumulate, uint32_t use) -> bool {
+      // O (+)= P V, the half with keys 64-127 first (the softmax publishes it first)
+      auto pv = [&](int item, bool accumulate, uint32_t use) -> bool {
         const uint64_t dv = dv0 + (uint64_t)((slot_of(item) * C::SLOT_BYTES) >> 4);
-        const uint32_t d_tmem = tmem_base + C::COL_O + x * D;
-        const uint32_t a_tmem = tmem_base + C::COL_S + sb * BN + BN / 2;
+        const uint32_t a_tmem = tmem_base + C::COL_S + BN / 2;
+        bool first = true;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          if (!d3b::mbar_wait(&bars.p_full[x][h], use & 1, abort_flag, p.err, kSitePPPFull)) return false;
+        for (int hh = 0; hh < 2; ++hh) {
+          const int h = 1 - hh;
+          if (!d3b::mbar_wait(&bars.p_full[h], use & 1, abort_flag, p.err, kSite2CPFull)) return false;
           d3b::tc_fence_after();
 #pragma unroll
-          for (int k = h * BN / 32; k < (h + 1) * BN / 32; ++k)
-            d3b::mma_f16_ts(d_tmem, a_tmem + k * 8, dv + (uint64_t)((k * 16 * C::ROWB) >> 4), idesc_pv,
-                            (accumulate || k > 0) ? 1u : 0u);
+          for (int k = h * BN / 32; k < (h + 1) * BN / 32; ++k) {
+            d3b::mma_f16_ts(tmem_base + C::COL_O, a_tmem + k * 8, dv + (uint64_t)((k * 16 * C::ROWB) >> 4),
+                            idesc_pv, (accumulate || !first) ? 1u : 0u);
+            first = false;
+          }
         }
-        d3b::mma_commit(&bars.pv_done[x]);
         return true;
       };
-      bool ok = d3b::mbar_wait(&bars.q_full, 0, abort_flag, p.err, kSitePPQ);
-      if (ns == 2) {
-        for (int j = 0; j < n && ok; ++j) {
-          const int it_k = 2 * j, it_v = 2 * j + 1;
-          const uint32_t prev = (uint32_t)((j - 1) & 1);
-          // QK_A(j) (in issue order after PV_A(j-1), which read P_A from S_A)
-          if (!(ok = wait_item(it_k))) break;
-          if (D3B_STRICT_MMA_ORDER && j > 0 &&
-              !(ok = d3b::mbar_wait(&bars.pv_done[0], prev, abort_flag, p.err, kSitePPPv)))
-            break;
-          d3b::tc_fence_after();
-          qk(0, 0, it_k);
-          if (j > 0) {  // PV_B(j-1)
-            if (!(ok = pv(1, 1, it_v - 2, j - 1 > 0, prev))) break;
-            d3b::mma_commit(&bars.slot_empty[slot_of(it_v - 2)]);  // V_{j-1} done
-          }
-          // QK_B(j)
-          if (D3B_STRICT_MMA_ORDER && j > 0 &&
-              !(ok = d3b::mbar_wait(&bars.pv_done[1], prev, abort_flag, p.err, kSitePPPv)))
-            break;
-          d3b::tc_fence_after();
-          qk(1, 1, it_k);
-          d3b::mma_commit(&bars.slot_empty[slot_of(it_k)]);  // K_j done
-          // PV_A(j)
-          if (!(ok = wait_item(it_v))) break;
-          if (!(ok = pv(0, 0, it_v, j > 0, (uint32_t)j))) break;
-        }
-        if (ok) {
-          d3b::mma_commit(&bars.o_final[0]);
-          if (pv(1, 1, 2 * n - 1, n - 1 > 0, (uint32_t)(n - 1))) d3b::mma_commit(&bars.o_final[1]);
-          d3b::mma_commit(&bars.slot_empty[slot_of(2 * n - 1)]);
-        }
-      } else {
-        // one Q tile, S double-buffered in S_A / S_B
-        if (ok && (ok = wait_item(0))) {
-          d3b::tc_fence_after();
-          qk(0, 0, 0);
-          d3b::mma_commit(&bars.slot_empty[slot_of(0)]);
-        }
-        for (int j = 0; j < n && ok; ++j) {
-          if (j + 1 < n) {  // QK(j+1) into S[(j+1)%2] (after PV(j-1), which read that buffer's P)
-            const int it_k = 2 * (j + 1);
-            if (!(ok = wait_item(it_k))) break;
-            d3b::tc_fence_after();
-            qk(0, (j + 1) & 1, it_k);
-            d3b::mma_commit(&bars.slot_empty[slot_of(it_k)]);
-          }
-          const int it_v = 2 * j + 1;
-          if (!(ok = wait_item(it_v))) break;
-          if (!(ok = pv(0, j & 1, it_v, j > 0, (uint32_t)j))) break;
-          d3b::mma_commit(&bars.slot_empty[slot_of(it_v)]);
-        }
-        if (ok) d3b::mma_commit(&bars.o_final[0]);
+      bool ok = d3b::mbar_wait(&bars.q_full, 0, abort_flag, p.err, kSite2CQ);
+      if (ok && (ok = wait_item(0))) {
+        d3b::tc_fence_after();
+        qk(0);
+        d3b::mma_commit(&bars.slot_empty[slot_of(0)]);
       }
+      for (int j = 0; j < n && ok; ++j) {
+        const int it_v = 2 * j + 1;
+        if (!(ok = wait_item(it_v))) break;
+        if (!(ok = pv(it_v, j > 0, (uint32_t)j))) break;
+        d3b::mma_commit(&bars.slot_empty[slot_of(it_v)]);
+        if (j + 1 < n) {  // QK(j+1): in issue order after PV(j), which read P from S
+          const int it_k = 2 * (j + 1);
+          if (D3B_STRICT_MMA_ORDER) {
+            d3b::mma_commit(&bars.pv_done);
+            if (!(ok = d3b::mbar_wait(&bars.pv_done, (uint32_t)(j & 1), abort_flag, p.err, kSite2CPvDone))) break;
+          }
+          if (!(ok = wait_item(it_k))) break;
+          d3b::tc_fence_after();
+          qk(it_k);
+          d3b::mma_commit(&bars.slot_empty[slot_of(it_k)]);
+        }
+      }
+      if (ok) d3b::mma_commit(&bars.o_final);
       d3b::mma_commit(&bars.drain);
       const uint32_t addr = d3b::smem_u32(&bars.drain);
       const uint64_t t0 = d3b::globaltimer_ns();
       while (!d3b::mbar_try_wait(addr, 0)) {
         if (d3b::globaltimer_ns() - t0 > D3B_WAIT_LIMIT_NS) {
-          d3b::record_device_error(p.err, kSitePPDrain);
+          d3b::record_device_error(p.err, kSite2CDrain);
           break;
         }
       }
     }
-   }
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 200;" ::: "memory");
-    // ================= softmax + epilogue (warps 0-7) =================
-    const int x = warp >> 2;  // Q tile of this warpgroup
-    const int quarter = warp & 3;
+    // ================= softmax + epilogue (warps 0-3) =================
+    const int quarter = warp;
     const int r = quarter * 32 + lane;
-    if (x >= ns) {
-      zero_tile_rows<D>(p, b, g, tok_b, quarter, lane);
-    } else {
-      const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
-      const uint32_t col_o = C::COL_O + x * D;
-      const float sl2 = p.scale_log2;
-      float m_ref = -INFINITY, l_sum = 0.f;
-      bool ok = true;
-      for (int j = 0; j < n; ++j) {
-        // S buffer and its use count: own buffer with two tiles, alternating with one
-        const int sb = ns == 2 ? x : (j & 1);
-        const uint32_t s_use = ns == 2 ? (uint32_t)j : (uint32_t)(j >> 1);
-        const uint32_t col_s = C::COL_S + sb * BN, col_p = col_s + BN / 2;
-        if (!d3b::warp_wait(&bars.s_full[sb], s_use & 1, abort_flag, p.err, kSitePPSFull)) { ok = false; break; }
-        d3b::tc_fence_after();
-        const int valid = j < n_s ? p.S - j * BN : len_b - (j - n_s) * BN;
-        float s[BN];
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c)
-          d3b::tmem_ld32(lane_addr + col_s + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
-        d3b::tmem_wait_ld();
-        if (valid < BN) {
-#pragma unroll
-          for (int c = 0; c < BN; ++c)
-            if (c >= valid) s[c] = -INFINITY;
-        }
-        const float m_tile = max_n<BN>(s) * sl2;
-        const bool rescale = __any_sync(0xffffffffu, m_tile > m_ref + kRescaleThreshold);
-        const float m_new = rescale ? fmaxf(m_ref, m_tile) : m_ref;
-        const float alpha = rescale ? d3b::ex2_approx(m_ref - m_new) : 1.f;
-        // P (BN/2 columns, into the upper half of S whose values are in registers),
-        // published in two halves. A rescale of O must land before the first.
-        if (rescale && j > 0) {
-          // O_x must hold PV(j-1). With two tiles that is already implied by
-          // s_full (QK_x(j) was committed after PV_x(j-1)); with one tile, QK(j)
-          // was issued before PV(j-1), so wait for PV(j-1)'s commit (the barrier
-          // is at most one phase ahead here, so the parity wait is exact).
-          if (!d3b::warp_wait(&bars.pv_done[x], (uint32_t)((j - 1) & 1), abort_flag, p.err, kSitePPPv)) {
-            ok = false;
-            break;
-          }
-          d3b::tc_fence_after();
-#pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t o[32];
-            d3b::tmem_ld32(lane_addr + col_o + c * 32, o);
-            d3b::tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            d3b::tmem_st32(lane_addr + col_o + c * 32, o);
-          }
-        }
-        float rowsum = 0.f;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint32_t pk[BN / 4];
-          rowsum += exp_row<BN / 2, FP16>(s + h * (BN / 2), sl2, m_new, pk);
-          d3b::tmem_st32(lane_addr + col_p + h * 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
-          d3b::tmem_wait_st();
-          d3b::tc_fence_before();
-          d3b::mbar_arrive(&bars.p_full[x][h]);
-        }
-        l_sum = l_sum * alpha + rowsum;
-        m_ref = m_new;
-      }
-      if (ok) ok = d3b::warp_wait(&bars.o_final[x], 0, abort_flag, p.err, kSitePPFinal);
-      if (ok) {
-        d3b::tc_fence_after();
-        const int tok = tok_a + x * T + r / G, h = r % G;
-        const bool in_tensor = r < rows_used && tok < p.L;
-        const bool real = tok < len_b;
-        const float inv_l = 1.f / l_sum;
-        uint16_t* dst_row = static_cast<uint16_t*>(p.out) + (int64_t)b * p.out_sb +
-                            (int64_t)(g * G + h) * p.out_sh + (int64_t)tok * p.out_sl;
+    const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
+    const uint32_t col_s = C::COL_S, col_p = C::COL_S + BN / 2, col_o = C::COL_O;
+    const float sl2 = p.scale_log2;
+    float m_ref = -INFINITY, l_sum = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      if (!d3b::warp_wait(&bars.s_full, (uint32_t)(j & 1), abort_flag, p.err, kSite2CSFull)) { ok = false; break; }
+      d3b::tc_fence_after();
+      const int valid = j < n_s ? p.S - j * BN : len_b - (j - n_s) * BN;
+      float s[64];
+      load64(lane_addr + col_s, 0, valid, s);
+      const float m_lo = max_n<64>(s);
+      load64(lane_addr + col_s + 64, 64, valid, s);  // keys 64-127 stay in registers
+      const float m_tile = fmaxf(m_lo, max_n<64>(s)) * sl2;
+      const bool rescale = __any_sync(0xffffffffu, m_tile > m_ref + kRescaleThreshold);
+      const float m_new = rescale ? fmaxf(m_ref, m_tile) : m_ref;
+      const float alpha = rescale ? d3b::ex2_approx(m_ref - m_new) : 1.f;
+      if (rescale && j > 0) {
+        // s_full(j) is a commit issued after PV(j-1): O is complete here
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t o[32];
           d3b::tmem_ld32(lane_addr + col_o + c * 32, o);
           d3b::tmem_wait_ld();
-          if (in_tensor) {
-            uint32_t w[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-              w[i] = real ? pack2<FP16>(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l)
-                          : 0u;
-            uint4* dst = reinterpret_cast<uint4*>(dst_row + c * 32);
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          d3b::tmem_st32(lane_addr + col_o + c * 32, o);
+        }
+      }
+      // P into the upper half of S (whose values are all in registers), keys
+      // 64-127 first: the MMA thread consumes that half first.
+      uint32_t pk[32];
+      // keys 64-127 -> P columns 32-63 (S columns 96-127, held in registers)
+      float rowsum = exp_row<64, FP16>(s, sl2, m_new, pk);
+      d3b::tmem_st32(lane_addr + col_p + 32, pk);
+      d3b::tmem_wait_st();
+      d3b::tc_fence_before();
+      d3b::mbar_arrive(&bars.p_full[1]);
+      // keys 0-63 (reloaded) -> P columns 0-31 (S columns 64-95, consumed above)
+      load64(lane_addr + col_s, 0, valid, s);
+      rowsum += exp_row<64, FP16>(s, sl2, m_new, pk);
+      d3b::tmem_st32(lane_addr + col_p, pk);
+      d3b::tmem_wait_st();
+      d3b::tc_fence_before();
+      d3b::mbar_arrive(&bars.p_full[0]);
+      l_sum = l_sum * alpha + rowsum;
+      m_ref = m_new;
+    }
+    if (ok) ok = d3b::warp_wait(&bars.o_final, 0, abort_flag, p.err, kSite2CFinal);
+    if (ok) {
+      d3b::tc_fence_after();
+      const int tok = tok0 + r / G, h = r % G;
+      const bool in_tensor = r < rows_used && tok < p.L;
+      const bool real = tok < len_b;
+      const float inv_l = 1.f / l_sum;
+      uint16_t* dst_row = static_cast<uint16_t*>(p.out) + (int64_t)b * p.out_sb + (int64_t)(g * G + h) * p.out_sh +
+                          (int64_t)tok * p.out_sl;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        d3b::tmem_ld32(lane_addr + col_o + c * 32, o);
+        d3b::tmem_wait_ld();
+        if (in_tensor) {
+          uint32_t w[16];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-          }
+          for (int i = 0; i < 16; ++i)
+            w[i] = real ? pack2<FP16>(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l) : 0u;
+          uint4* dst = reinterpret_cast<uint4*>(dst_row + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
         }
       }
     }
@@ -871,23 +826,22 @@ __global__ void __launch_bounds__(PP_THREADS, 1)
   d3b::tc_fence_before();
   __syncthreads();
   d3b::tc_fence_after();
-  if (warp == 9) d3b::tmem_dealloc(tmem_base, 512);
+  if (warp == 5) d3b::tmem_dealloc(tmem_base, C::TMEM_COLS);
 }
 
 template <int D, int FP16>
-int launch_pp(const CUtensorMap* maps, const Params& prm, int tiles, int Hkv, int B, cudaStream_t stream) {
-  using C = CfgPP<D>;
+int launch_2c(const CUtensorMap* maps, const Params& prm, dim3 grid, cudaStream_t stream) {
+  using C = Cfg2C<D>;
   static int attr_set[64] = {0};
   const int dev = d3b_host::current_device();
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(prefix_bidir_pp_kernel<D, FP16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(prefix_bidir_2c_kernel<D, FP16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::SMEM_BYTES) != cudaSuccess)
       return D3B_ECUDA;
     attr_set[dev] = 1;
   }
-  dim3 grid((tiles + 1) / 2, Hkv, B);
-  prefix_bidir_pp_kernel<D, FP16><<<grid, PP_THREADS, C::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3],
-                                                                              maps[4], prm);
+  prefix_bidir_2c_kernel<D, FP16><<<grid, C2_THREADS, C::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3],
+                                                                             maps[4], prm);
   return d3b_host::check_launch();
 }
 
@@ -909,14 +863,15 @@ int launch(const CUtensorMap* maps, const Params& prm, dim3 grid, cudaStream_t s
 
 template <int FP16>
 int dispatch(int D, const CUtensorMap* maps, const Params& prm, dim3 grid, cudaStream_t s) {
-  // D <= 128: two Q tiles per CTA; D = 256 (O needs 256 TMEM columns): one.
+  // D = 256 (O needs 256 TMEM columns): one tile per CTA, one CTA per SM.
+  if (D == 256) return launch<256, 64, FP16>(maps, prm, grid, s);
+  // D <= 128: one tile per CTA, two CTAs per SM.
   switch (D) {
-    case 32: return launch_pp<32, FP16>(maps, prm, grid.x, grid.y, grid.z, s);
-    case 64: return launch_pp<64, FP16>(maps, prm, grid.x, grid.y, grid.z, s);
-    case 128: return launch_pp<128, FP16>(maps, prm, grid.x, grid.y, grid.z, s);
-    case 256: return launch<256, 64, FP16>(maps, prm, grid, s);
-    default: return D3B_EUNSUPPORTED;
+    case 32: return launch_2c<32, FP16>(maps, prm, grid, s);
+    case 64: return launch_2c<64, FP16>(maps, prm, grid, s);
+    case 128: return launch_2c<128, FP16>(maps, prm, grid, s);
   }
+  return D3B_EUNSUPPORTED;
 }
 
 }  // namespace
