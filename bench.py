@@ -376,7 +376,7 @@ def main():
                        "l2": "flushed before every timed step (256 MiB write)"},
             "roofline": {"bound": "tensor", "achieved": achieved_tflops, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved_tflops / peak, "traffic": traffic,
-                         "kernel": "prefix_bidir_2c_kernel<128,bf16>",
+                         "kernel": "prefix_bidir_dual_kernel<128,bf16>",
                          "algorithmic_flops_per_launch": flops,
                          "peak_source": f"{peaks['source']} bf16 dense (burst)"},
             "e2e": {"value": cfg["B"] * world / (e2e_ms / 1e3), "unit": "question-blocks/s",

@@ -20,11 +20,12 @@
 // then ceil(len_b/BN) own-block tiles; only the last state tile and the own
 // tiles carry a key mask. Nothing outside [state | own block] is touched.
 //
-// Two kernels share this work unit, the key schedule and the softmax:
-//   D <= 128  prefix_bidir_2c_kernel: one Q tile per CTA, two CTAs per SM
-//             (the tensor core alternates between the two CTAs' chains).
-//   D == 256  prefix_bidir_kernel: one Q tile per CTA, one CTA per SM, S
-//             double-buffered in TMEM (O alone takes 256 columns).
+// Two kernels share this work unit, the key schedule and the softmax; both run
+// one CTA per SM with S and P double-buffered in TMEM:
+//   D <= 128  prefix_bidir_dual_kernel: QK^T and PV issued by two threads,
+//             two softmax warpgroups on alternating key tiles.
+//   D == 256  prefix_bidir_kernel: one MMA-issuing thread, one softmax
+//             warpgroup, 64-key tiles (O alone takes 256 TMEM columns).
 // Both use one thread per Q row for the softmax: tcgen05.ld of the S row,
 // online softmax in the log2 domain, P as bf16/f16 written back to TMEM for
 // the TS-form PV MMA (V read MN-major from shared memory), O rescaled in TMEM
@@ -46,6 +47,9 @@ namespace {
 constexpr int BM = 128;
 constexpr int NUM_THREADS = 192;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O when max grows by > 2^8
+#ifndef D3B_POLY8
+#define D3B_POLY8 1  // FMA-pipe exponentials per eight pairs in the D <= 128 softmax
+#endif
 
 enum {
   kSiteQ = 2001,
@@ -179,17 +183,17 @@ __device__ __forceinline__ void exp2_poly2(float x0, float x1, float& p0, float&
 }
 
 // P = 2^(s * sl2 - m) for one row of N scores: packed pairs into pk (bf16 or
-// f16), returns the row sum of the fp32 values. One pair in four goes through
-// the FMA-pipe exponential, the rest through MUFU ex2, so neither unit alone
-// bounds the softmax.
-template <int N, int FP16>
+// f16), returns the row sum of the fp32 values. POLY8 pairs in every eight go
+// through the FMA-pipe exponential, the rest through MUFU ex2, so neither unit
+// alone bounds the softmax.
+template <int N, int FP16, int POLY8 = 2>
 __device__ __forceinline__ float exp_row(const float* s, float sl2, float m, uint32_t* pk) {
   float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int c = 0; c < N; c += 2) {
     float x0, x1, p0, p1;
     fma2_bc(x0, x1, s[c], s[c + 1], sl2, -m);
-    if (((c >> 1) & 3) == 3) {
+    if (((c >> 1) & 7) >= 8 - POLY8) {
       exp2_poly2(x0, x1, p0, p1);
     } else {
       p0 = d3b::ex2_approx(x0);
@@ -475,81 +479,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 1) d3b::tmem_dealloc(tmem_base, C::TMEM_COLS);
 }
 
-// ===========================================================================
-// One Q tile per CTA, two CTAs per SM (D <= 128).
-//
-// 256 TMEM columns per CTA: O (D) | S (128 keys); P (bf16/f16) goes into the
-// upper half of S once S has been read. Two co-resident CTAs share the SM's
-// tensor core, so while one CTA's softmax runs, the other's QK^T / PV execute;
-// each CTA's chain QK(j) -> softmax(j) -> PV(j) -> QK(j+1) needs no
-// cross-CTA ordering. Shared memory stays under half an SM (Q + two 32 KB K/V
-// slots at D = 128).
-// Warps 0-3 softmax + epilogue, warp 4 TMA producer, warp 5 TMEM + MMA. At
-// 128 registers per thread a softmax thread holds 64 scores at a time: it
-// reduces keys 0-63, then 64-127, turns the second half into P, reloads the
-// first half and turns it into P. P is published in those two halves
-// (separate barriers), so the first four PV MMAs run while the softmax still
-// exponentiates keys 0-63. (An 8-warp variant that lends the softmax 200
-// registers through setmaxnreg, to keep all 128 scores in registers,
-// measured slower.)
-// QK(j+1) overwrites S, whose upper half still holds P(j) for PV(j). Both are
-// issued by the same thread in that order, and tcgen05.mma operations of one
-// issuing thread execute in issue order on the SM's tensor core, so QK(j+1)
-// cannot write S before PV(j) has read P(j). This is an observed property of
-// the hardware, not one of the PTX ISA's guaranteed "pipelined" pairs (those
-// cover MMAs on the same accumulator). Building with -DD3B_STRICT_MMA_ORDER=1
-// instead waits for PV(j)'s commit before issuing QK(j+1) (slower: the tensor
-// pipe drains once per key tile); the parity tests pass in both builds.
-// Either way, s_full(j+1) is a tcgen05.commit after PV(j), so O is complete
-// when the softmax sees S(j+1) and may rescale O without further
-// synchronisation.
-// ===========================================================================
-#ifndef D3B_STRICT_MMA_ORDER
-#define D3B_STRICT_MMA_ORDER 0
-#endif
-constexpr int C2_THREADS = 192;
-
-template <int D>
-struct Cfg2C {
-  static constexpr int BN = 128;
-  static constexpr int CH = D >= 64 ? 64 : D;
-  static constexpr int ROWB = CH * 2;
-  static constexpr int NCH = D / CH;
-  static constexpr uint32_t LAYOUT = ROWB == 128 ? d3b::kLayoutSW128 : d3b::kLayoutSW64;
-  static constexpr int SBO = 8 * ROWB;
-  static constexpr int Q_BYTES = BM * D * 2;
-  static constexpr int SLOT_BYTES = BN * D * 2;
-  static constexpr int Q_CHUNK = BM * ROWB;
-  static constexpr int SLOT_CHUNK = BN * ROWB;
-  static constexpr int NSLOT_RAW = (110 * 1024 - Q_BYTES - 1024) / SLOT_BYTES;
-  static constexpr int NSLOT = NSLOT_RAW > 8 ? 8 : NSLOT_RAW;
-  static constexpr int SMEM_BYTES = Q_BYTES + NSLOT * SLOT_BYTES + 1024;
-  static constexpr int COL_O = 0;
-  static constexpr int COL_S = D;
-  static constexpr uint32_t TMEM_COLS = 256;
-  static_assert(D + BN <= 256, "TMEM budget");
-  static_assert(NSLOT >= 2, "smem budget");
-  static_assert(SMEM_BYTES <= 113 * 1024, "two CTAs per SM");
-};
-
-struct __align__(8) Bars2C {
-  uint64_t q_full;
-  uint64_t slot_full[8];
-  uint64_t slot_empty[8];
-  uint64_t s_full;
-  uint64_t p_full[2];  // halves of P: [0] keys 0-63, [1] keys 64-127
-  uint64_t o_final;
-  uint64_t pv_done;  // only with D3B_STRICT_MMA_ORDER
-  uint64_t drain;
-  uint32_t tmem_slot;
-  int abort_flag;
-};
-
-enum {
-  kSite2CQ = 5001, kSite2CSlotEmpty, kSite2CSlotFull, kSite2CPFull, kSite2CSFull, kSite2CFinal, kSite2CDrain,
-  kSite2CPvDone
-};
-
 // Zero the output rows of a Q tile that holds no real token (rows past the
 // tensor's L are skipped).
 template <int D>
@@ -564,27 +493,121 @@ __device__ __forceinline__ void zero_tile_rows(const Params& p, int b, int g, in
   }
 }
 
-// 64 columns of this thread's TMEM row into registers, keys >= valid masked.
-__device__ __forceinline__ void load64(uint32_t addr, int key0, int valid, float (&s)[64]) {
-  d3b::tmem_ld32(addr, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
-  d3b::tmem_ld32(addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
-  d3b::tmem_wait_ld();
-  if (valid - key0 < 64) {
+// ===========================================================================
+// One Q tile per CTA, one CTA per SM, two MMA-issuing threads (D <= 128).
+//
+// A tcgen05.mma stream from one issuing thread runs an M128·N128·K16 bf16
+// instruction in ~84 cycles (76% of the tensor rate); two threads issuing
+// independent MMAs on the same SM share the tensor core at up to its full
+// rate (measured on this B200: 128 cycles per instruction each when both
+// streams use the same operand form, ~167 each for an SS stream next to a TS
+// stream). So QK^T and PV get one issuing thread each:
+//   warp 9  (lane 0)  S[j%2] = Q K_j^T   (SS: Q and K from shared memory)
+//   warp 10 (lane 0)  O += P[j%2] V_j     (TS: P from TMEM, V from shared memory)
+// TMEM (512 columns): O [0,D) | S0 [128,256) | S1 [256,384) | P0 [384,448) |
+// P1 [448,512). With S and P double-buffered, QK(j+1) runs while the softmax
+// works on S(j), and PV(j) while it works on S(j+1).
+// Softmax: 8 warps in two groups of four, one thread per row in each group.
+// Group 0 takes the even key tiles (S0, P0), group 1 the odd ones (S1, P1),
+// so the two groups work half a tile apart and one group's waits overlap the
+// other's arithmetic. The per-row reference max is handed from tile to tile
+// through shared memory (see the softmax section).
+// Warp 8 streams Q and then K_0, K_1, ... into the K ring (read by the QK
+// thread), warp 11 streams V_0, V_1, ... into the V ring (read by the PV
+// thread): each ring has one producer and one consumer that take its tiles in
+// order (an mbarrier parity wait may not run more than one phase ahead), and
+// K tiles never wait behind a full V ring.
+// Bounds measured on this B200 for this design, per 128-key tile: tensor
+// 16 x 64 cycles at the full rate; MUFU 128 x 128 exponentials / 16 per cycle
+// = 1024 cycles (one pair in eight goes to the FMA pipe instead); shared
+// memory 160 KB (Q, K, V operand reads + K/V TMA writes) at ~128 B/cycle.
+// ===========================================================================
+constexpr int DU_THREADS = 384;  // 8 softmax warps, K producer, QK issuer, PV issuer, V producer
+
+template <int D>
+struct CfgDual {
+  static constexpr int BN = 128;
+  static constexpr int CH = D >= 64 ? 64 : D;
+  static constexpr int ROWB = CH * 2;
+  static constexpr int NCH = D / CH;
+  static constexpr uint32_t LAYOUT = ROWB == 128 ? d3b::kLayoutSW128 : d3b::kLayoutSW64;
+  static constexpr int SBO = 8 * ROWB;
+  static constexpr int Q_BYTES = BM * D * 2;
+  static constexpr int SLOT_BYTES = BN * D * 2;
+  static constexpr int Q_CHUNK = BM * ROWB;
+  static constexpr int SLOT_CHUNK = BN * ROWB;
+  // 227 KB of shared memory per CTA, minus the static barriers/exchange arrays
+  static constexpr int NSLOT_RAW = (227 * 1024 - 4096 - 1024 - Q_BYTES) / SLOT_BYTES;
+  static constexpr int NK_RAW = (NSLOT_RAW + 1) / 2;
+  static constexpr int NK = NK_RAW > 8 ? 8 : NK_RAW;                  // K ring slots
+  static constexpr int NV = NSLOT_RAW - NK > 8 ? 8 : NSLOT_RAW - NK;  // V ring slots
+  static constexpr int SMEM_BYTES = Q_BYTES + (NK + NV) * SLOT_BYTES + 1024;
+  static constexpr int COL_O = 0;
+  static constexpr int COL_S = 128;  // + b * BN
+  static constexpr int COL_P = 384;  // + b * BN / 2
+  static constexpr int OH = D / 2;   // O columns per softmax half
+  static constexpr uint32_t TMEM_COLS = 512;
+  static_assert(D <= 128, "TMEM budget");
+  static_assert(NK >= 2 && NV >= 2, "smem budget");
+};
+
+struct __align__(8) BarsDual {
+  uint64_t q_full;
+  uint64_t k_full[8], k_empty[8];  // K ring
+  uint64_t v_full[8], v_empty[8];  // V ring
+  uint64_t s_full[2];   // QK(j) committed into S[j%2]
+  uint64_t s_free[2];   // softmax group j%2 has read S[j%2]
+  uint64_t p_full[2];   // softmax group j%2 has written P[j%2]
+  uint64_t p_free[2];   // PV(j) committed: P[j%2] is free and O holds PV(0..j)
+  uint64_t mdone[2];    // reference max of tile j published (by group j%2)
+  uint64_t xsum[4];     // per-group sums exchanged for the epilogue (per warp pair)
+  uint64_t o_final;
+  uint64_t drain_qk, drain_pv;
+  uint32_t tmem_slot;
+  int abort_flag;
+};
+
+enum {
+  kSiteDuQ = 6001, kSiteDuSlotK, kSiteDuSlotV, kSiteDuSlotEmpty, kSiteDuSFree, kSiteDuSFull, kSiteDuPFull,
+  kSiteDuPFree, kSiteDuXMax, kSiteDuFinal, kSiteDuDrain
+};
+
+// Columns [c0, c0 + W) of this thread's TMEM row, scaled by f, written back (W = 16 or 32 multiple).
+template <int W>
+__device__ __forceinline__ void scale_cols(uint32_t addr, float f) {
+  if constexpr (W % 32 == 0) {
+#pragma unroll 1
+    for (int c = 0; c < W / 32; ++c) {
+      uint32_t o[32];
+      d3b::tmem_ld32(addr + c * 32, o);
+      d3b::tmem_wait_ld();
 #pragma unroll
-    for (int c = 0; c < 64; ++c)
-      if (key0 + c >= valid) s[c] = -INFINITY;
+      for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+      d3b::tmem_st32(addr + c * 32, o);
+    }
+  } else {
+    static_assert(W == 16, "half-row width");
+    uint32_t o[16];
+    d3b::tmem_ld16(addr, o);
+    d3b::tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+    d3b::tmem_st16(addr, o);
   }
 }
 
 template <int D, int FP16>
-__global__ void __launch_bounds__(C2_THREADS, 2)
-    prefix_bidir_2c_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapKs,
-                           const __grid_constant__ CUtensorMap mapVs, const __grid_constant__ CUtensorMap mapKq,
-                           const __grid_constant__ CUtensorMap mapVq, const Params p) {
-  using C = Cfg2C<D>;
+__global__ void __launch_bounds__(DU_THREADS, 1)
+    prefix_bidir_dual_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapKs,
+                             const __grid_constant__ CUtensorMap mapVs, const __grid_constant__ CUtensorMap mapKq,
+                             const __grid_constant__ CUtensorMap mapVq, const Params p) {
+  using C = CfgDual<D>;
   constexpr int BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ Bars2C bars;
+  __shared__ BarsDual bars;
+  __shared__ float mref_s[2][BM];   // reference max of the last tile of each group, per row
+  __shared__ float lsum_s[2][BM];   // epilogue exchange: running sums and their references
+  __shared__ float mlast_s[2][BM];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int G = p.G, T = p.T;
@@ -597,227 +620,290 @@ __global__ void __launch_bounds__(C2_THREADS, 2)
   }
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sKV = smem + C::Q_BYTES;
+  uint8_t* sK = smem + C::Q_BYTES;
+  uint8_t* sV = sK + C::NK * C::SLOT_BYTES;
   volatile int* abort_flag = &bars.abort_flag;
   const int n_s = (p.S + BN - 1) / BN;
   const int n = n_s + (len_b + BN - 1) / BN;
 
   if (threadIdx.x == 0) {
     d3b::mbar_init(&bars.q_full, 1);
-    for (int i = 0; i < C::NSLOT; ++i) {
-      d3b::mbar_init(&bars.slot_full[i], 1);
-      d3b::mbar_init(&bars.slot_empty[i], 1);
+    for (int i = 0; i < 8; ++i) {
+      d3b::mbar_init(&bars.k_full[i], 1);
+      d3b::mbar_init(&bars.k_empty[i], 1);
+      d3b::mbar_init(&bars.v_full[i], 1);
+      d3b::mbar_init(&bars.v_empty[i], 1);
     }
-    d3b::mbar_init(&bars.s_full, 1);
-    d3b::mbar_init(&bars.p_full[0], 128);
-    d3b::mbar_init(&bars.p_full[1], 128);
+    for (int i = 0; i < 2; ++i) {
+      d3b::mbar_init(&bars.s_full[i], 1);
+      d3b::mbar_init(&bars.s_free[i], 128);
+      d3b::mbar_init(&bars.p_full[i], 128);
+      d3b::mbar_init(&bars.p_free[i], 1);
+      d3b::mbar_init(&bars.mdone[i], 128);
+    }
+    for (int q = 0; q < 4; ++q) d3b::mbar_init(&bars.xsum[q], 64);
     d3b::mbar_init(&bars.o_final, 1);
-    d3b::mbar_init(&bars.pv_done, 1);
-    d3b::mbar_init(&bars.drain, 1);
+    d3b::mbar_init(&bars.drain_qk, 1);
+    d3b::mbar_init(&bars.drain_pv, 1);
     bars.abort_flag = 0;
     d3b::fence_barrier_init();
   }
   if (rows_used < BM) {
     const int per_chunk = (BM - rows_used) * C::ROWB / 16;
-    for (int i = threadIdx.x; i < C::NCH * per_chunk; i += C2_THREADS) {
+    for (int i = threadIdx.x; i < C::NCH * per_chunk; i += DU_THREADS) {
       const int c = i / per_chunk, o = i % per_chunk;
       reinterpret_cast<uint4*>(sQ + c * C::Q_CHUNK + rows_used * C::ROWB)[o] = make_uint4(0, 0, 0, 0);
     }
     d3b::fence_proxy_async_smem();
   }
-  if (warp == 5) d3b::tmem_alloc(&bars.tmem_slot, C::TMEM_COLS);
+  if (warp == 9) d3b::tmem_alloc(&bars.tmem_slot, C::TMEM_COLS);
   d3b::tc_fence_before();
   __syncthreads();
   d3b::tc_fence_after();
   const uint32_t tmem_base = bars.tmem_slot;
+  constexpr uint32_t fmt = FP16 ? 0u : 1u;
 
-  if (warp == 4) {
-    // ================= TMA producer: Q, then K_0, V_0, K_1, V_1, ... =================
+  if (warp >= 8) {
+    // Registers: launched at 168 per thread (384 threads); the producer / MMA
+    // warpgroup gives back to 48 and the softmax warpgroups rise to 224
+    // (128 * 48 + 256 * 224 = 63488 <= 384 * 168), so a softmax thread keeps
+    // a whole 128-key row of S in registers.
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 48;" ::: "memory");
+   if (warp == 8 || warp == 11) {
+    // ================= TMA producers: warp 8 Q and K_0, K_1, ..., warp 11 V_0, V_1, ... =================
+    // (one producer per ring, so K tiles never wait behind a full V ring)
     if (lane == 0) {
-      d3b::tma_prefetch_desc(&mapQ);
-      d3b::tma_prefetch_desc(&mapKq);
-      d3b::tma_prefetch_desc(&mapVq);
-      if (n_s) {
-        d3b::tma_prefetch_desc(&mapKs);
-        d3b::tma_prefetch_desc(&mapVs);
+      const bool is_v = warp == 11;
+      if (is_v) {
+        if (n_s) d3b::tma_prefetch_desc(&mapVs);
+        d3b::tma_prefetch_desc(&mapVq);
+      } else {
+        d3b::tma_prefetch_desc(&mapQ);
+        d3b::tma_prefetch_desc(&mapKq);
+        if (n_s) d3b::tma_prefetch_desc(&mapKs);
+        d3b::mbar_arrive_expect_tx(&bars.q_full, C::NCH * rows_used * C::ROWB);
+#pragma unroll
+        for (int c = 0; c < C::NCH; ++c)
+          d3b::tma_load_4d(sQ + c * C::Q_CHUNK, &mapQ, &bars.q_full, c * C::CH, g * G, tok0, b);
       }
-      d3b::mbar_arrive_expect_tx(&bars.q_full, C::NCH * rows_used * C::ROWB);
-#pragma unroll
-      for (int c = 0; c < C::NCH; ++c)
-        d3b::tma_load_4d(sQ + c * C::Q_CHUNK, &mapQ, &bars.q_full, c * C::CH, g * G, tok0, b);
-      int stage = 0;
-      uint32_t phase = 0;
-      for (int i = 0; i < 2 * n; ++i) {
-        const int is_v = i & 1, j = i >> 1;
-        if (!d3b::mbar_wait(&bars.slot_empty[stage], phase ^ 1, abort_flag, p.err, kSite2CSlotEmpty)) break;
-        d3b::mbar_arrive_expect_tx(&bars.slot_full[stage], C::SLOT_BYTES);
-        uint8_t* dst = sKV + stage * C::SLOT_BYTES;
+      const int nslot = is_v ? C::NV : C::NK;
+      uint64_t* fulls = is_v ? bars.v_full : bars.k_full;
+      uint64_t* empties = is_v ? bars.v_empty : bars.k_empty;
+      uint8_t* ring = is_v ? sV : sK;
+      const CUtensorMap* m_state = is_v ? &mapVs : &mapKs;
+      const CUtensorMap* m_own = is_v ? &mapVq : &mapKq;
+      int slot = 0;
+      uint32_t ph = 0;
+      for (int j = 0; j < n; ++j) {
+        if (!d3b::mbar_wait(&empties[slot], ph ^ 1, abort_flag, p.err, kSiteDuSlotEmpty)) break;
+        uint64_t* full = &fulls[slot];
+        uint8_t* dst = ring + slot * C::SLOT_BYTES;
+        d3b::mbar_arrive_expect_tx(full, C::SLOT_BYTES);
         if (j < n_s) {
-          const CUtensorMap* m = is_v ? &mapVs : &mapKs;
 #pragma unroll
           for (int c = 0; c < C::NCH; ++c)
-            d3b::tma_load_3d(dst + c * C::SLOT_CHUNK, m, &bars.slot_full[stage], c * C::CH, j * BN, g);
+            d3b::tma_load_3d(dst + c * C::SLOT_CHUNK, m_state, full, c * C::CH, j * BN, g);
         } else {
-          const CUtensorMap* m = is_v ? &mapVq : &mapKq;
 #pragma unroll
           for (int c = 0; c < C::NCH; ++c)
-            d3b::tma_load_4d(dst + c * C::SLOT_CHUNK, m, &bars.slot_full[stage], c * C::CH, (j - n_s) * BN, g,
-                             b);
+            d3b::tma_load_4d(dst + c * C::SLOT_CHUNK, m_own, full, c * C::CH, (j - n_s) * BN, g, b);
         }
-        if (++stage == C::NSLOT) { stage = 0; phase ^= 1; }
+        if (++slot == nslot) { slot = 0; ph ^= 1; }
       }
     }
-  } else if (warp == 5) {
-    // ================= MMA issuer =================
+  } else if (warp == 9) {
+    // ================= QK^T issuer =================
     if (lane == 0) {
-      constexpr uint32_t fmt = FP16 ? 0u : 1u;
       constexpr uint32_t idesc_qk = d3b::make_idesc(1, fmt, fmt, 0, 0, BM, BN);
-      constexpr uint32_t idesc_pv = d3b::make_idesc(1, fmt, fmt, 0, 1, BM, D);
       const uint64_t dq0 = d3b::make_smem_desc(d3b::smem_u32(sQ), 16, C::SBO, C::LAYOUT);
-      const uint64_t dk0 = d3b::make_smem_desc(d3b::smem_u32(sKV), 16, C::SBO, C::LAYOUT);
-      const uint64_t dv0 = d3b::make_smem_desc(d3b::smem_u32(sKV), C::SLOT_CHUNK, C::SBO, C::LAYOUT);
-      auto slot_of = [&](int item) { return item % C::NSLOT; };
-      auto wait_item = [&](int item) -> bool {
-        return d3b::mbar_wait(&bars.slot_full[slot_of(item)], (uint32_t)(item / C::NSLOT) & 1, abort_flag, p.err,
-                              kSite2CSlotFull);
-      };
-      auto qk = [&](int item) {
-        const uint64_t dk = dk0 + (uint64_t)((slot_of(item) * C::SLOT_BYTES) >> 4);
+      const uint64_t dk0 = d3b::make_smem_desc(d3b::smem_u32(sK), 16, C::SBO, C::LAYOUT);
+      bool ok = d3b::mbar_wait(&bars.q_full, 0, abort_flag, p.err, kSiteDuQ);
+      for (int j = 0; j < n && ok; ++j) {
+        const int sb = j & 1;
+        const uint32_t u = (uint32_t)(j >> 1);
+        // S[sb] was last read by the softmax of tile j-2
+        if (!(ok = d3b::mbar_wait(&bars.s_free[sb], (u & 1) ^ 1, abort_flag, p.err, kSiteDuSFree))) break;
+        const int slot = j % C::NK;
+        if (!(ok = d3b::mbar_wait(&bars.k_full[slot], (uint32_t)(j / C::NK) & 1, abort_flag, p.err, kSiteDuSlotK)))
+          break;
+        d3b::tc_fence_after();
+        const uint64_t dk = dk0 + (uint64_t)((slot * C::SLOT_BYTES) >> 4);
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
           const int c = (k * 16) / C::CH, off = ((k * 16) % C::CH) * 2;
-          d3b::mma_f16_ss(tmem_base + C::COL_S, dq0 + (uint64_t)((c * C::Q_CHUNK + off) >> 4),
+          d3b::mma_f16_ss(tmem_base + C::COL_S + sb * BN, dq0 + (uint64_t)((c * C::Q_CHUNK + off) >> 4),
                           dk + (uint64_t)((c * C::SLOT_CHUNK + off) >> 4), idesc_qk, k > 0 ? 1u : 0u);
         }
-        d3b::mma_commit(&bars.s_full);
-      };
-      // O (+)= P V, the half with keys 64-127 first (the softmax publishes it first)
-      auto pv = [&](int item, bool accumulate, uint32_t use) -> bool {
-        const uint64_t dv = dv0 + (uint64_t)((slot_of(item) * C::SLOT_BYTES) >> 4);
-        const uint32_t a_tmem = tmem_base + C::COL_S + BN / 2;
-        bool first = true;
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int h = 1 - hh;
-          if (!d3b::mbar_wait(&bars.p_full[h], use & 1, abort_flag, p.err, kSite2CPFull)) return false;
-          d3b::tc_fence_after();
-#pragma unroll
-          for (int k = h * BN / 32; k < (h + 1) * BN / 32; ++k) {
-            d3b::mma_f16_ts(tmem_base + C::COL_O, a_tmem + k * 8, dv + (uint64_t)((k * 16 * C::ROWB) >> 4),
-                            idesc_pv, (accumulate || !first) ? 1u : 0u);
-            first = false;
-          }
-        }
-        return true;
-      };
-      bool ok = d3b::mbar_wait(&bars.q_full, 0, abort_flag, p.err, kSite2CQ);
-      if (ok && (ok = wait_item(0))) {
-        d3b::tc_fence_after();
-        qk(0);
-        d3b::mma_commit(&bars.slot_empty[slot_of(0)]);
+        d3b::mma_commit(&bars.s_full[sb]);
+        d3b::mma_commit(&bars.k_empty[slot]);
       }
-      for (int j = 0; j < n && ok; ++j) {
-        const int it_v = 2 * j + 1;
-        if (!(ok = wait_item(it_v))) break;
-        if (!(ok = pv(it_v, j > 0, (uint32_t)j))) break;
-        d3b::mma_commit(&bars.slot_empty[slot_of(it_v)]);
-        if (j + 1 < n) {  // QK(j+1): in issue order after PV(j), which read P from S
-          const int it_k = 2 * (j + 1);
-          if (D3B_STRICT_MMA_ORDER) {
-            d3b::mma_commit(&bars.pv_done);
-            if (!(ok = d3b::mbar_wait(&bars.pv_done, (uint32_t)(j & 1), abort_flag, p.err, kSite2CPvDone))) break;
-          }
-          if (!(ok = wait_item(it_k))) break;
-          d3b::tc_fence_after();
-          qk(it_k);
-          d3b::mma_commit(&bars.slot_empty[slot_of(it_k)]);
-        }
-      }
-      if (ok) d3b::mma_commit(&bars.o_final);
-      d3b::mma_commit(&bars.drain);
-      const uint32_t addr = d3b::smem_u32(&bars.drain);
+      d3b::mma_commit(&bars.drain_qk);
+      const uint32_t addr = d3b::smem_u32(&bars.drain_qk);
       const uint64_t t0 = d3b::globaltimer_ns();
       while (!d3b::mbar_try_wait(addr, 0)) {
         if (d3b::globaltimer_ns() - t0 > D3B_WAIT_LIMIT_NS) {
-          d3b::record_device_error(p.err, kSite2CDrain);
+          d3b::record_device_error(p.err, kSiteDuDrain);
           break;
         }
       }
     }
-  } else {
-    // ================= softmax + epilogue (warps 0-3) =================
-    const int quarter = warp;
-    const int r = quarter * 32 + lane;
-    const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
-    const uint32_t col_s = C::COL_S, col_p = C::COL_S + BN / 2, col_o = C::COL_O;
-    const float sl2 = p.scale_log2;
-    float m_ref = -INFINITY, l_sum = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n; ++j) {
-      if (!d3b::warp_wait(&bars.s_full, (uint32_t)(j & 1), abort_flag, p.err, kSite2CSFull)) { ok = false; break; }
-      d3b::tc_fence_after();
-      const int valid = j < n_s ? p.S - j * BN : len_b - (j - n_s) * BN;
-      float s[64];
-      load64(lane_addr + col_s, 0, valid, s);
-      const float m_lo = max_n<64>(s);
-      load64(lane_addr + col_s + 64, 64, valid, s);  // keys 64-127 stay in registers
-      const float m_tile = fmaxf(m_lo, max_n<64>(s)) * sl2;
-      const bool rescale = __any_sync(0xffffffffu, m_tile > m_ref + kRescaleThreshold);
-      const float m_new = rescale ? fmaxf(m_ref, m_tile) : m_ref;
-      const float alpha = rescale ? d3b::ex2_approx(m_ref - m_new) : 1.f;
-      if (rescale && j > 0) {
-        // s_full(j) is a commit issued after PV(j-1): O is complete here
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          d3b::tmem_ld32(lane_addr + col_o + c * 32, o);
-          d3b::tmem_wait_ld();
+  } else if (warp == 10) {
+    // ================= PV issuer =================
+    if (lane == 0) {
+      constexpr uint32_t idesc_pv = d3b::make_idesc(1, fmt, fmt, 0, 1, BM, D);
+      const uint64_t dv0 = d3b::make_smem_desc(d3b::smem_u32(sV), C::SLOT_CHUNK, C::SBO, C::LAYOUT);
+      bool ok = true;
+      for (int j = 0; j < n && ok; ++j) {
+        const int sb = j & 1;
+        const uint32_t u = (uint32_t)(j >> 1);
+        if (!(ok = d3b::mbar_wait(&bars.p_full[sb], u & 1, abort_flag, p.err, kSiteDuPFull))) break;
+        const int slot = j % C::NV;
+        if (!(ok = d3b::mbar_wait(&bars.v_full[slot], (uint32_t)(j / C::NV) & 1, abort_flag, p.err, kSiteDuSlotV)))
+          break;
+        d3b::tc_fence_after();
+        const uint64_t dv = dv0 + (uint64_t)((slot * C::SLOT_BYTES) >> 4);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          d3b::tmem_st32(lane_addr + col_o + c * 32, o);
+        for (int k = 0; k < BN / 16; ++k)
+          d3b::mma_f16_ts(tmem_base + C::COL_O, tmem_base + C::COL_P + sb * (BN / 2) + k * 8,
+                          dv + (uint64_t)((k * 16 * C::ROWB) >> 4), idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+        d3b::mma_commit(&bars.p_free[sb]);
+        d3b::mma_commit(&bars.v_empty[slot]);
+      }
+      if (ok) d3b::mma_commit(&bars.o_final);
+      d3b::mma_commit(&bars.drain_pv);
+      const uint32_t addr = d3b::smem_u32(&bars.drain_pv);
+      const uint64_t t0 = d3b::globaltimer_ns();
+      while (!d3b::mbar_try_wait(addr, 0)) {
+        if (d3b::globaltimer_ns() - t0 > D3B_WAIT_LIMIT_NS) {
+          d3b::record_device_error(p.err, kSiteDuDrain);
+          break;
         }
       }
-      // P into the upper half of S (whose values are all in registers), keys
-      // 64-127 first: the MMA thread consumes that half first.
-      uint32_t pk[32];
-      // keys 64-127 -> P columns 32-63 (S columns 96-127, held in registers)
-      float rowsum = exp_row<64, FP16>(s, sl2, m_new, pk);
-      d3b::tmem_st32(lane_addr + col_p + 32, pk);
-      d3b::tmem_wait_st();
-      d3b::tc_fence_before();
-      d3b::mbar_arrive(&bars.p_full[1]);
-      // keys 0-63 (reloaded) -> P columns 0-31 (S columns 64-95, consumed above)
-      load64(lane_addr + col_s, 0, valid, s);
-      rowsum += exp_row<64, FP16>(s, sl2, m_new, pk);
-      d3b::tmem_st32(lane_addr + col_p, pk);
-      d3b::tmem_wait_st();
-      d3b::tc_fence_before();
-      d3b::mbar_arrive(&bars.p_full[0]);
-      l_sum = l_sum * alpha + rowsum;
-      m_ref = m_new;
     }
-    if (ok) ok = d3b::warp_wait(&bars.o_final, 0, abort_flag, p.err, kSite2CFinal);
+   }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory");
+    // ================= softmax + epilogue (warps 0-7) =================
+    // Group wg (warps 4wg .. 4wg+3, one thread per row) takes the key tiles
+    // j = wg, wg+2, ... with S[wg] and P[wg]. Both groups scale P by the same
+    // per-row reference max, decided tile by tile in order: tile j reads the
+    // reference of tile j-1 (from the other group, through shared memory),
+    // raises it only if its own max exceeds it by more than 2^8, and publishes
+    // its own. Each group keeps its own running sum l (with the reference of
+    // its last tile); the two are combined in the epilogue.
+    const int wg = warp >> 2, quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
+    const uint32_t col_s = C::COL_S + wg * BN, col_p = C::COL_P + wg * (BN / 2);
+    const float sl2 = p.scale_log2;
+    float m_last = -INFINITY, l_sum = 0.f;
+    bool ok = true;
+    for (int j = wg; j < n && ok; j += 2) {
+      const uint32_t u = (uint32_t)(j >> 1);
+      if (!d3b::warp_wait(&bars.s_full[wg], u & 1, abort_flag, p.err, kSiteDuSFull)) { ok = false; break; }
+      d3b::tc_fence_after();
+      float s[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c)
+        d3b::tmem_ld32(lane_addr + col_s + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
+      d3b::tmem_wait_ld();
+      d3b::tc_fence_before();
+      d3b::mbar_arrive(&bars.s_free[wg]);
+      const int valid = j < n_s ? p.S - j * BN : len_b - (j - n_s) * BN;
+      if (valid < BN) {
+#pragma unroll
+        for (int c = 0; c < BN; ++c)
+          if (c >= valid) s[c] = -INFINITY;
+      }
+      const float m_tile = max_n<BN>(s) * sl2;
+      float m_prev = -INFINITY;
+      if (j > 0) {
+        if (!d3b::warp_wait(&bars.mdone[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1, abort_flag, p.err, kSiteDuXMax)) {
+          ok = false;
+          break;
+        }
+        m_prev = mref_s[(j - 1) & 1][r];
+      }
+      // Lazy rescale, decided per warp: tcgen05.ld/st are warp-collective.
+      const bool rescale = __any_sync(0xffffffffu, m_tile > m_prev + kRescaleThreshold);
+      const float m_new = rescale ? fmaxf(m_prev, m_tile) : m_prev;
+      mref_s[wg][r] = m_new;
+      d3b::mbar_arrive(&bars.mdone[wg]);
+      if (rescale && j > 0) {
+        // O holds PV(0..j-1) scaled to m_prev: wait for PV(j-1), then rescale
+        if (!d3b::warp_wait(&bars.p_free[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1, abort_flag, p.err,
+                            kSiteDuPFree)) {
+          ok = false;
+          break;
+        }
+        d3b::tc_fence_after();
+        scale_cols<D>(lane_addr + C::COL_O, d3b::ex2_approx(m_prev - m_new));
+      }
+      // P[wg] is free once PV(j-2) has completed
+      if (!d3b::warp_wait(&bars.p_free[wg], (u & 1) ^ 1, abort_flag, p.err, kSiteDuPFree)) { ok = false; break; }
+      d3b::tc_fence_after();
+      float rowsum = 0.f;
+#pragma unroll
+      for (int qq = 0; qq < BN / 32; ++qq) {
+        uint32_t pk[16];
+        rowsum += exp_row<32, FP16, D3B_POLY8>(s + qq * 32, sl2, m_new, pk);
+        d3b::tmem_st16(lane_addr + col_p + qq * 16, pk);
+      }
+      d3b::tmem_wait_st();
+      d3b::tc_fence_before();
+      d3b::mbar_arrive(&bars.p_full[wg]);
+      l_sum = (m_last == m_new ? l_sum : l_sum * d3b::ex2_approx(m_last - m_new)) + rowsum;
+      m_last = m_new;
+    }
+    if (ok) ok = d3b::warp_wait(&bars.o_final, 0, abort_flag, p.err, kSiteDuFinal);
+    if (ok) {
+      lsum_s[wg][r] = l_sum;
+      mlast_s[wg][r] = m_last;
+      d3b::mbar_arrive(&bars.xsum[quarter]);
+      ok = d3b::warp_wait(&bars.xsum[quarter], 0, abort_flag, p.err, kSiteDuXMax);
+    }
     if (ok) {
       d3b::tc_fence_after();
+      // O is scaled to the last tile's reference, the larger of the two groups' last references
+      const float m0 = mlast_s[0][r], m1 = mlast_s[1][r];
+      const float m_fin = fmaxf(m0, m1);
+      const float l = lsum_s[0][r] * d3b::ex2_approx(m0 - m_fin) + lsum_s[1][r] * d3b::ex2_approx(m1 - m_fin);
       const int tok = tok0 + r / G, h = r % G;
       const bool in_tensor = r < rows_used && tok < p.L;
       const bool real = tok < len_b;
-      const float inv_l = 1.f / l_sum;
+      const float inv_l = 1.f / l;
+      // each group normalises and stores half of the D columns
       uint16_t* dst_row = static_cast<uint16_t*>(p.out) + (int64_t)b * p.out_sb + (int64_t)(g * G + h) * p.out_sh +
-                          (int64_t)tok * p.out_sl;
+                          (int64_t)tok * p.out_sl + wg * C::OH;
+      if constexpr (C::OH % 32 == 0) {
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        d3b::tmem_ld32(lane_addr + col_o + c * 32, o);
+        for (int c = 0; c < C::OH / 32; ++c) {
+          uint32_t o[32];
+          d3b::tmem_ld32(lane_addr + C::COL_O + wg * C::OH + c * 32, o);
+          d3b::tmem_wait_ld();
+          if (in_tensor) {
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              w[i] = real ? pack2<FP16>(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l)
+                          : 0u;
+            uint4* dst = reinterpret_cast<uint4*>(dst_row + c * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          }
+        }
+      } else {
+        uint32_t o[16];
+        d3b::tmem_ld16(lane_addr + C::COL_O + wg * C::OH, o);
         d3b::tmem_wait_ld();
         if (in_tensor) {
-          uint32_t w[16];
+          uint32_t w[8];
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
+          for (int i = 0; i < 8; ++i)
             w[i] = real ? pack2<FP16>(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l) : 0u;
-          uint4* dst = reinterpret_cast<uint4*>(dst_row + c * 32);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          uint4* dst = reinterpret_cast<uint4*>(dst_row);
+          dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
         }
       }
     }
@@ -826,22 +912,22 @@ __global__ void __launch_bounds__(C2_THREADS, 2)
   d3b::tc_fence_before();
   __syncthreads();
   d3b::tc_fence_after();
-  if (warp == 5) d3b::tmem_dealloc(tmem_base, C::TMEM_COLS);
+  if (warp == 9) d3b::tmem_dealloc(tmem_base, C::TMEM_COLS);
 }
 
 template <int D, int FP16>
-int launch_2c(const CUtensorMap* maps, const Params& prm, dim3 grid, cudaStream_t stream) {
-  using C = Cfg2C<D>;
+int launch_dual(const CUtensorMap* maps, const Params& prm, dim3 grid, cudaStream_t stream) {
+  using C = CfgDual<D>;
   static int attr_set[64] = {0};
   const int dev = d3b_host::current_device();
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(prefix_bidir_2c_kernel<D, FP16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(prefix_bidir_dual_kernel<D, FP16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::SMEM_BYTES) != cudaSuccess)
       return D3B_ECUDA;
     attr_set[dev] = 1;
   }
-  prefix_bidir_2c_kernel<D, FP16><<<grid, C2_THREADS, C::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3],
-                                                                             maps[4], prm);
+  prefix_bidir_dual_kernel<D, FP16><<<grid, DU_THREADS, C::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2],
+                                                                                maps[3], maps[4], prm);
   return d3b_host::check_launch();
 }
 
@@ -865,11 +951,11 @@ template <int FP16>
 int dispatch(int D, const CUtensorMap* maps, const Params& prm, dim3 grid, cudaStream_t s) {
   // D = 256 (O needs 256 TMEM columns): one tile per CTA, one CTA per SM.
   if (D == 256) return launch<256, 64, FP16>(maps, prm, grid, s);
-  // D <= 128: one tile per CTA, two CTAs per SM.
+  // D <= 128: one tile per CTA, one CTA per SM, two MMA-issuing threads.
   switch (D) {
-    case 32: return launch_2c<32, FP16>(maps, prm, grid, s);
-    case 64: return launch_2c<64, FP16>(maps, prm, grid, s);
-    case 128: return launch_2c<128, FP16>(maps, prm, grid, s);
+    case 32: return launch_dual<32, FP16>(maps, prm, grid, s);
+    case 64: return launch_dual<64, FP16>(maps, prm, grid, s);
+    case 128: return launch_dual<128, FP16>(maps, prm, grid, s);
   }
   return D3B_EUNSUPPORTED;
 }
