@@ -1,11 +1,14 @@
 // Per-token activation quantisation (d3trt/model/quant.py:92-100) and, on a
 // weight matrix, per-output-channel weight quantisation (quant.py:77-89).
 //
-// One warp owns one row (8 warps per CTA, so many rows per SM are in flight).
-// Pass 1 reads the row with 16-byte loads (batches of 8 per lane in flight) and reduces max|x| with warp shuffles; pass 2 re-reads the
-// row, which the first pass has just brought into L2, and writes the 8-bit
-// codes with 8-byte stores. HBM traffic is the algorithmic minimum: read x
-// once, write q and the scale.
+// One warp owns one row. bf16 rows up to 6144 elements (the model's hidden
+// and attention widths) are read once into registers (all of a lane's 16-byte
+// loads in flight together), reduced and quantised from there. Longer rows
+// (and f16/f32 input) take two passes: pass 1 reads the row with 16-byte loads
+// (batches of 8 per lane in flight) and reduces max|x| with warp shuffles;
+// pass 2 re-reads the row, which the first pass has just brought into L2, and
+// writes the 8-bit codes with 8-byte stores. HBM traffic is the algorithmic
+// minimum either way: read x once, write q and the scale.
 //
 // Bit-exactness with the reference formulas:
 //   amax  = max(max_k |x|, 1e-12f)                (fp32, order independent)
@@ -13,13 +16,13 @@
 //   fp8 : q = e4m3fn(clamp(x / scale, -448, 448))   cvt.rn.satfinite = RNE
 //   int8: q = int8(clamp(rint(x / scale), -127, 127))  rint = half-to-even
 // x / scale must be the IEEE quotient RN(x / scale). Per element the kernel
-// first forms v = RN(x * RN(1 / scale)), which is within 1.5 ulp of x / scale.
-// The code only depends on which side of a rounding boundary of the target
-// format (an e4m3 midpoint, or k + 1/2 for int8) the quotient lies; when v is
-// 4 ulp or more away from every boundary, v and RN(x / scale) give the same
-// code. Otherwise (and for every |v| in the e4m3 subnormal range) the element
-// is recomputed with __fdiv_rn (IEEE). So the codes equal those of the
-// reference's IEEE division in every case.
+// forms v = RN(x * RN(1 / scale)) and converts v shrunk and grown by 2^-21
+// relative; when both give the same code, so does RN(x / scale) (rounding is
+// monotone and the bracket covers the error of v). Otherwise (about one pair
+// in 10^5 on N(0,1) data) the pair is recomputed with __fdiv_rn (IEEE). So the
+// codes equal those of the reference's IEEE division in every case.
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace {
@@ -73,40 +76,95 @@ __device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
   return r;
 }
 
-// The exact IEEE quotient, out of line so the compiler cannot evaluate it
-// speculatively for every element: it runs only for the rare elements whose
-// fast quotient lies next to a rounding boundary.
-__device__ __noinline__ float exact_quotient(float x, float scale) { return __fdiv_rn(x, scale); }
-
-// RN(x / scale), given rcp = RN(1 / scale): the fast product unless it may sit
-// within 4 ulp of a rounding boundary of the target format.
+// Two codes from two quotients (already in the target's range or not: the
+// fp8 conversion saturates to +-448 like the reference's clamp, int8 clamps).
 template <int MODE>
-__device__ __forceinline__ float quotient(float x, float scale, float rcp) {
-  const float v = __fmul_rn(x, rcp);
-  bool near;
-  if (MODE == D3B_MODE_FP8) {
-    const float a = fminf(fabsf(v), 448.f);
-    // e4m3 normals keep 3 mantissa bits: a tie has dropped bits == 0x80000
-    const int dropped = static_cast<int>(__float_as_uint(a) & 0xFFFFFu);
-    near = (a < 0.015625f) || (abs(dropped - 0x80000) <= 4);
-  } else {
-    const float a = fminf(fabsf(v), 127.f);
-    near = fabsf(a - floorf(a) - 0.5f) <= 1.0f / 32768.f;  // 4 ulp at |v| < 128
-  }
-  if (__builtin_expect(near, 0)) return exact_quotient(x, scale);
-  return v;
+__device__ __forceinline__ uint32_t codes2(float v0, float v1) {
+  if (MODE == D3B_MODE_FP8) return e4m3x2(v0, v1);
+  const int i0 = min(max(__float2int_rn(v0), -127), 127);
+  const int i1 = min(max(__float2int_rn(v1), -127), 127);
+  return (static_cast<uint32_t>(i0) & 0xFFu) | ((static_cast<uint32_t>(i1) & 0xFFu) << 8);
 }
 
+// The codes of the exact IEEE quotients, out of line: it runs only for the
+// rare pairs whose fast quotient lies next to a rounding boundary.
+template <int MODE>
+__device__ __noinline__ uint32_t exact_codes2(float x0, float x1, float scale) {
+  float v0 = __fdiv_rn(x0, scale), v1 = __fdiv_rn(x1, scale);
+  if (MODE == D3B_MODE_FP8) {
+    v0 = fminf(fmaxf(v0, -448.f), 448.f);
+    v1 = fminf(fmaxf(v1, -448.f), 448.f);
+  }
+  return codes2<MODE>(v0, v1);
+}
+
+// Codes of RN(x / scale) for two elements, given rcp = RN(1 / scale).
+// v = RN(x * rcp) is within 1.5 * 2^-23 |v| of RN(x / scale). Rounding to the
+// target format is monotone, so if v * (1 - 2^-21) and v * (1 + 2^-21) (each
+// still at least 1.75 * 2^-22 |v| away from v after rounding) give the same
+// code, every value between them does, RN(x / scale) included. Otherwise the
+// pair is recomputed with IEEE division.
 template <int MODE>
 __device__ __forceinline__ uint32_t quant2(float x0, float x1, float scale, float rcp) {
-  const float v0 = quotient<MODE>(x0, scale, rcp), v1 = quotient<MODE>(x1, scale, rcp);
+  constexpr float kLo = 1.0f - 0x1p-21f, kHi = 1.0f + 0x1p-21f;
+  const float v0 = __fmul_rn(x0, rcp), v1 = __fmul_rn(x1, rcp);
+  const uint32_t lo = codes2<MODE>(__fmul_rn(v0, kLo), __fmul_rn(v1, kLo));
+  const uint32_t hi = codes2<MODE>(__fmul_rn(v0, kHi), __fmul_rn(v1, kHi));
+  if (__builtin_expect(lo == hi, 1)) return lo;
+  return exact_codes2<MODE>(x0, x1, scale);
+}
+
+// ---- bf16 rows: packed arithmetic (the common case) ----
+// Non-negative bf16 bit patterns order like unsigned integers, so max|x| of a
+// pair word is a packed u16 max of (w & 0x7FFF7FFF).
+__device__ __forceinline__ uint32_t umax2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+// (d0, d1) = (a0, a1) * (b, b), one packed fp32x2 multiply, round to nearest
+__device__ __forceinline__ void mul2(float& d0, float& d1, float a0, float a1, float b) {
+  asm("{.reg .b64 x, y; mov.b64 x, {%2, %3}; mov.b64 y, {%4, %4}; mul.rn.f32x2 x, x, y; mov.b64 {%0, %1}, x;}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b));
+}
+// The bracket codes (see quant2) of one word of two bf16 values.
+template <int MODE>
+__device__ __forceinline__ void pair_codes(uint32_t w, float rcp, uint32_t& lo, uint32_t& hi) {
+  constexpr float kLo = 1.0f - 0x1p-21f, kHi = 1.0f + 0x1p-21f;
+  float v0, v1, l0, l1, h0, h1;
+  mul2(v0, v1, __uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u), rcp);
+  mul2(l0, l1, v0, v1, kLo);
+  mul2(h0, h1, v0, v1, kHi);
   if (MODE == D3B_MODE_FP8) {
-    return e4m3x2(fminf(fmaxf(v0, -448.f), 448.f), fminf(fmaxf(v1, -448.f), 448.f));
+    lo = e4m3x2(l0, l1);
+    hi = e4m3x2(h0, h1);
   } else {
-    const int i0 = min(max(__float2int_rn(v0), -127), 127);
-    const int i1 = min(max(__float2int_rn(v1), -127), 127);
-    return (static_cast<uint32_t>(i0) & 0xFFu) | ((static_cast<uint32_t>(i1) & 0xFFu) << 8);
+    // |v| <= 127 (1 + 2^-21) because |x| <= amax: the reference's clamp to
+    // +-127 never changes a code here
+    lo = (static_cast<uint32_t>(__float2int_rn(l0)) & 0xFFu) | ((static_cast<uint32_t>(__float2int_rn(l1)) & 0xFFu) << 8);
+    hi = (static_cast<uint32_t>(__float2int_rn(h0)) & 0xFFu) | ((static_cast<uint32_t>(__float2int_rn(h1)) & 0xFFu) << 8);
   }
+}
+template <int MODE>
+__device__ __noinline__ uint2 exact_codes8_bf16(uint4 raw, float scale) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  uint32_t c[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) c[i] = exact_codes2<MODE>(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u), scale);
+  return make_uint2(c[0] | (c[1] << 16), c[2] | (c[3] << 16));
+}
+// Eight codes of eight bf16 values (one 16-byte load -> one 8-byte store).
+template <int MODE>
+__device__ __forceinline__ uint2 quant8_bf16(uint4 raw, float scale, float rcp) {
+  uint32_t l0, l1, l2, l3, h0, h1, h2, h3;
+  pair_codes<MODE>(raw.x, rcp, l0, h0);
+  pair_codes<MODE>(raw.y, rcp, l1, h1);
+  pair_codes<MODE>(raw.z, rcp, l2, h2);
+  pair_codes<MODE>(raw.w, rcp, l3, h3);
+  const uint32_t w0 = l0 | (l1 << 16), w1 = l2 | (l3 << 16);
+  if (__builtin_expect((w0 == (h0 | (h1 << 16))) & (w1 == (h2 | (h3 << 16))), 1)) return make_uint2(w0, w1);
+  return exact_codes8_bf16<MODE>(raw, scale);
 }
 
 __device__ __forceinline__ float row_scale(float amax, int mode) {
@@ -149,8 +207,10 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) act_quant_kernel(const T* _
   if (VEC) {
     // batches of kBatch 16-byte loads per lane, all issued before any use
     constexpr int kBatch = 8;
+    constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
     const uint4* src = reinterpret_cast<const uint4*>(xr);
     const int nvec = static_cast<int>(K / VN);
+    uint32_t m0 = 0, m1 = 0;  // bf16: packed max |x|
     for (int k0 = lane; k0 < nvec; k0 += 32 * kBatch) {
       uint4 raw[kBatch];
 #pragma unroll
@@ -158,11 +218,22 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) act_quant_kernel(const T* _
         raw[u] = k0 + 32 * u < nvec ? __ldg(src + k0 + 32 * u) : make_uint4(0, 0, 0, 0);
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) {
-        float v[8];
-        Vec<T>::unpack(raw[u], v);
+        if constexpr (kBf16) {
+          m0 = umax2(m0, raw[u].x & 0x7FFF7FFFu);
+          m1 = umax2(m1, raw[u].y & 0x7FFF7FFFu);
+          m0 = umax2(m0, raw[u].z & 0x7FFF7FFFu);
+          m1 = umax2(m1, raw[u].w & 0x7FFF7FFFu);
+        } else {
+          float v[8];
+          Vec<T>::unpack(raw[u], v);
 #pragma unroll
-        for (int e = 0; e < VN; ++e) amax = fmaxf(amax, fabsf(v[e]));
+          for (int e = 0; e < VN; ++e) amax = fmaxf(amax, fabsf(v[e]));
+        }
       }
+    }
+    if constexpr (kBf16) {
+      const uint32_t m = umax2(m0, m1);
+      amax = __uint_as_float(max(m & 0xFFFFu, m >> 16) << 16);
     }
     const float scale = row_scale(amax, MODE);
     const float rcp = __frcp_rn(scale);
@@ -174,7 +245,12 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) act_quant_kernel(const T* _
         if (k0 + 32 * u < nvec) raw[u] = __ldg(src + k0 + 32 * u);
 #pragma unroll
       for (int u = 0; u < kBatch; ++u)
-        if (k0 + 32 * u < nvec) quant_vec<T, MODE>(raw[u], scale, rcp, qr + (int64_t)(k0 + 32 * u) * VN);
+        if (k0 + 32 * u < nvec) {
+          if constexpr (kBf16)
+            *reinterpret_cast<uint2*>(qr + (int64_t)(k0 + 32 * u) * VN) = quant8_bf16<MODE>(raw[u], scale, rcp);
+          else
+            quant_vec<T, MODE>(raw[u], scale, rcp, qr + (int64_t)(k0 + 32 * u) * VN);
+        }
     }
   } else {
     for (int64_t k = lane; k < K; k += 32) amax = fmaxf(amax, fabsf(to_f32(xr[k])));
@@ -186,12 +262,70 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) act_quant_kernel(const T* _
   }
 }
 
+// ---------------------------------------------------------------------------
+// bf16 rows with K <= 32 * 8 * NV: one pass, the row held in registers. Each
+// lane issues all of its NV 16-byte loads at once (one memory round trip per
+// row), reduces max|x|, and writes the codes from the same registers.
+// ---------------------------------------------------------------------------
+constexpr int kRegWarps = 4;  // warps (rows) per CTA
+
+template <int MODE, int NV>
+__global__ void __launch_bounds__(kRegWarps * 32) act_quant_reg_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                        int64_t ldx, uint8_t* __restrict__ q,
+                                                                        float* __restrict__ scale_out, int64_t M,
+                                                                        int64_t K) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kRegWarps + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const uint4* src = reinterpret_cast<const uint4*>(x + row * ldx);
+  uint8_t* qr = q + row * K;
+  const int nvec = static_cast<int>(K / 8);
+  uint4 raw[NV];
+#pragma unroll
+  for (int u = 0; u < NV; ++u)
+    raw[u] = lane + 32 * u < nvec ? __ldg(src + lane + 32 * u) : make_uint4(0, 0, 0, 0);
+  uint32_t m0 = 0, m1 = 0;
+#pragma unroll
+  for (int u = 0; u < NV; ++u) {
+    m0 = umax2(m0, raw[u].x & 0x7FFF7FFFu);
+    m1 = umax2(m1, raw[u].y & 0x7FFF7FFFu);
+    m0 = umax2(m0, raw[u].z & 0x7FFF7FFFu);
+    m1 = umax2(m1, raw[u].w & 0x7FFF7FFFu);
+  }
+  const uint32_t m = umax2(m0, m1);
+  const float scale = row_scale(__uint_as_float(max(m & 0xFFFFu, m >> 16) << 16), MODE);
+  const float rcp = __frcp_rn(scale);
+  if (lane == 0) scale_out[row] = scale;
+#pragma unroll
+  for (int u = 0; u < NV; ++u)
+    if (lane + 32 * u < nvec)
+      *reinterpret_cast<uint2*>(qr + (int64_t)(lane + 32 * u) * 8) = quant8_bf16<MODE>(raw[u], scale, rcp);
+}
+
+template <int NV>
+void launch_reg(const __nv_bfloat16* x, int64_t ldx, uint8_t* q, float* scale, int64_t M, int64_t K, int mode,
+                cudaStream_t stream) {
+  const dim3 grid((unsigned)((M + kRegWarps - 1) / kRegWarps)), block(kRegWarps * 32);
+  if (mode == D3B_MODE_FP8) act_quant_reg_kernel<D3B_MODE_FP8, NV><<<grid, block, 0, stream>>>(x, ldx, q, scale, M, K);
+  else act_quant_reg_kernel<D3B_MODE_INT8, NV><<<grid, block, 0, stream>>>(x, ldx, q, scale, M, K);
+}
+
 template <typename T>
 int launch_typed(const void* x, int64_t ldx, void* q, float* scale, int64_t M, int64_t K, int mode,
                  cudaStream_t stream) {
   const int64_t elem = sizeof(T);
   const bool vec = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((ldx * elem) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(q) % 16 == 0) && (K % 8 == 0);
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    if (vec && K <= 32 * 8 * 24 && (M + kRegWarps - 1) / kRegWarps <= 0x7FFFFFFF) {
+      const auto* xb = static_cast<const __nv_bfloat16*>(x);
+      auto* qb = static_cast<uint8_t*>(q);
+      if (K <= 32 * 8 * 16) launch_reg<16>(xb, ldx, qb, scale, M, K, mode, stream);
+      else if (K <= 32 * 8 * 20) launch_reg<20>(xb, ldx, qb, scale, M, K, mode, stream);
+      else launch_reg<24>(xb, ldx, qb, scale, M, K, mode, stream);
+      return d3b_host::check_launch();
+    }
+  }
   const int64_t blocks = (M + kWarpsPerCta - 1) / kWarpsPerCta;
   if (blocks > 0x7FFFFFFF) return D3B_EINVAL;
   const dim3 grid((unsigned)blocks), block(kWarpsPerCta * 32);

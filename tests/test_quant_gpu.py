@@ -53,6 +53,22 @@ def test_act_quant_cfg2_bit_exact(mode, dtype):
     assert np.array_equal(_codes(q), rq.view(np.uint8))
 
 
+@pytest.mark.parametrize("k", [8, 4096, 5120, 5128, 6144, 6152, 17408])
+def test_act_quant_bf16_row_lengths_bit_exact(k):
+    """bf16 rows up to 6144 wide go through the one-pass register kernel (three
+    sizes of it), longer rows through the two-pass kernel; a padded row pitch
+    exercises both with ldx > K."""
+    x = _cfg2_activations(rows=67, k=k, seed=k)
+    padded = torch.zeros(67, k + 64, dtype=torch.bfloat16)
+    padded[:, :k] = x
+    for src in (x.to(DEV), padded.to(DEV)[:, :k]):
+        for mode in ("fp8", "int8"):
+            q, s = quant.quantize_rows(src, mode)
+            rq, rs = oq.quantize_rows(x.float().numpy(), mode)
+            assert np.array_equal(s.cpu().numpy(), rs)
+            assert np.array_equal(_codes(q), rq.view(np.uint8))
+
+
 def test_act_quant_strided_rows_and_zero_row():
     base = torch.randn(33, 200, dtype=torch.bfloat16)
     base[7] = 0
