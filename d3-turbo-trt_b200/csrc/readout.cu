@@ -16,6 +16,7 @@
 // Workspace layout: [tickets: kMaxGroups x u32 at offset 0][logits: B x n_opt f32].
 // The ticket region never moves, so one zero-filled workspace serves calls of
 // any shape (B <= 8 * kMaxGroups).
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -59,6 +60,71 @@ __device__ __forceinline__ int unpack16(uint4 a, const __half*, float (&v)[8]) {
 __device__ __forceinline__ float load_h(const float* p) { return __ldg(p); }
 __device__ __forceinline__ float load_h(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 __device__ __forceinline__ float load_h(const __half* p) { return __half2float(*p); }
+
+// Masked softmax of NR rows of logits (one warp, rows row0 .. row0+NR-1,
+// handled together so their loads and reductions overlap):
+// logits[j >= counts[row]] = -inf, probs = softmax(logits / temperature); a row
+// with count <= 0 is all NaN, as the reference's softmax of an all -inf row.
+// PER = values per lane (n_opt <= 32 * PER).
+template <int PER, int NR>
+__device__ __forceinline__ void rows_softmax(int row0, int B, int n_opt, const int32_t* __restrict__ counts,
+                                             float temperature, const float* logits, float* __restrict__ probs,
+                                             int lane) {
+  float v[NR][PER];
+  float mx[NR], sum[NR];
+  int cnt[NR];
+#pragma unroll
+  for (int q = 0; q < NR; ++q) {
+    const int row = row0 + q;
+    cnt[q] = row < B ? counts[row] : 0;
+    mx[q] = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int j = lane + 32 * i;
+      float x = -INFINITY;
+      if (row < B && j < n_opt && j < cnt[q]) x = __ldcg(logits + (int64_t)row * n_opt + j) / temperature;
+      v[q][i] = x;
+      mx[q] = fmaxf(mx[q], x);
+    }
+  }
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1)
+#pragma unroll
+    for (int q = 0; q < NR; ++q) mx[q] = fmaxf(mx[q], __shfl_xor_sync(0xffffffffu, mx[q], s));
+#pragma unroll
+  for (int q = 0; q < NR; ++q) {
+    sum[q] = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const float e = (v[q][i] == -INFINITY) ? 0.f : expf(v[q][i] - mx[q]);
+      v[q][i] = e;
+      sum[q] += e;
+    }
+  }
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1)
+#pragma unroll
+    for (int q = 0; q < NR; ++q) sum[q] += __shfl_xor_sync(0xffffffffu, sum[q], s);
+#pragma unroll
+  for (int q = 0; q < NR; ++q) {
+    const int row = row0 + q;
+    if (row >= B) continue;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int j = lane + 32 * i;
+      if (j < n_opt) probs[(int64_t)row * n_opt + j] = (cnt[q] > 0) ? v[q][i] / sum[q] : __int_as_float(0x7fc00000);
+    }
+  }
+}
+
+// One warp, one row.
+__device__ __forceinline__ void softmax_row(int row, int B, int n_opt, const int32_t* __restrict__ counts,
+                                            float temperature, const float* logits, float* __restrict__ probs,
+                                            int lane) {
+  if (n_opt <= 32 * 8) rows_softmax<8, 1>(row, B, n_opt, counts, temperature, logits, probs, lane);
+  else if (n_opt <= 32 * 16) rows_softmax<16, 1>(row, B, n_opt, counts, temperature, logits, probs, lane);
+  else rows_softmax<32, 1>(row, B, n_opt, counts, temperature, logits, probs, lane);
+}
 
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(kRows * 32) readout_kernel(const T* __restrict__ hidden,
@@ -184,39 +250,228 @@ __global__ void __launch_bounds__(kRows * 32) readout_kernel(const T* __restrict
   if (!s_last) return;
   __threadfence();
 
-  const int row = r0 + warp;
-  if (row < B) {
-    constexpr int kPer = kMaxOpts / 32;
-    const int cnt = counts[row];
-    float v[kPer];
-    float mx = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const int j = lane + 32 * i;
-      float x = -INFINITY;
-      if (j < n_opt && j < cnt) x = __ldcg(logits_ws + (int64_t)row * n_opt + j) / temperature;
-      v[i] = x;
-      mx = fmaxf(mx, x);
-    }
-#pragma unroll
-    for (int s = 16; s > 0; s >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, s));
-    float sum = 0.f;
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const float e = (v[i] == -INFINITY) ? 0.f : expf(v[i] - mx);
-      v[i] = e;
-      sum += e;
-    }
-#pragma unroll
-    for (int s = 16; s > 0; s >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, s);
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const int j = lane + 32 * i;
-      // A row with count <= 0 is all -inf in the reference; softmax gives NaN.
-      if (j < n_opt) probs[(int64_t)row * n_opt + j] = (cnt > 0) ? v[i] / sum : __int_as_float(0x7fc00000);
-    }
-  }
+  softmax_row(r0 + warp, B, n_opt, counts, temperature, logits_ws, probs, lane);
   if (threadIdx.x == 0) tickets[blockIdx.x] = 0u;
+}
+
+// ---------------------------------------------------------------------------
+// Tiled split-K readout (the d3b_readout path for 16-byte aligned rows):
+// grid (row tiles of 64, option tiles of 64, K splits). A CTA stages its rows
+// of hidden and its options of R for 64 k at a time in shared memory (as
+// fp32, k-major, double-buffered) and each thread accumulates a 4 x 4 block of
+// dot products with fp32 FMAs, so every element of R read from L2 serves 64
+// rows. Each CTA writes its partial sums; the last CTA of a (row tile, option
+// tile) to finish (atomic ticket) adds the K splits in split order (so the
+// result does not depend on CTA timing) into the logits, and the last option
+// tile of a row tile runs the masked softmax of its 64 rows. Tickets are reset
+// by whoever used them last, so the workspace is ready for the next call.
+// ---------------------------------------------------------------------------
+constexpr int kTR = 64;          // rows per tile
+constexpr int kTO = 64;          // options per tile
+constexpr int kKC = 64;          // k per shared-memory stage
+constexpr int kTiledSmem = 2 * kKC * (kTR + 4) * 4 + 2 * kKC * (kTO + 4) * 4;  // 69632 bytes
+constexpr int kMaxSplit = 32;    // K splits at most
+constexpr int kTiledTicketWords = 16384;  // ticket1: row tiles x option tiles (<= 512 x 16), ticket2: row tiles
+constexpr size_t kTiledTicketBytes = kTiledTicketWords * sizeof(unsigned int);
+
+template <typename T>
+__device__ __forceinline__ void load_hidden8(const T* p, bool ok, float (&v)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 a = ok ? __ldg(reinterpret_cast<const float4*>(p)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 b = ok ? __ldg(reinterpret_cast<const float4*>(p) + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 a = ok ? __ldg(reinterpret_cast<const uint4*>(p)) : make_uint4(0, 0, 0, 0);
+    unpack16(a, static_cast<const T*>(nullptr), v);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) readout_tiled_kernel(const T* __restrict__ hidden, const float* __restrict__ R,
+                                                            int B, int K, int n_opt,
+                                                            int kper, int b_pad, int o_pad,
+                                                            float* __restrict__ partials) {
+  // [2 buffers][kKC][64 + 4] for hidden, then the same for R (dynamic: 69.6 KB)
+  extern __shared__ __align__(16) float smem_f[];
+  auto hs = [&](int buf, int k) -> float* { return smem_f + (buf * kKC + k) * (kTR + 4); };
+  auto rs = [&](int buf, int k) -> float* { return smem_f + 2 * kKC * (kTR + 4) + (buf * kKC + k) * (kTO + 4); };
+  const int t = threadIdx.x;
+  const int tr = blockIdx.x, to = blockIdx.y, kz = blockIdx.z;
+  const int r0 = tr * kTR, o0 = to * kTO;
+  const int kb = kz * kper, ke = min(K, kb + kper);
+  // loader roles: hidden row r0 + t/4 at k offsets (t%4)*8 and 32 + (t%4)*8;
+  // R options o0 + t/8 and o0 + 32 + t/8 at k offsets (t%8)*4 and 32 + (t%8)*4
+  const int hr = t >> 2, hk = (t & 3) * 8;
+  const int ro = t >> 3, rk = (t & 7) * 4;
+  const bool h_row_ok = r0 + hr < B;
+  const bool r_ok0 = o0 + ro < n_opt, r_ok1 = o0 + 32 + ro < n_opt;
+  const T* hp = hidden + (int64_t)min(r0 + hr, B - 1) * K;
+  const float* rp0 = R + (int64_t)min(o0 + ro, n_opt - 1) * K;
+  const float* rp1 = R + (int64_t)min(o0 + 32 + ro, n_opt - 1) * K;
+  float hv[2][8];
+  float4 rv[2][2];
+  auto fetch = [&](int k0) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int kh = k0 + 32 * h;
+      const bool hk_ok = kh + hk < ke, rk_ok = kh + rk < ke;  // K, kper and k0 are multiples of 8
+      load_hidden8<T>(hp + kh + hk, h_row_ok && hk_ok, hv[h]);
+      rv[h][0] = (r_ok0 && rk_ok) ? __ldg(reinterpret_cast<const float4*>(rp0 + kh + rk)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      rv[h][1] = (r_ok1 && rk_ok) ? __ldg(reinterpret_cast<const float4*>(rp1 + kh + rk)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  auto stash = [&](int buf) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) hs(buf, 32 * h + hk + i)[hr] = hv[h][i];
+      const float a[4] = {rv[h][0].x, rv[h][0].y, rv[h][0].z, rv[h][0].w};
+      const float c[4] = {rv[h][1].x, rv[h][1].y, rv[h][1].z, rv[h][1].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        rs(buf, 32 * h + rk + i)[ro] = a[i];
+        rs(buf, 32 * h + rk + i)[32 + ro] = c[i];
+      }
+    }
+  };
+  const int ty = t >> 4, tx = t & 15;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  fetch(kb);
+  stash(0);
+  __syncthreads();
+  int buf = 0;
+  for (int k0 = kb; k0 < ke; k0 += kKC) {
+    const bool more = k0 + kKC < ke;
+    if (more) fetch(k0 + kKC);
+#pragma unroll 8
+    for (int kk = 0; kk < kKC; ++kk) {
+      const float4 a = *reinterpret_cast<const float4*>(hs(buf, kk) + ty * 4);
+      const float4 b = *reinterpret_cast<const float4*>(rs(buf, kk) + tx * 4);
+      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    if (more) stash(buf ^ 1);
+    __syncthreads();
+    buf ^= 1;
+  }
+  // partial sums of this K split: partials[kz][row][opt], padded to b_pad x o_pad
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    *reinterpret_cast<float4*>(partials + ((int64_t)kz * b_pad + r0 + ty * 4 + i) * o_pad + o0 + tx * 4) =
+        make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+
+}
+
+// Second kernel of the tiled readout: one CTA per row adds the K-split partial
+// logits in split order, then runs the masked softmax of the row.
+__global__ void __launch_bounds__(256) readout_reduce_softmax_kernel(const float* __restrict__ partials,
+                                                                     const int32_t* __restrict__ counts,
+                                                                     float temperature, float* __restrict__ probs,
+                                                                     int n_opt, int ksplit, int b_pad, int o_pad) {
+  __shared__ float red[8];
+  __shared__ float bcast;
+  const int row = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int cnt = counts[row];
+  constexpr int kPer = kMaxOpts / 256;
+  float v[kPer];
+  float mx = -INFINITY;
+  const int64_t zstride = (int64_t)b_pad * o_pad;
+  const float* base = partials + (int64_t)row * o_pad;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int j = t + 256 * i;
+    float x = -INFINITY;
+    if (j < n_opt) {
+      float acc = 0.f;
+      int z = 0;
+      for (; z + 4 <= ksplit; z += 4) {  // four loads in flight, added in split order
+        const float p0 = base[z * zstride + j], p1 = base[(z + 1) * zstride + j];
+        const float p2 = base[(z + 2) * zstride + j], p3 = base[(z + 3) * zstride + j];
+        acc += p0; acc += p1; acc += p2; acc += p3;
+      }
+      for (; z < ksplit; ++z) acc += base[z * zstride + j];
+      if (j < cnt) x = acc / temperature;
+    }
+    v[i] = x;
+    mx = fmaxf(mx, x);
+  }
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, s));
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  if (t == 0) {
+    float m = red[0];
+    for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w]);
+    bcast = m;
+  }
+  __syncthreads();
+  mx = bcast;
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const float e = (v[i] == -INFINITY) ? 0.f : expf(v[i] - mx);
+    v[i] = e;
+    sum += e;
+  }
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, s);
+  __syncthreads();
+  if (lane == 0) red[warp] = sum;
+  __syncthreads();
+  if (t == 0) {
+    float m = 0.f;
+    for (int w = 0; w < 8; ++w) m += red[w];  // fixed order
+    bcast = m;
+  }
+  __syncthreads();
+  sum = bcast;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int j = t + 256 * i;
+    // a row with count <= 0 is all -inf in the reference; softmax gives NaN
+    if (j < n_opt) probs[(int64_t)row * n_opt + j] = (cnt > 0) ? v[i] / sum : __int_as_float(0x7fc00000);
+  }
+}
+
+struct TiledShape {
+  int kper, ksplit, b_pad, o_pad;
+};
+
+inline TiledShape tiled_shape(int B, int K, int n_opt) {
+  TiledShape sh;
+  sh.b_pad = (B + kTR - 1) / kTR * kTR;
+  sh.o_pad = (n_opt + kTO - 1) / kTO * kTO;
+  const int tiles = (sh.b_pad / kTR) * (sh.o_pad / kTO);
+  const int sms = std::max(1, d3b_host::num_sms(d3b_host::current_device()));
+  int want = (3 * sms + tiles - 1) / tiles;                 // about three CTAs per SM
+  want = std::max(1, std::min(want, std::min(kMaxSplit, K / 128)));  // at least 128 k per split
+  sh.kper = ((K + want - 1) / want + kKC - 1) / kKC * kKC;
+  sh.ksplit = (K + sh.kper - 1) / sh.kper;
+  return sh;
+}
+
+template <typename T>
+void launch_tiled(const void* hidden, const float* readout, const int32_t* counts, float temperature, float* probs,
+                  int B, int K, int n_opt, float* partials, cudaStream_t s) {
+  const TiledShape sh = tiled_shape(B, K, n_opt);
+  const dim3 grid(sh.b_pad / kTR, sh.o_pad / kTO, sh.ksplit), block(256);
+  static int attr_set[64] = {0};
+  const int dev = d3b_host::current_device();
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaFuncSetAttribute(readout_tiled_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTiledSmem);
+    attr_set[dev] = 1;
+  }
+  readout_tiled_kernel<T><<<grid, block, kTiledSmem, s>>>(static_cast<const T*>(hidden), readout, B, K, n_opt, sh.kper,
+                                                          sh.b_pad, sh.o_pad, partials);
+  readout_reduce_softmax_kernel<<<B, 256, 0, s>>>(partials, counts, temperature, probs, n_opt, sh.ksplit, sh.b_pad,
+                                                  sh.o_pad);
 }
 
 template <typename T>
@@ -236,9 +491,15 @@ void launch_typed(const void* hidden, const float* readout, const int32_t* count
 
 }  // namespace
 
+// Workspace of d3b_readout:
+//   [tickets: kTiledTicketBytes][logits: B x n_opt f32][partials: kMaxSplit x b_pad x o_pad f32]
+// (the fallback kernel for unaligned rows uses the first kTicketBytes of the
+// ticket region and the logits).
 extern "C" size_t d3b_readout_workspace_size(int B, int n_opt) {
   if (B <= 0 || n_opt <= 0) return 0;
-  return kTicketBytes + (((size_t)B * n_opt * sizeof(float) + 255) & ~(size_t)255);
+  const size_t b_pad = (size_t)(B + kTR - 1) / kTR * kTR, o_pad = (size_t)(n_opt + kTO - 1) / kTO * kTO;
+  return kTiledTicketBytes + (((size_t)B * n_opt * sizeof(float) + 255) & ~(size_t)255) +
+         (size_t)kMaxSplit * b_pad * o_pad * sizeof(float);
 }
 
 extern "C" int d3b_readout(const void* hidden, int h_dtype, const float* readout, const int32_t* counts,
@@ -252,13 +513,26 @@ extern "C" int d3b_readout(const void* hidden, int h_dtype, const float* readout
   if (workspace_bytes < d3b_readout_workspace_size(B, n_opt)) return D3B_ENOSPACE;
   if (reinterpret_cast<uintptr_t>(workspace) % 16) return D3B_EALIGN;
   unsigned int* tickets = static_cast<unsigned int*>(workspace);
-  float* logits = reinterpret_cast<float*>(static_cast<char*>(workspace) + kTicketBytes);
+  float* logits = reinterpret_cast<float*>(static_cast<char*>(workspace) + kTiledTicketBytes);
+  float* partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kTiledTicketBytes +
+                                             (((size_t)B * n_opt * sizeof(float) + 255) & ~(size_t)255));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int esize = h_dtype == D3B_F32 ? 4 : 2;
+  const bool tiled = (K % 8 == 0) && (reinterpret_cast<uintptr_t>(readout) % 16 == 0) &&
+                     (reinterpret_cast<uintptr_t>(hidden) % 16 == 0) && ((int64_t)K * esize % 16 == 0);
   switch (h_dtype) {
-    case D3B_F32: launch_typed<float>(hidden, readout, counts, temperature, probs, B, K, n_opt, logits, tickets, s); break;
-    case D3B_F16: launch_typed<__half>(hidden, readout, counts, temperature, probs, B, K, n_opt, logits, tickets, s); break;
+    case D3B_F32:
+      if (tiled) launch_tiled<float>(hidden, readout, counts, temperature, probs, B, K, n_opt, partials, s);
+      else launch_typed<float>(hidden, readout, counts, temperature, probs, B, K, n_opt, logits, tickets, s);
+      break;
+    case D3B_F16:
+      if (tiled) launch_tiled<__half>(hidden, readout, counts, temperature, probs, B, K, n_opt, partials, s);
+      else launch_typed<__half>(hidden, readout, counts, temperature, probs, B, K, n_opt, logits, tickets, s);
+      break;
     case D3B_BF16:
-      launch_typed<__nv_bfloat16>(hidden, readout, counts, temperature, probs, B, K, n_opt, logits, tickets, s);
+      if (tiled)
+        launch_tiled<__nv_bfloat16>(hidden, readout, counts, temperature, probs, B, K, n_opt, partials, s);
+      else launch_typed<__nv_bfloat16>(hidden, readout, counts, temperature, probs, B, K, n_opt, logits, tickets, s);
       break;
     default: return D3B_EUNSUPPORTED;
   }
@@ -324,7 +598,8 @@ extern "C" int d3b_readout_noalloc(const void* hidden, int h_dtype, const float*
   if (B == 0) return D3B_OK;
   if (!hidden || !readout || !counts || !probs) return D3B_EINVAL;
   if (h_dtype != D3B_F32 && h_dtype != D3B_F16 && h_dtype != D3B_BF16) return D3B_EUNSUPPORTED;
-  if (d3b_readout_workspace_size(B, n_opt) > kNoAllocScratchBytes) return D3B_ENOSPACE;
+  if (kTicketBytes + (((size_t)B * n_opt * sizeof(float) + 255) & ~(size_t)255) > kNoAllocScratchBytes)
+    return D3B_ENOSPACE;
   void* scratch = nullptr;
   const int rc = noalloc_scratch(&scratch);
   if (rc != D3B_OK) return rc;

@@ -134,8 +134,9 @@ D3B_API int d3b_readout(const void* hidden, int h_dtype, const float* readout, c
  * counterpart in the reference. Same arguments and results as d3b_readout,
  * without the workspace: the scratch is one fixed 1 MiB array inside the
  * library, held by every GPU that loads it until the process exits.
- *   Limit: d3b_readout_workspace_size(B, n_opt) <= 1 MiB (B * n_opt up to
- *   258048 logits), otherwise D3B_ENOSPACE and nothing is enqueued.
+ *   Limit: 16 KiB of counters plus B * n_opt * 4 bytes of logits must fit in
+ *   1 MiB (B * n_opt up to 258048 logits), otherwise D3B_ENOSPACE and nothing
+ *   is enqueued.
  *   Calls on one device share the array: calls whose work overlaps on the
  *   GPU (unordered streams) race and give wrong results.
  *   The first call on a device looks up the array's device address; make it
