@@ -282,7 +282,19 @@ def main():
     if world > 1:
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        # NCCL may print its banner on stdout when the communicator comes up (with
+        # NCCL_DEBUG set); stdout carries only the JSON line, so it goes to stderr.
+        sys.stdout.flush()
+        saved_stdout = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+            dist.barrier()
+            torch.cuda.synchronize()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved_stdout, 1)
+            os.close(saved_stdout)
     stream = torch.cuda.current_stream(dev)
     flush_buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     flush = lambda: flush_buf.fill_(1)
