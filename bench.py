@@ -20,8 +20,10 @@ A step = one such pass; value = question blocks per second over all ranks.
   state K/V is the resident snapshot (computed once per request in the
   state-once design).
 * extra: state pass, config 3b (16384-token state + 255 blocks of 48), the
-  W8A8 GEMM at config 2 (e4m3 and int8) with the act-quant kernel, and the
-  readout, each timed the same way and reported in TFLOP/s or GB/s.
+  W8A8 GEMM at config 2 (e4m3 and int8) with the act-quant kernel, the fused
+  producers (add + RMSNorm + quant, sigmoid gate + quant) against their
+  unfused two-kernel form, and the readout, each timed the same way and
+  reported in TFLOP/s or GB/s.
 * cpu_baseline: the CPU oracle's question pass (a restatement of
   ops.sdpa_questions in fp32) on all host threads, over a bounded sample.
 
@@ -480,6 +482,30 @@ def secondary(dev, stream, flush, peaks, quant, pb, d3b):
         del layer, qa, sa
     res["fp8_int8_peak_tflops"] = fp8_peak
     del x, w
+    # fused producers at config 2 rows (4096 x 5120): residual add + RMSNorm + fp8 quant of
+    # the normed rows in one kernel, against the same two steps as separate kernels
+    from d3_turbo_trt_b200.model import fused
+    r = torch.randn(M, K, generator=g).to(torch.bfloat16).to(dev)
+    dl = torch.randn(M, K, generator=g).to(torch.bfloat16).to(dev)
+    w1 = (1 + torch.randn(K, generator=g) * 0.1).to(dev)
+    tf = statistics.median(time_steps(lambda: fused.add_rmsnorm_quant(r, dl, w1, 1e-6, "fp8"), 10, 3, stream, flush))
+    tu = statistics.median(time_steps(
+        lambda: quant.quantize_rows(fused.add_rmsnorm(r, dl, w1, 1e-6)[1], "fp8"), 10, 3, stream, flush))
+    nbytes = M * K * (2 + 2 + 2 + 1) + M * 4 + K * 4  # read residual, delta; write hidden, codes, scale
+    res["add_rmsnorm_fp8_quant_cfg2"] = {"fused_ms": tf, "unfused_ms": tu, "fused_gbs": nbytes / tf / 1e6,
+                                         "fused_frac_hbm": nbytes / tf / 1e6 / peaks["hbm_gbs"]}
+    del r, dl
+    # sigmoid gate + fp8 quant for o_proj: 4096 tokens x 32 heads x 128
+    Tt, Hh, Dd = 4096, 32, 128
+    at = torch.randn(1, Hh, Tt, Dd, generator=g).to(torch.bfloat16).to(dev).permute(0, 2, 1, 3)
+    gt = torch.randn(1, Tt, Hh, 2 * Dd, generator=g).to(torch.bfloat16).to(dev)[..., Dd:]
+    tf = statistics.median(time_steps(lambda: fused.sigmoid_gate_quant(at, gt, "fp8"), 10, 3, stream, flush))
+    tu = statistics.median(time_steps(
+        lambda: quant.quantize_rows(fused.sigmoid_gate(at, gt).reshape(Tt, Hh * Dd), "fp8"), 10, 3, stream, flush))
+    nbytes = Tt * Hh * Dd * (2 + 2 + 1) + Tt * 4
+    res["sigmoid_gate_fp8_quant_4k_tokens"] = {"fused_ms": tf, "unfused_ms": tu, "fused_gbs": nbytes / tf / 1e6,
+                                               "fused_frac_hbm": nbytes / tf / 1e6 / peaks["hbm_gbs"]}
+    del at, gt
     # readout: 255 blocks x 5120 x 255 options
     hidden = torch.randn(255, 5120, generator=g).to(torch.bfloat16).to(dev)
     ro = (torch.randn(255, 5120, generator=g) * 0.02).to(dev)

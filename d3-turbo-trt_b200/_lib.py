@@ -18,7 +18,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libd3b200.so"
 
 OK, EINVAL, EALIGN, EUNSUPPORTED, ECUDA, ETIMEOUT, ENOSPACE = 0, -1, -2, -3, -4, -5, -6
 F32, F16, BF16, I32 = 0, 1, 2, 3
-MODE_FP8, MODE_INT8 = 0, 1
+MODE_FP8, MODE_INT8, MODE_NONE = 0, 1, 2
 
 # (name, restype, argtypes) for every symbol include/d3b200.h declares.
 _VP, _I, _I64, _F, _SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
@@ -28,6 +28,12 @@ SIGNATURES: list[tuple[str, Any, list[Any]]] = [
     ("d3b_error_string", ctypes.c_char_p, [_I]),
     ("d3b_device_error", _I, [_VP, _I]),
     ("d3b_act_quant", _I, [_VP, _I, _I64, _VP, _VP, _I64, _I64, _I, _VP]),
+    (
+        "d3b_add_rmsnorm_quant",
+        _I,
+        [_VP, _I64, _VP, _I64, _VP, _F, _VP, _VP, _I64, _VP, _I64, _VP, _VP, _I64, _I64, _I, _VP],
+    ),
+    ("d3b_sigmoid_gate_quant", _I, [_VP, _I64P, _VP, _I64P, _VP, _VP, _VP, _I, _I, _I, _I, _I, _VP]),
     ("d3b_w8a8_gemm", _I, [_VP, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _I64, _I, _I, _VP]),
     (
         "d3b_prefix_bidir",

@@ -1,0 +1,137 @@
+"""Fused producers of the W8A8 linears' inputs (sm_100a kernels in csrc/norm_quant.cu).
+
+Every ``QuantLinear`` input of the model comes out of one of two element-wise
+ops; these functions compute them and, for the ``*_quant`` forms, the
+per-row activation quantisation of the consuming linear in the same pass, so
+the bf16 normed / gated rows never travel through HBM:
+
+* ``add_rmsnorm(residual, delta, weight_plus_one, eps, rowmask=None)`` ->
+  ``(hidden, normed)``: drop-in for reference/d3_kernels.py:145-170 (residual
+  add + zero-centred RMSNorm of Qwen3.5).
+* ``add_rmsnorm_quant(..., mode)`` -> ``(hidden, q, scale)``: the same, with
+  ``normed`` quantised as ``quantize_rows`` (d3trt/model/quant.py:92-100) would;
+  feed ``QuantLinear.forward_quantized(q, scale)`` of q/k/v_proj or gate/up_proj.
+* ``sigmoid_gate(attn_out, gate)`` -> ``[B, T, H*D]``: drop-in for
+  reference/d3_kernels.py:502-525 (``attn_out * sigmoid(gate)``, core.py:297).
+* ``sigmoid_gate_quant(attn_out, gate, mode)`` -> ``(q, scale)``: the gated rows
+  quantised for o_proj.
+
+bf16 tensors on the GPU only; rows of up to 6144 elements (a multiple of 8),
+16-byte aligned. A ``RuntimeError`` names any other case; there is no fallback.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _lib
+from .quant import _FP8, _mode_code
+
+
+def _check_bf16(t: torch.Tensor, what: str) -> None:
+    _lib.require_cuda(t, what)
+    if t.dtype != torch.bfloat16:
+        raise RuntimeError(f"{what}: expected bfloat16, got {t.dtype}")
+
+
+def _rows(t: torch.Tensor, what: str) -> torch.Tensor:
+    """[..., K] -> [M, K] view with unit last stride (copied only if it has none)."""
+    flat = t.reshape(-1, t.shape[-1])
+    if flat.stride(1) != 1 or flat.stride(0) < flat.shape[1]:
+        flat = flat.contiguous()
+    return flat
+
+
+def _norm(residual, delta, weight_plus_one, eps, rowmask, mode_code):
+    _check_bf16(residual, "add_rmsnorm")
+    shape = residual.shape
+    res = _rows(residual, "residual")
+    M, K = res.shape
+    dev = res.device
+    d = None
+    if delta is not None:
+        _check_bf16(delta, "add_rmsnorm")
+        if delta.shape != shape:
+            raise RuntimeError(f"delta {tuple(delta.shape)} and residual {tuple(shape)} differ")
+        d = _rows(delta, "delta")
+    w1 = weight_plus_one.to(device=dev, dtype=torch.float32).contiguous()
+    if w1.numel() != K:
+        raise RuntimeError(f"weight_plus_one has {w1.numel()} elements for rows of {K}")
+    mask = None
+    if rowmask is not None:
+        mask = rowmask.to(device=dev, dtype=torch.int32).reshape(-1).contiguous()
+        if mask.numel() != M:
+            raise RuntimeError(f"rowmask has {mask.numel()} entries for {M} rows")
+    hidden = torch.empty((M, K), dtype=torch.bfloat16, device=dev) if d is not None else res
+    normed = torch.empty((M, K), dtype=torch.bfloat16, device=dev) if mode_code == _lib.MODE_NONE else None
+    q = scale = None
+    if mode_code != _lib.MODE_NONE:
+        q = torch.empty((M, K), dtype=_FP8 if mode_code == _lib.MODE_FP8 else torch.int8, device=dev)
+        scale = torch.empty((M,), dtype=torch.float32, device=dev)
+    if M:
+        status = _lib.lib().d3b_add_rmsnorm_quant(
+            _lib.ptr(res), res.stride(0), _lib.ptr(d), d.stride(0) if d is not None else 0, _lib.ptr(w1), float(eps),
+            _lib.ptr(mask), _lib.ptr(hidden if d is not None else None), K, _lib.ptr(normed), K, _lib.ptr(q),
+            _lib.ptr(scale), M, K, mode_code, _lib.stream_of(res),
+        )
+        _lib.check(status, "d3b_add_rmsnorm_quant")
+    hidden_out = hidden.reshape(shape) if d is not None else residual
+    return hidden_out, normed, q, scale
+
+
+def add_rmsnorm(residual: torch.Tensor, delta: torch.Tensor | None, weight_plus_one: torch.Tensor, eps: float,
+                rowmask: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """(hidden, normed) bf16: hidden = residual + delta (or residual), normed = Qwen3.5 RMSNorm of hidden.
+
+    ``weight_plus_one`` is the fp32 ``1 + w``; ``rowmask`` (one integer per row)
+    zeroes the normed rows of padding (reference/d3_kernels.py:145-170).
+    """
+    hidden, normed, _, _ = _norm(residual, delta, weight_plus_one, eps, rowmask, _lib.MODE_NONE)
+    return hidden, normed.reshape(residual.shape)
+
+
+def add_rmsnorm_quant(residual: torch.Tensor, delta: torch.Tensor | None, weight_plus_one: torch.Tensor, eps: float,
+                      mode: str, rowmask: torch.Tensor | None = None):
+    """(hidden, q [M, K], scale [M, 1]): the normed rows quantised per row in ``mode`` ("fp8"/"int8")."""
+    hidden, _, q, scale = _norm(residual, delta, weight_plus_one, eps, rowmask, _mode_code(mode))
+    return hidden, q, scale[:, None]
+
+
+def _gate(attn_out, gate, mode_code):
+    _check_bf16(attn_out, "sigmoid_gate")
+    _check_bf16(gate, "sigmoid_gate")
+    if attn_out.dim() != 4 or gate.shape != attn_out.shape:
+        raise RuntimeError(f"attn_out and gate must both be [B, T, H, D], got {tuple(attn_out.shape)}, "
+                           f"{tuple(gate.shape)}")
+    if attn_out.stride(3) != 1:
+        attn_out = attn_out.contiguous()
+    if gate.stride(3) != 1:
+        gate = gate.contiguous()
+    B, T, H, D = attn_out.shape
+    dev = attn_out.device
+    gated = torch.empty((B, T, H * D), dtype=torch.bfloat16, device=dev) if mode_code == _lib.MODE_NONE else None
+    q = scale = None
+    if mode_code != _lib.MODE_NONE:
+        q = torch.empty((B * T, H * D), dtype=_FP8 if mode_code == _lib.MODE_FP8 else torch.int8, device=dev)
+        scale = torch.empty((B * T,), dtype=torch.float32, device=dev)
+    if B * T:
+        sa = _lib.i64_array(attn_out.stride()[:3])
+        sg = _lib.i64_array(gate.stride()[:3])
+        status = _lib.lib().d3b_sigmoid_gate_quant(
+            _lib.ptr(attn_out), sa, _lib.ptr(gate), sg, _lib.ptr(gated), _lib.ptr(q), _lib.ptr(scale), B, T, H, D,
+            mode_code, _lib.stream_of(attn_out),
+        )
+        _lib.check(status, "d3b_sigmoid_gate_quant")
+    return gated, q, scale
+
+
+def sigmoid_gate(attn_out: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
+    """``attn_out * sigmoid(gate)`` -> [B, T, H * D] bf16 from [B, T, H, D] views with unit last stride."""
+    gated, _, _ = _gate(attn_out, gate, _lib.MODE_NONE)
+    return gated
+
+
+def sigmoid_gate_quant(attn_out: torch.Tensor, gate: torch.Tensor, mode: str):
+    """(q [B*T, H*D], scale [B*T, 1]): the gated rows quantised per row in ``mode`` for o_proj."""
+    _, q, scale = _gate(attn_out, gate, _mode_code(mode))
+    return q, scale[:, None]

@@ -197,6 +197,16 @@ class QuantLinear(nn.Module):
         self.kernel = KERNEL_NAME
         return out.reshape(*shape, self.out_features)
 
+    def forward_quantized(self, q: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+        """The linear on input rows already quantised in this layer's mode, e.g. by the
+        fused producers of ``d3_turbo_trt_b200.model.fused``: q [M, K], scale [M, 1] -> [M, N]."""
+        expect = _FP8 if self.mode == "fp8" else torch.int8
+        if q.dtype != expect or q.dim() != 2 or q.shape[1] != self.in_features:
+            raise ValueError(f"expected [M, {self.in_features}] {expect} codes, got {tuple(q.shape)} {q.dtype}")
+        out = scaled_mm(q, self.weight, scale, self.weight_scale, out_dtype=self.dtype)
+        self.kernel = KERNEL_NAME
+        return out
+
 
 def make_linear(
     in_features: int,

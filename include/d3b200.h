@@ -46,7 +46,7 @@ enum {
 };
 
 enum { D3B_F32 = 0, D3B_F16 = 1, D3B_BF16 = 2, D3B_I32 = 3 };
-enum { D3B_MODE_FP8 = 0, D3B_MODE_INT8 = 1 };
+enum { D3B_MODE_FP8 = 0, D3B_MODE_INT8 = 1, D3B_MODE_NONE = 2 /* fused producers: bf16 rows only */ };
 
 /* Library version (major*10000 + minor*100 + patch). */
 D3B_API int d3b_version(void);
@@ -71,6 +71,44 @@ D3B_API int d3b_device_error(d3b_stream_t stream, int reset);
  */
 D3B_API int d3b_act_quant(const void* x, int x_dtype, int64_t ldx, void* q, float* scale, int64_t M, int64_t K,
                   int mode, d3b_stream_t stream);
+
+/*
+ * Residual add + zero-centred RMSNorm fused with the per-row activation quant
+ * of the linear that consumes the normed rows (q/k/v_proj, gate/up_proj).
+ * Replaces reference/d3_kernels.py:97-170 (add_rmsnorm, the bf16-exact
+ * restatement of Qwen3_5RMSNorm with a preceding bf16 residual add) followed
+ * by d3trt/model/quant.py:92-100 (quantize_rows) on its output.
+ *   residual, delta [M, K] bf16 rows of ld_res / ld_delta elements (delta may
+ *     be NULL: hidden = residual, no hidden_out)
+ *   hidden_out [M, K] bf16 = bf16(residual + delta) (required with delta)
+ *   normed = bf16((hidden * rsqrt(mean(hidden^2) + eps)) * weight_plus_one),
+ *     fp32 math, mean over an fp64 sum of squares, rsqrt correctly rounded;
+ *     rows whose rowmask entry is 0 are zero (rowmask may be NULL)
+ *   normed_out [M, K] bf16, optional (required with mode D3B_MODE_NONE)
+ *   q [M, K] contiguous codes + scale [M] of normed, as d3b_act_quant
+ *     (not written with mode D3B_MODE_NONE)
+ * bf16 only, K % 8 == 0, K <= 6144, 16-byte aligned rows (else
+ * D3B_EUNSUPPORTED / D3B_EALIGN).
+ */
+D3B_API int d3b_add_rmsnorm_quant(const void* residual, int64_t ld_res, const void* delta, int64_t ld_delta,
+                                  const float* weight_plus_one, float eps, const int32_t* rowmask, void* hidden_out,
+                                  int64_t ld_hidden, void* normed_out, int64_t ld_normed, void* q, float* scale,
+                                  int64_t M, int64_t K, int mode, d3b_stream_t stream);
+
+/*
+ * Attention output gate fused with the per-row activation quant of o_proj.
+ * Replaces reference/d3_kernels.py:467-525 (sigmoid_gate; d3trt/model/core.py:297)
+ * followed by d3trt/model/quant.py:92-100 on its output.
+ *   attn, gate: [B, T, H, D] bf16 views with unit last stride and element
+ *     strides attn_strides / gate_strides = {b, t, h} (multiples of 8)
+ *   gated = bf16(attn * bf16(1 / (1 + exp(-gate)))) as rows [B*T, H*D]
+ *   gated_out [B*T, H*D] bf16 contiguous, optional (required with D3B_MODE_NONE)
+ *   q [B*T, H*D] contiguous codes + scale [B*T] of gated, as d3b_act_quant
+ * D % 8 == 0, H*D <= 6144.
+ */
+D3B_API int d3b_sigmoid_gate_quant(const void* attn, const int64_t* attn_strides, const void* gate,
+                                   const int64_t* gate_strides, void* gated_out, void* q, float* scale, int B, int T,
+                                   int H, int D, int mode, d3b_stream_t stream);
 
 /*
  * W8A8 scaled GEMM: y[m, n] = (sum_k qa[m,k] * qw[n,k]) * sa[m] * sw[n].
