@@ -53,6 +53,7 @@ sys.path.insert(0, str(ROOT))
 
 CFG3A = dict(B=16, H=32, Hkv=4, L=64, D=128, S=4096)
 CFG3B = dict(B=255, H=32, Hkv=4, L=48, D=128, S=16384)
+CFG5 = dict(B=255, H=32, Hkv=4, L=64, D=128, S=16384)
 METRIC = "question-blocks/s at 4k state"
 L2_FLUSH_BYTES = 256 << 20
 
@@ -387,6 +388,7 @@ def main():
     extra = {}
     if not args.no_extra:
         extra = secondary(dev, stream, flush, peaks, quant, pb, d3b)
+        extra["cfg5_strong_scaling"] = cfg5_strong(dev, stream, flush, peaks, pb, d3dist, rank, world)
     if world > 1:
         dist.barrier()
 
@@ -424,6 +426,57 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def cfg5_strong(dev, stream, flush, peaks, pb, d3dist, rank, world):
+    """Config 5: one request, 255 question blocks of 64 over a 16384-token
+    state, split over the ranks (contiguous, length-sorted shards; sizes differ by <= 1).
+    Rank 0 builds the state K/V and broadcasts it (32 MiB, timed on its own); each rank
+    then runs its shard; the pass time is the max over ranks (strong scaling)."""
+    import torch.distributed as dist
+
+    cfg = CFG5
+    S, Hkv, D, L = cfg["S"], cfg["Hkv"], cfg["D"], cfg["L"]
+    g = torch.Generator().manual_seed(55)
+    ks = torch.empty(S, Hkv, D, dtype=torch.bfloat16, device=dev)
+    vs = torch.empty_like(ks)
+    if rank == 0:
+        ks.copy_(torch.randn(S, Hkv, D, generator=g).to(torch.bfloat16))
+        vs.copy_(torch.randn(S, Hkv, D, generator=g).to(torch.bfloat16))
+    bcast_ms = None
+    if world > 1:
+        d3dist.broadcast_state_kv([(ks, vs)], src=0)  # warm
+        torch.cuda.synchronize()
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        d3dist.broadcast_state_kv([(ks, vs)], src=0)
+        b.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([a.elapsed_time(b)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        bcast_ms = float(t.item())
+    lengths = [L] * cfg["B"]
+    order = d3dist.length_order(lengths)
+    lo, hi = d3dist.shard_bounds(cfg["B"], world, rank)
+    mine = [order[i] for i in range(lo, hi)]
+    nb = len(mine)
+    q = torch.randn(nb, L, cfg["H"], D, generator=g).to(torch.bfloat16).to(dev).permute(0, 2, 1, 3)
+    kq = torch.randn(nb, L, Hkv, D, generator=g).to(torch.bfloat16).to(dev).permute(0, 2, 1, 3)
+    vq = torch.randn(nb, L, Hkv, D, generator=g).to(torch.bfloat16).to(dev).permute(0, 2, 1, 3)
+    lens = [lengths[i] for i in mine]
+    ksv, vsv = ks.permute(1, 0, 2), vs.permute(1, 0, 2)
+    fn = lambda: pb.prefix_bidir_attention(q, ksv, vsv, kq, vq, lens, scale=D ** -0.5)
+    t_ms = statistics.median(time_steps(fn, 5, 3, stream, flush))
+    if world > 1:
+        t = torch.tensor([t_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_ms = float(t.item())
+    fl = attn_flops(**cfg)
+    return {"workload": "255 blocks x 64 tokens over a 16384-token state, H32/Hkv4/D128 bf16, split over ranks",
+            "question_pass_ms": t_ms, "blocks_per_s": cfg["B"] / (t_ms / 1e3),
+            "tflops_total": fl / t_ms / 1e9, "state_kv_broadcast_ms": bcast_ms, "state_kv_bytes": 2 * ks.numel() * 2,
+            "timing": "device, max over ranks, L2 flushed before each pass", "scaling": "strong"}
 
 
 def secondary(dev, stream, flush, peaks, quant, pb, d3b):
