@@ -127,17 +127,22 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return r;
 }
 
-// Max of N values: three-input max, 8 independent accumulators (short
-// dependency chains; N/2 + 4 instructions).
+// Max of N values (N a multiple of 8): three-input max, 8 independent
+// accumulators (short dependency chains; about N/2 + 4 instructions).
 template <int N>
 __device__ __forceinline__ float max_n(const float* v) {
+  static_assert(N >= 8 && N % 8 == 0, "max_n takes multiples of 8");
   float a[8];
 #pragma unroll
   for (int k = 0; k < 8; ++k) a[k] = v[k];
 #pragma unroll
-  for (int c = 8; c < N; c += 16)
+  for (int c = 8; c + 16 <= N; c += 16)
 #pragma unroll
     for (int k = 0; k < 8; ++k) a[k] = max3(a[k], v[c + k], v[c + 8 + k]);
+  if constexpr ((N - 8) % 16 == 8) {  // the last 8 values
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[k] = fmaxf(a[k], v[N - 8 + k]);
+  }
   return max3(max3(a[0], a[1], a[2]), max3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
 }
 
