@@ -535,6 +535,39 @@ def secondary(dev, stream, flush, peaks, quant, pb, d3b):
         del layer, qa, sa
     res["fp8_int8_peak_tflops"] = fp8_peak
     del x, w
+    # launch-bound regime: back-to-back config-1-sized question passes, eager wrapper calls
+    # against replays of a captured CUDA graph (events around the whole loop: host gaps count)
+    from d3_turbo_trt_b200.kernels.graphs import QuestionPassGraph
+    c1 = dict(B=8, H=8, Hkv=2, L=32, D=64, S=512)
+    ks1 = torch.randn(c1["Hkv"], c1["S"], c1["D"], generator=g).to(torch.bfloat16).to(dev)
+    vs1 = torch.randn(c1["Hkv"], c1["S"], c1["D"], generator=g).to(torch.bfloat16).to(dev)
+    q1 = torch.randn(c1["B"], c1["H"], c1["L"], c1["D"], generator=g).to(torch.bfloat16).to(dev)
+    kq1 = torch.randn(c1["B"], c1["Hkv"], c1["L"], c1["D"], generator=g).to(torch.bfloat16).to(dev)
+    vq1 = torch.randn(c1["B"], c1["Hkv"], c1["L"], c1["D"], generator=g).to(torch.bfloat16).to(dev)
+    lens1 = [c1["L"]] * c1["B"]
+    gp = QuestionPassGraph(ks1, vs1, rows=c1["B"], width=c1["L"], heads=c1["H"], scale=c1["D"] ** -0.5)
+    gp.q.copy_(q1); gp.k_q.copy_(kq1); gp.v_q.copy_(vq1); gp.set_lengths(lens1)
+    calls = 200
+
+    def loop_us(fn):
+        for _ in range(10):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(calls):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) * 1e3 / calls
+
+    eager_us = loop_us(lambda: pb.prefix_bidir_attention(q1, ks1, vs1, kq1, vq1, lens1, scale=c1["D"] ** -0.5))
+    graph_us = loop_us(gp.replay)
+    kern_us = statistics.median(time_steps(gp.replay, 10, 3, stream, flush)) * 1e3
+    res["question_pass_call_cost_cfg1"] = {"eager_us_per_call": eager_us, "graph_replay_us_per_call": graph_us,
+                                           "kernel_us": kern_us,
+                                           "workload": "config 1 pass (8 blocks x 32 over a 512-token state, D64)"}
+    del gp
     # fused producers at config 2 rows (4096 x 5120): residual add + RMSNorm + fp8 quant of
     # the normed rows in one kernel, against the same two steps as separate kernels
     from d3_turbo_trt_b200.model import fused
