@@ -592,6 +592,8 @@ def secondary(dev, stream, flush, peaks, quant, pb, d3b):
     res["sigmoid_gate_fp8_quant_4k_tokens"] = {"fused_ms": tf, "unfused_ms": tu, "fused_gbs": nbytes / tf / 1e6,
                                                "fused_frac_hbm": nbytes / tf / 1e6 / peaks["hbm_gbs"]}
     del at, gt
+    # state snapshot of the 64-layer model at a 4096-token state, packed into one arena block
+    res["state_snapshot_4k_64_layers"] = snapshot_line(dev, stream, flush, peaks)
     # readout: 255 blocks x 5120 x 255 options
     hidden = torch.randn(255, 5120, generator=g).to(torch.bfloat16).to(dev)
     ro = (torch.randn(255, 5120, generator=g) * 0.02).to(dev)
@@ -600,6 +602,38 @@ def secondary(dev, stream, flush, peaks, quant, pb, d3b):
                                      stream, flush))
     res["readout_255x5120x255"] = {"ms": t}
     return res
+
+
+def snapshot_line(dev, stream, flush, peaks):
+    """Packing a state snapshot (cache format): one copy launch over 128 tensors, bytes held
+    against the reference's list of views, and the pinned-host round trip of the packed block."""
+    from d3_turbo_trt_b200.model.snapshot import SnapshotArena, SnapshotLayout, copy_segments, pack_snapshot
+    from d3_turbo_trt_b200.profile import state_snapshot
+
+    snap = state_snapshot(dev)
+    layout = SnapshotLayout.of(snap)
+    storages = {}
+    for e in snap:
+        for t in (getattr(e, f) for f in e.__slots__):
+            storages[t.untyped_storage().data_ptr()] = t.untyped_storage().nbytes()
+    arena = SnapshotArena(2 * layout.nbytes + (1 << 20), dev)
+    block = arena.allocate(layout.nbytes)
+    table = layout.table(snap, arena.buffer.data_ptr() + block.offset)
+    tk = statistics.median(time_steps(lambda: copy_segments(table, dev), 10, 3, stream, flush))
+    del block
+    tcall = statistics.median(time_steps(lambda: pack_snapshot(snap, arena), 10, 3, stream, flush, host_bound=True))
+    packed = pack_snapshot(snap, arena)
+    host = packed.to_host()
+    view = packed.block.bytes_view()[: layout.nbytes]
+    t_d2h = statistics.median(time_steps(lambda: host.host.copy_(view, non_blocking=True), 5, 2, stream, flush))
+    del packed, view
+    t_h2d = statistics.median(time_steps(lambda: host.restore(arena), 5, 2, stream, flush, host_bound=True))
+    moved = 2 * layout.tensor_bytes  # read + write, the measure of the copy peak
+    return {"tensors": len(layout.slots), "tensor_bytes": layout.tensor_bytes, "block_bytes": layout.nbytes,
+            "reference_held_bytes": sum(storages.values()), "pack_kernel_ms": tk,
+            "pack_kernel_gbs": moved / tk / 1e6, "pack_kernel_frac_hbm": moved / tk / 1e6 / peaks["hbm_gbs"],
+            "pack_call_ms": tcall, "to_host_ms": t_d2h, "restore_ms": t_h2d,
+            "host_copy_gbs": layout.nbytes / max(t_d2h, t_h2d) / 1e6}
 
 
 if __name__ == "__main__":

@@ -23,6 +23,25 @@ MODE_FP8, MODE_INT8, MODE_NONE = 0, 1, 2
 # (name, restype, argtypes) for every symbol include/d3b200.h declares.
 _VP, _I, _I64, _F, _SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
 _I64P = ctypes.POINTER(ctypes.c_int64)
+_U64, _U64P = ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64)
+
+
+class CopySegment(ctypes.Structure):
+    """``d3b_copy_segment``: outer x rows rows of row_bytes bytes, byte strides on both sides."""
+
+    _fields_ = [
+        ("src", ctypes.c_void_p),
+        ("dst", ctypes.c_void_p),
+        ("outer", ctypes.c_int64),
+        ("rows", ctypes.c_int64),
+        ("row_bytes", ctypes.c_int64),
+        ("src_outer_stride", ctypes.c_int64),
+        ("src_row_stride", ctypes.c_int64),
+        ("dst_outer_stride", ctypes.c_int64),
+        ("dst_row_stride", ctypes.c_int64),
+    ]
+
+
 SIGNATURES: list[tuple[str, Any, list[Any]]] = [
     ("d3b_version", _I, []),
     ("d3b_error_string", ctypes.c_char_p, [_I]),
@@ -44,6 +63,12 @@ SIGNATURES: list[tuple[str, Any, list[Any]]] = [
     ("d3b_readout", _I, [_VP, _I, _VP, _VP, _F, _VP, _I, _I, _I, _VP, _SZ, _VP]),
     ("d3b_readout_noalloc", _I, [_VP, _I, _VP, _VP, _F, _VP, _I, _I, _I, _VP]),
     ("d3b_selftest_wait_timeout", _I, [_I, _VP]),
+    ("d3b_copy_segments", _I, [ctypes.POINTER(CopySegment), _I, _VP]),
+    ("d3b_arena_create", _I, [_U64, _U64, ctypes.POINTER(ctypes.c_void_p)]),
+    ("d3b_arena_alloc", _I, [_VP, _U64, _U64P]),
+    ("d3b_arena_free", _I, [_VP, _U64]),
+    ("d3b_arena_stats", _I, [_VP, _U64P]),
+    ("d3b_arena_destroy", None, [_VP]),
 ]
 
 _lock = threading.Lock()

@@ -7,7 +7,8 @@ device footprint) and as a quick device-time probe: it prints the median
 CUDA-event time per launch and the algorithmic work per launch. Configs follow
 cfg3a (4096-token state + 16 x 64-token blocks), cfg3b (16384 +
 255 x 48), state4k (the state pass of cfg3a), cfg2 (W8A8 4096 x 5120 x 13824),
-cfg4 (readout 255 x 5120 x 255). Inputs are seeded synthetic tensors.
+cfg4 (readout 255 x 5120 x 255; snapshot: the 64-layer state snapshot at a
+4096-token state, packed by one copy launch). Inputs are seeded synthetic tensors.
 """
 
 from __future__ import annotations
@@ -21,6 +22,7 @@ import torch
 from .kernels import prefix_bidir as pb
 from .model import quant
 from .model.readout import probabilities_tensor
+from .model.snapshot import AttentionEntry, DeltaEntry, SnapshotArena, SnapshotLayout, copy_segments
 
 ATTN = {
     "cfg3a": dict(B=16, H=32, Hkv=4, L=64, D=128, S=4096),
@@ -79,6 +81,44 @@ def _readout(dev: torch.device, B=255, K=5120, n_opt=255):
         "flops": 2.0 * B * K * n_opt, "bytes": B * K * 2 + n_opt * K * 4 + B * n_opt * 4}
 
 
+def state_snapshot(dev: torch.device, S: int = 4096, layers: int = 64, Hkv: int = 4, D: int = 128,
+                   conv_dim: int = 10240, Hv: int = 48, dk: int = 128, dv: int = 128, window: int = 3,
+                   shared_parent: bool = False) -> list:
+    """The snapshot D3Core's state pass leaves for the 64-layer model (every 4th layer full
+    attention): K token-major after RoPE and V as a transposed view of v_proj's output
+    (core.py:233-251); the GDN conv tail as the last ``window`` columns of the whole
+    in_proj_qkv output and an fp32 recurrent state (core.py:301-358). ``shared_parent``
+    cuts every tail from one in_proj_qkv buffer instead of one per layer (same copy work,
+    80 MiB instead of 3.75 GiB on the device)."""
+    g = torch.Generator(device=dev).manual_seed(5)
+    snap, mixed = [], None
+    for i in range(layers):
+        if i % 4 == 3:
+            k = torch.randn(1, S, Hkv, D, generator=g, device=dev).to(torch.bfloat16).transpose(1, 2)
+            v = torch.randn(1, S, Hkv * D, generator=g, device=dev).to(torch.bfloat16)
+            snap.append(AttentionEntry(keys=k, values=v.view(1, S, Hkv, D).transpose(1, 2)))
+        else:
+            if mixed is None or not shared_parent:
+                mixed = torch.randn(1, S, conv_dim, generator=g, device=dev).to(torch.bfloat16).transpose(1, 2)
+            rec = torch.randn(1, Hv, dk, dv, generator=g, device=dev)
+            snap.append(DeltaEntry(tail=mixed[:, :, -window:], recurrent=rec))
+    return snap
+
+
+def _snapshot(dev: torch.device):
+    snap = state_snapshot(dev, shared_parent=True)
+    layout = SnapshotLayout.of(snap)
+    arena = SnapshotArena(layout.nbytes, dev)
+    block = arena.allocate(layout.nbytes)
+    table = layout.table(snap, arena.buffer.data_ptr() + block.offset)
+
+    def run():  # holds the snapshot, arena and block alive with the table
+        copy_segments(table, dev)
+        return snap, arena, block
+
+    return run, {"bytes": 2 * layout.tensor_bytes}
+
+
 def build(kernel: str, config: str, dev: torch.device):
     if kernel == "attention":
         return _state(dev) if config == "state4k" else _attention(config, dev)
@@ -92,13 +132,16 @@ def build(kernel: str, config: str, dev: torch.device):
         return _act_quant("int8", dev)
     if kernel == "readout":
         return _readout(dev)
+    if kernel == "snapshot":
+        return _snapshot(dev)
     raise SystemExit(f"unknown kernel {kernel!r}")
 
 
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", required=True,
-                    choices=["attention", "gemm_fp8", "gemm_int8", "act_quant_fp8", "act_quant_int8", "readout"])
+                    choices=["attention", "gemm_fp8", "gemm_int8", "act_quant_fp8", "act_quant_int8", "readout",
+                             "snapshot"])
     ap.add_argument("--config", default="cfg3a", choices=[*ATTN, "state4k", "cfg2", "cfg4"])
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=1)

@@ -192,6 +192,47 @@ D3B_API int d3b_readout_noalloc(const void* hidden, int h_dtype, const float* re
  */
 D3B_API int d3b_selftest_wait_timeout(int limit_ms, d3b_stream_t stream);
 
+/*
+ * State snapshots (the per-layer K/V and GDN states one state pass leaves
+ * behind; replaces the tensor lists that d3trt/model/core.py:28-40 defines and
+ * d3trt/model/cache.py:50-184 caches).
+ *
+ * d3b_copy_segments: one launch copies `n` strided byte segments. Segment i
+ * moves outer x rows rows of row_bytes contiguous bytes; the row (o, r) starts
+ * at src + o*src_outer_stride + r*src_row_stride and lands at
+ * dst + o*dst_outer_stride + r*dst_row_stride (byte strides, any sign). Source
+ * and destination ranges must not overlap. The widest access (16, 8, 4, 2 or 1
+ * bytes) that divides every address, row size and used stride of a segment is
+ * chosen per segment. Empty segments are skipped. Up to 128 segments go into
+ * one launch (the table travels as the kernel's parameter, so the call
+ * allocates and copies nothing else and can be captured in a CUDA graph).
+ */
+typedef struct d3b_copy_segment {
+  const void* src;
+  void* dst;
+  int64_t outer, rows, row_bytes;
+  int64_t src_outer_stride, src_row_stride;
+  int64_t dst_outer_stride, dst_row_stride;
+} d3b_copy_segment;
+
+D3B_API int d3b_copy_segments(const d3b_copy_segment* segments, int n, d3b_stream_t stream);
+
+/*
+ * Snapshot arena: host-side bookkeeping of one caller-owned device buffer of
+ * `capacity` bytes. Blocks are `alignment`-aligned (a power of two >= 16),
+ * placed best-fit and coalesced on free. The arena touches no device memory;
+ * it only hands out offsets. Thread-safe.
+ *   d3b_arena_alloc  -> D3B_ENOSPACE when no free range holds `bytes`
+ *   d3b_arena_free   -> D3B_EINVAL when `offset` is not a live block
+ *   d3b_arena_stats  -> stats[0] bytes in live blocks, [1] free bytes,
+ *                       [2] largest free range, [3] live blocks
+ */
+D3B_API int d3b_arena_create(uint64_t capacity, uint64_t alignment, void** arena);
+D3B_API int d3b_arena_alloc(void* arena, uint64_t bytes, uint64_t* offset);
+D3B_API int d3b_arena_free(void* arena, uint64_t offset);
+D3B_API int d3b_arena_stats(void* arena, uint64_t* stats);
+D3B_API void d3b_arena_destroy(void* arena);
+
 #ifdef __cplusplus
 }
 #endif

@@ -104,6 +104,22 @@ def test_readout_rejects_bad_arguments():
     assert lib.d3b_readout(a, _lib.BF16, a, a, 1.0, a, 8 * 4096 + 1, 64, 255, a, 1 << 40, None) == _lib.EINVAL
 
 
+def test_copy_segments_rejects_bad_arguments():
+    lib = _lib.lib()
+    seg = _lib.CopySegment
+    p = 4096
+    one = (seg * 1)(seg(p, p * 2, 1, -1, 16, 0, 0, 0, 0))
+    assert lib.d3b_copy_segments(one, 1, None) == _lib.EINVAL  # negative rows
+    one = (seg * 1)(seg(None, p, 1, 1, 16, 0, 0, 0, 0))
+    assert lib.d3b_copy_segments(one, 1, None) == _lib.EINVAL  # null source with bytes to move
+    one = (seg * 1)(seg(p, p * 2, 1 << 31, 1, 16, 0, 0, 0, 0))
+    assert lib.d3b_copy_segments(one, 1, None) == _lib.EINVAL  # outer count past 2^31 - 1
+    assert lib.d3b_copy_segments(None, -1, None) == _lib.EINVAL
+    assert lib.d3b_copy_segments(None, 0, None) == _lib.OK  # nothing to copy: no launch
+    empty = (seg * 2)(seg(None, None, 0, 1, 16, 0, 0, 0, 0), seg(p, p, 3, 4, 0, 0, 0, 0, 0))
+    assert lib.d3b_copy_segments(empty, 2, None) == _lib.OK  # empty segments are skipped
+
+
 def test_wait_selftest_rejects_bad_limit():
     assert _lib.lib().d3b_selftest_wait_timeout(0, None) == _lib.EINVAL
     assert _lib.lib().d3b_selftest_wait_timeout(10_000, None) == _lib.EINVAL
