@@ -25,7 +25,8 @@ namespace {
 constexpr int kMaxSegs = 128;
 constexpr int kTileShift = 15;  // 32 KiB of one segment per tile
 constexpr int kThreads = 256;
-constexpr int kUnroll = 4;  // accesses in flight per thread: 64 KiB per SM at 4 CTAs of 256
+constexpr int kUnroll = 8;  // contiguous runs: 16-byte accesses in flight per thread (128 KiB per SM)
+constexpr int kUnrollStrided = 4;
 constexpr uint64_t kMaxVecs = 1ull << 31;  // accesses per (split) segment
 
 struct Seg {
@@ -66,7 +67,7 @@ __device__ __forceinline__ void copy_flat(const Seg& s, unsigned vbeg, unsigned 
 // Several rows per tile: each access index is split into (outer, row, column).
 template <typename V>
 __device__ __forceinline__ void copy_strided(const Seg& s, unsigned vbeg, unsigned vend) {
-  constexpr int U = kUnroll;
+  constexpr int U = kUnrollStrided;
 #pragma unroll 1
   for (unsigned base = vbeg + threadIdx.x; base < vend; base += U * kThreads) {
     V v[U];
@@ -89,16 +90,9 @@ __device__ __forceinline__ void copy_strided(const Seg& s, unsigned vbeg, unsign
   }
 }
 
-template <typename V>
-__device__ __forceinline__ void copy_tile(const Seg& s, unsigned vbeg, unsigned vend) {
-  if (s.outer == 1 && s.rows == 1)
-    copy_flat<V>(s, vbeg, vend);
-  else
-    copy_strided<V>(s, vbeg, vend);
-}
-
-// One instantiation per access width keeps each path's registers to itself.
-template <typename V>
+// One instantiation per access width and per shape (one contiguous run, or rows)
+// keeps each path's registers to itself.
+template <typename V, bool kFlat>
 __global__ void __launch_bounds__(kThreads, 4) copy_segments_kernel(const __grid_constant__ SegTable t) {
   const unsigned total = t.prefix[t.n];
 #pragma unroll 1
@@ -113,7 +107,10 @@ __global__ void __launch_bounds__(kThreads, 4) copy_segments_kernel(const __grid
     const unsigned nvec = s.outer * s.rows * s.row_vecs;
     const unsigned vbeg = (tile - t.prefix[lo]) * per_tile;
     const unsigned vend = min(vbeg + per_tile, nvec);
-    copy_tile<V>(s, vbeg, vend);
+    if constexpr (kFlat)
+      copy_flat<V>(s, vbeg, vend);
+    else
+      copy_strided<V>(s, vbeg, vend);
   }
 }
 
@@ -128,42 +125,53 @@ int vec_shift(const d3b_copy_segment& g) {
 }
 
 struct Launcher {
-  SegTable table[5];  // one per access width, index = log2(bytes)
+  SegTable table[5][2];  // [log2(access bytes)][one contiguous run]
   cudaStream_t stream;
   int status = D3B_OK;
 
   explicit Launcher(cudaStream_t s) : stream(s) {
-    for (SegTable& t : table) {
-      t.n = 0;
-      t.prefix[0] = 0;
-    }
+    for (auto& per_width : table)
+      for (SegTable& t : per_width) {
+        t.n = 0;
+        t.prefix[0] = 0;
+      }
   }
 
-  void flush(int sh) {
-    SegTable& t = table[sh];
+  template <typename V>
+  void launch(const SegTable& t, bool flat, int grid) {
+    if (flat)
+      copy_segments_kernel<V, true><<<grid, kThreads, 0, stream>>>(t);
+    else
+      copy_segments_kernel<V, false><<<grid, kThreads, 0, stream>>>(t);
+  }
+
+  void flush(int sh, int flat) {
+    SegTable& t = table[sh][flat];
     if (status != D3B_OK || t.n == 0) return;
     const unsigned tiles = t.prefix[t.n];
     const int grid = (int)std::min<unsigned>(tiles, (unsigned)d3b_host::num_sms(d3b_host::current_device()) * 4u);
     switch (sh) {
-      case 4: copy_segments_kernel<uint4><<<grid, kThreads, 0, stream>>>(t); break;
-      case 3: copy_segments_kernel<uint2><<<grid, kThreads, 0, stream>>>(t); break;
-      case 2: copy_segments_kernel<unsigned int><<<grid, kThreads, 0, stream>>>(t); break;
-      case 1: copy_segments_kernel<unsigned short><<<grid, kThreads, 0, stream>>>(t); break;
-      default: copy_segments_kernel<unsigned char><<<grid, kThreads, 0, stream>>>(t); break;
+      case 4: launch<uint4>(t, flat, grid); break;
+      case 3: launch<uint2>(t, flat, grid); break;
+      case 2: launch<unsigned int>(t, flat, grid); break;
+      case 1: launch<unsigned short>(t, flat, grid); break;
+      default: launch<unsigned char>(t, flat, grid); break;
     }
     status = d3b_host::check_launch();
     t.n = 0;
   }
 
   void flush_all() {
-    for (int sh = 4; sh >= 0; --sh) flush(sh);
+    for (int sh = 4; sh >= 0; --sh)
+      for (int flat = 1; flat >= 0; --flat) flush(sh, flat);
   }
 
   // Append one piece of at most kMaxVecs accesses.
   void add(const unsigned char* src, unsigned char* dst, long long s_outer, long long s_row, long long d_outer,
            long long d_row, uint64_t outer, uint64_t rows, uint64_t row_vecs, int sh) {
-    SegTable& t = table[sh];
-    if (t.n == kMaxSegs) flush(sh);
+    const int flat = (outer == 1 && rows == 1) ? 1 : 0;
+    SegTable& t = table[sh][flat];
+    if (t.n == kMaxSegs) flush(sh, flat);
     if (status != D3B_OK) return;
     Seg& s = t.seg[t.n];
     s.src = src;
@@ -180,7 +188,7 @@ struct Launcher {
     t.prefix[t.n + 1] = t.prefix[t.n] + (unsigned)tiles;
     ++t.n;
     // keep the launch's tile count well inside 32 bits
-    if (t.prefix[t.n] > (1u << 30)) flush(sh);
+    if (t.prefix[t.n] > (1u << 30)) flush(sh, flat);
   }
 
   // Split a validated segment into pieces of at most kMaxVecs accesses.

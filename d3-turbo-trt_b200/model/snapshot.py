@@ -14,7 +14,8 @@ GDN layer keeps a ``[S, conv_dim]`` buffer alive (80 MiB at S = 4096) while
 and the order of its strides (a token-major K stays token-major, the layout the
 attention kernel reads through TMA) and becomes dense, so a packed state holds
 exactly its tensor bytes, 256-byte aligned per tensor. The result is a
-``PackedSnapshot``: a list of entries of the same classes as the input, which
+``PackedSnapshot``: a list of entries of the same classes as the input (bare tensors
+are entries too), which
 ``D3Core.questions`` and ``prefix_bidir_attention`` take unchanged.
 
 Lifetime: a block goes back to the arena when the last reference to its
@@ -115,9 +116,16 @@ def _plan_copy(shape: tuple[int, ...], strides: tuple[int, ...]) -> tuple[tuple[
 
 
 def _fields(entry: Any) -> tuple[str, ...]:
+    """Field names of an entry; a bare tensor entry has the one field ""."""
+    if isinstance(entry, torch.Tensor):
+        return ("",)
     if not dataclasses.is_dataclass(entry):
-        raise TypeError(f"snapshot entries must be dataclasses of tensors, got {type(entry).__name__}")
+        raise TypeError(f"snapshot entries must be tensors or dataclasses of tensors, got {type(entry).__name__}")
     return tuple(f.name for f in dataclasses.fields(entry))
+
+
+def _get(entry: Any, name: str) -> Any:
+    return entry if name == "" else getattr(entry, name)
 
 
 @dataclass(frozen=True, slots=True)
@@ -160,9 +168,9 @@ class SnapshotLayout:
         sig = []
         for entry in snapshot:
             fields = _fields(entry)
-            sig.append(type(entry))
+            sig.append(torch.Tensor if isinstance(entry, torch.Tensor) else type(entry))
             for name in fields:
-                t = getattr(entry, name)
+                t = _get(entry, name)
                 sig.append((name, None) if t is None else (name, tuple(t.shape), t.stride(), t.dtype))
         key = tuple(sig)
         hit = _LAYOUTS.get(key)
@@ -198,7 +206,7 @@ class SnapshotLayout:
         """The ``d3b_copy_segment`` rows that copy ``snapshot`` into a block at device address ``base``."""
         src = np.zeros(len(self.slots), dtype=np.int64)
         for i, s in enumerate(self.slots):
-            t = getattr(snapshot[s.entry], s.field)
+            t = _get(snapshot[s.entry], s.field)
             if t is not None:
                 src[i] = t.data_ptr()
         out = self.segments.copy()
@@ -254,6 +262,16 @@ class SnapshotArena:
         self.buffer = torch.empty(self.capacity_bytes, dtype=torch.uint8, device=dev)
         self._lock = threading.RLock()
         self._pending: collections.deque[tuple[int, torch.cuda.Event]] = collections.deque()
+        self._typed: dict[torch.dtype, torch.Tensor] = {}
+
+    def typed(self, dtype: torch.dtype) -> torch.Tensor:
+        """The whole buffer viewed as ``dtype`` (cached); element offsets are byte offsets / itemsize."""
+        view = self._typed.get(dtype)
+        if view is None:
+            es = dtype.itemsize
+            view = self.buffer[: self.capacity_bytes - self.capacity_bytes % es].view(dtype)
+            self._typed[dtype] = view
+        return view
 
     def allocate(self, nbytes: int) -> _Block | None:
         """A block of at least ``nbytes`` bytes, or None when no free range is large enough."""
@@ -302,13 +320,15 @@ class PackedSnapshot(list):
     @classmethod
     def _from_block(cls, block: _Block, layout: SnapshotLayout) -> "PackedSnapshot":
         fields: list[dict[str, Any]] = [{} for _ in layout.types]
-        raw = block.bytes_view()
+        arena = block.arena
         for s in layout.slots:
             if s.shape is None:
                 fields[s.entry][s.field] = None
-            else:
-                fields[s.entry][s.field] = raw.narrow(0, s.offset, s.nbytes).view(s.dtype).as_strided(s.shape, s.strides)
-        out = cls(typ(**kw) for typ, kw in zip(layout.types, fields))
+            else:  # one as_strided over the arena viewed in the slot's dtype
+                es = s.dtype.itemsize
+                fields[s.entry][s.field] = torch.as_strided(arena.typed(s.dtype), s.shape, s.strides,
+                                                            (block.offset + s.offset) // es)
+        out = cls(kw[""] if typ is torch.Tensor else typ(**kw) for typ, kw in zip(layout.types, fields))
         out.block, out.layout = block, layout
         return out
 
@@ -370,7 +390,7 @@ def pack_snapshot(snapshot: Sequence[Any], arena: SnapshotArena,
     """Copy a snapshot into one arena block (one launch); None when the arena has no room."""
     layout = layout or SnapshotLayout.of(snapshot)
     for s in layout.slots:
-        t = getattr(snapshot[s.entry], s.field)
+        t = _get(snapshot[s.entry], s.field)
         if t is not None and t.device != arena.device:
             raise RuntimeError(f"snapshot tensor on {t.device}, arena on {arena.device}")
     block = arena.allocate(layout.nbytes)

@@ -50,6 +50,47 @@ def test_replays_reference_trace(name):
         assert gen.observe(cache) == step["after"], f"step {i} {step['call']}"
 
 
+class _FakeArena:
+    """Host stand-in for SnapshotArena: tracks bytes only (the copy itself needs a GPU)."""
+
+    def __init__(self, capacity):
+        self.capacity, self.used, self.live = capacity, 0, {}
+
+    def stats(self):
+        return {"used_bytes": self.used}
+
+
+@pytest.mark.parametrize("name", ["lru", "tight"])
+def test_arena_mode_evicts_like_the_reference(name, monkeypatch):
+    """With an arena the eviction set is chosen before the copy; it must equal the reference's
+    post-insert trim, and a full arena falls back to keeping the caller's tensors."""
+    trace = json.loads((GOLDEN / "cache_trace.json").read_text())[name]
+    gen = _load_trace_module()
+    arena = _FakeArena(3 * max(trace["capacity"], 1))
+
+    class Packed(list):
+        def __del__(self):
+            arena.used -= self.nbytes
+
+    def fake_pack(snapshot, arena_, layout):
+        assert arena_ is arena
+        if arena.used + layout.nbytes > arena.capacity:
+            return None
+        out = Packed(snapshot)
+        out.nbytes = layout.nbytes
+        arena.used += layout.nbytes
+        return out
+
+    monkeypatch.setattr(dcache, "pack_snapshot", fake_pack)
+    cache = dcache.StateCache(trace["capacity"], arena=arena)
+    for i, step in enumerate(trace["steps"]):
+        got = gen.apply(cache, step["call"], dcache.StateCacheError)
+        assert got == step["result"], f"step {i} {step['call']}"
+        assert gen.observe(cache) == step["after"], f"step {i} {step['call']}"
+    stats = cache.stats()
+    assert stats["arena"]["used_bytes"] == arena.used and "arena_fallbacks" in stats
+
+
 def test_tensor_bytes_nested():
     payload = [torch.zeros(2, 3, dtype=torch.float32), (torch.zeros(4, dtype=torch.float16),)]
     assert dcache.tensor_bytes(payload) == 2 * 3 * 4 + 4 * 2
@@ -154,6 +195,47 @@ def test_layout_offsets_and_bytes():
     # packed bytes are the tensor bytes: the tail no longer stands for its whole parent buffer
     assert layout.tensor_bytes == dcache.tensor_bytes(snap)
     assert tensors[2].untyped_storage().nbytes() > 10 * tensors[2].numel() * tensors[2].element_size()
+
+
+def test_layout_of_bare_tensors_and_cache_keys():
+    """Entries may be bare tensors (the reference cache takes any tensor list); layouts are cached."""
+    snap = [torch.zeros(64), torch.zeros(3, 5).t(), DeltaEntry(torch.zeros(1, 4, 3), None)]
+    a, b = SnapshotLayout.of(snap), SnapshotLayout.of([torch.ones(64), torch.ones(3, 5).t(), snap[2]])
+    assert a is b and a.types == [torch.Tensor, torch.Tensor, DeltaEntry]
+    assert [s.offset for s in a.slots] == [0, 256, 512, 768] and a.tensor_bytes == 256 + 60 + 48
+    assert SnapshotLayout.of([torch.zeros(64, dtype=torch.float64)]) is not a
+
+
+def test_packed_views_read_the_packed_bytes():
+    """PackedSnapshot views over a block filled by the packing oracle equal the source tensors."""
+    from d3_turbo_trt_b200.model import snapshot as sn
+
+    tensors = _views(3)
+    tensors.append(None)
+    snap = [AttentionEntry(tensors[i], tensors[i + 1]) for i in range(0, len(tensors), 2)]
+    layout = SnapshotLayout.of(snap)
+
+    class Arena:  # host stand-in: the views only need the buffer and its typed views
+        typed = sn.SnapshotArena.typed
+
+        def __init__(self, nbytes):
+            self.capacity_bytes, self._typed = nbytes, {}
+            self.buffer = torch.zeros(nbytes, dtype=torch.uint8)
+
+    class Block:
+        def __init__(self, arena, offset):
+            self.arena, self.offset = arena, offset
+
+    arena = Arena(layout.nbytes + 1024)
+    placed, _ = osnap.pack(tensors)
+    buf = arena.buffer.numpy()
+    for off, want in placed:
+        buf[512 + off: 512 + off + len(want)] = want
+    packed = sn.PackedSnapshot._from_block(Block(arena, 512), layout)
+    for e_src, e_pk in zip(snap, packed):
+        for name in ("keys", "values"):
+            a, b = getattr(e_src, name), getattr(e_pk, name)
+            assert (a is None and b is None) or (a.shape == b.shape and torch.equal(a, b))
 
 
 def test_dense_tensor_is_one_piece():

@@ -57,8 +57,18 @@ def _flat(snapshot):
     return [getattr(e, f.name) for e in snapshot for f in dataclasses.fields(e)]
 
 
+def _same_view(t: torch.Tensor, device) -> torch.Tensor:
+    """The same view (shape, strides, storage offset) over a copy of its whole storage on ``device``
+    (``Tensor.to`` would make sliced and broadcast views contiguous)."""
+    n = t.untyped_storage().nbytes() // t.element_size()
+    if n == 0:
+        return torch.empty(t.shape, dtype=t.dtype, device=device)
+    whole = torch.as_strided(t, (n,), (1,), 0).to(device)
+    return whole.as_strided(t.shape, t.stride(), t.storage_offset())
+
+
 def _check_block(packed: PackedSnapshot, tensors):
-    placed, total = osnap.pack([None if t is None else t.cpu() for t in tensors])
+    placed, total = osnap.pack([None if t is None else _same_view(t, "cpu") for t in tensors])
     raw = packed.block.bytes_view().cpu().numpy()
     assert packed.layout.nbytes == total
     for off, want in placed:
@@ -70,19 +80,11 @@ def _check_block(packed: PackedSnapshot, tensors):
         assert v.shape == t.shape and v.dtype == t.dtype and torch.equal(v, t)
 
 
-def _on_device(t: torch.Tensor) -> torch.Tensor:
-    """The same view (shape, strides, storage offset) over a device copy of its storage."""
-    if t.untyped_storage().nbytes() == 0:
-        return torch.empty(t.shape, dtype=t.dtype, device=DEV)
-    base = torch.frombuffer(bytearray(bytes(t.untyped_storage())), dtype=torch.uint8).to(DEV)
-    return base.view(t.dtype).as_strided(t.shape, t.stride(), t.storage_offset())
-
-
 def test_pack_matches_oracle_all_widths():
     """Strided, sliced, broadcast, empty, 0-d and misaligned tensors (16/8/4/2/1-byte paths)."""
     arena = SnapshotArena(1 << 20, DEV)
     for seed in range(3):
-        tensors = [_on_device(t) for t in _views(seed)]
+        tensors = [_same_view(t, DEV) for t in _views(seed)]
         tensors.append(None)
         snap = [AttentionEntry(keys=tensors[i], values=tensors[i + 1]) for i in range(0, len(tensors), 2)]
         packed = pack_snapshot(snap, arena)
