@@ -8,7 +8,8 @@ CUDA-event time per launch and the algorithmic work per launch. Configs follow
 cfg3a (4096-token state + 16 x 64-token blocks), cfg3b (16384 +
 255 x 48), state4k (the state pass of cfg3a), cfg2 (W8A8 4096 x 5120 x 13824),
 cfg4 (readout 255 x 5120 x 255; snapshot: the 64-layer state snapshot at a
-4096-token state, packed by one copy launch). Inputs are seeded synthetic tensors.
+4096-token state, packed by one copy launch; gdn: one GDN layer's question pass,
+255 blocks x 48 tokens x 48 value heads). Inputs are seeded synthetic tensors.
 """
 
 from __future__ import annotations
@@ -21,6 +22,7 @@ import torch
 
 from .kernels import prefix_bidir as pb
 from .model import quant
+from .model import gdn
 from .model.readout import probabilities_tensor
 from .model.snapshot import AttentionEntry, DeltaEntry, SnapshotArena, SnapshotLayout, copy_segments
 
@@ -119,6 +121,32 @@ def _snapshot(dev: torch.device):
     return run, {"bytes": 2 * layout.tensor_bytes}
 
 
+def gdn_question_inputs(dev: torch.device, B: int = 255, T: int = 48, H: int = 16, HV: int = 48, K: int = 128,
+                        V: int = 128, seed: int = 6) -> dict:
+    """One GDN layer's question pass as D3Core runs it at BASELINE config 3b/4 (255 blocks of 48
+    tokens; 16 q/k heads, 48 value heads of 128, core.py:333-347), state from the snapshot."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    return {
+        "q": torch.randn(B, T, H, K, generator=g, device=dev).to(torch.bfloat16),
+        "k": torch.randn(B, T, H, K, generator=g, device=dev).to(torch.bfloat16),
+        "v": torch.randn(B, T, HV, V, generator=g, device=dev).to(torch.bfloat16),
+        "g": -torch.rand(B, T, HV, generator=g, device=dev) * 0.5,
+        "beta": torch.sigmoid(torch.randn(B, T, HV, generator=g, device=dev)).to(torch.bfloat16),
+        "h0": torch.randn(1, HV, K, V, generator=g, device=dev) * 0.5,
+    }
+
+
+def _gdn(dev: torch.device):
+    x = gdn_question_inputs(dev)
+    B = x["q"].shape[0]
+    out = torch.empty_like(x["v"])
+    fn = lambda: gdn.gated_delta_rule(x["q"], x["k"], x["v"], g=x["g"], beta=x["beta"],
+                                      initial_state=x["h0"].expand(B, -1, -1, -1), out=out)
+    B, T, H, K = x["q"].shape
+    HV, V = x["v"].shape[2:]
+    return fn, {"flops": 2.0 * 3 * B * T * HV * K * V}
+
+
 def build(kernel: str, config: str, dev: torch.device):
     if kernel == "attention":
         return _state(dev) if config == "state4k" else _attention(config, dev)
@@ -134,6 +162,8 @@ def build(kernel: str, config: str, dev: torch.device):
         return _readout(dev)
     if kernel == "snapshot":
         return _snapshot(dev)
+    if kernel == "gdn":
+        return _gdn(dev)
     raise SystemExit(f"unknown kernel {kernel!r}")
 
 
@@ -141,7 +171,7 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", required=True,
                     choices=["attention", "gemm_fp8", "gemm_int8", "act_quant_fp8", "act_quant_int8", "readout",
-                             "snapshot"])
+                             "snapshot", "gdn"])
     ap.add_argument("--config", default="cfg3a", choices=[*ATTN, "state4k", "cfg2", "cfg4"])
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=1)

@@ -193,6 +193,29 @@ D3B_API int d3b_readout_noalloc(const void* hidden, int h_dtype, const float* re
 D3B_API int d3b_selftest_wait_timeout(int limit_ms, d3b_stream_t stream);
 
 /*
+ * Gated delta rule: the GDN layers' scan, token-recurrent, fp32 state. Replaces
+ * FLA's fused_recurrent_gated_delta_rule as the reference calls it
+ * (d3trt/model/ops.py:327-360, d3trt/model/core.py:360-372) and, for the same
+ * math, chunk_gated_delta_rule (ops.py:287-324). Per (row, value head), over t:
+ *   S <- exp(g_t) S;  v' = beta_t (v_t - S^T k_t);  S <- S + k_t v'^T;  o_t = S^T q_t
+ *   q, k [B, T, H, K]; v, o [B, T, HV, V]: `dtype` (D3B_BF16 / D3B_F16), innermost
+ *     dim contiguous, *_strides = element strides of (b, t, head); the q/k head
+ *     of value head hv is hv / (HV / H) (no repeated q/k needed)
+ *   g [B, T, HV] f32 (log decay); beta [B, T, HV] in beta_dtype (F32/BF16/F16)
+ *   h0 [B, HV, K, V] f32 or NULL (zeros); h0_strides = (b, hv, k-row), V
+ *     contiguous; a b stride of 0 shares one state across rows
+ *   ht [B, HV, K, V] f32 contiguous or NULL: the final state
+ *   K in {64, 128}, V % 32 == 0, HV % H == 0. l2norm != 0 divides q and k by
+ *   sqrt(sum x^2 + 1e-6); q is then multiplied by scale.
+ */
+D3B_API int d3b_gated_delta_rule(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                                 const void* v, const int64_t* v_strides, const float* g, const int64_t* g_strides,
+                                 const void* beta, int beta_dtype, const int64_t* beta_strides, const float* h0,
+                                 const int64_t* h0_strides, void* o, const int64_t* o_strides, float* ht, int B,
+                                 int T, int H, int HV, int K, int V, int dtype, float scale, int l2norm,
+                                 d3b_stream_t stream);
+
+/*
  * State snapshots (the per-layer K/V and GDN states one state pass leaves
  * behind; replaces the tensor lists that d3trt/model/core.py:28-40 defines and
  * d3trt/model/cache.py:50-184 caches).

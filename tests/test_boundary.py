@@ -120,6 +120,26 @@ def test_copy_segments_rejects_bad_arguments():
     assert lib.d3b_copy_segments(empty, 2, None) == _lib.OK  # empty segments are skipped
 
 
+def test_gated_delta_rejects_bad_arguments():
+    lib = _lib.lib()
+    p = ctypes.c_void_p(256)
+    st = _lib.i64_array([1000, 100, 10])
+
+    def call(B=2, T=3, H=1, HV=2, K=64, V=64, dtype=_lib.BF16, beta_dtype=_lib.BF16, ptr=p, strides=st):
+        return lib.d3b_gated_delta_rule(ptr, strides, ptr, strides, ptr, strides, ptr, strides, ptr, beta_dtype,
+                                        strides, None, None, ptr, strides, None, B, T, H, HV, K, V, dtype, 0.125,
+                                        1, None)
+
+    assert call(K=96) == _lib.EUNSUPPORTED
+    assert call(V=48) == _lib.EINVAL
+    assert call(HV=3, H=2) == _lib.EINVAL
+    assert call(dtype=_lib.F32) == _lib.EUNSUPPORTED
+    assert call(beta_dtype=_lib.I32) == _lib.EUNSUPPORTED
+    assert call(strides=None) == _lib.EINVAL
+    assert call(ptr=ctypes.c_void_p(257)) == _lib.EALIGN
+    assert call(B=0) == _lib.OK  # nothing to do: no launch
+
+
 def test_wait_selftest_rejects_bad_limit():
     assert _lib.lib().d3b_selftest_wait_timeout(0, None) == _lib.EINVAL
     assert _lib.lib().d3b_selftest_wait_timeout(10_000, None) == _lib.EINVAL

@@ -1,0 +1,122 @@
+"""GPU parity of d3b_gated_delta_rule against the fp64 oracle (pinned to the reference's
+CPU paths by test_gdn_oracle.py). Outputs are rounded to bf16/fp16: |err| <= 4e-3 +
+8e-3 |ref|; final states are fp32: |err| <= 2e-5 + 2e-4 |ref|."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.gated_delta import gated_delta_rule as oracle_gdr
+from test_gdn_oracle import golden_case
+
+from d3_turbo_trt_b200 import _lib
+from d3_turbo_trt_b200.model import gdn
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def _close_o(got, ref):
+    got = got.float().cpu().numpy()
+    assert np.all(np.abs(got - ref) <= 4e-3 + 8e-3 * np.abs(ref)), np.abs(got - ref).max()
+
+
+def _close_s(got, ref):
+    got = got.cpu().numpy()
+    assert np.all(np.abs(got - ref) <= 2e-5 + 2e-4 * np.abs(ref)), np.abs(got - ref).max()
+
+
+def _inputs(B, T, H, HV, K, V, seed, dtype=torch.bfloat16, shared_h0=True):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, T, H, K, generator=g).to(dtype)
+    k = torch.randn(B, T, H, K, generator=g).to(dtype)
+    v = torch.randn(B, T, HV, V, generator=g).to(dtype)
+    gl = -torch.rand(B, T, HV, generator=g) * 0.5
+    beta = torch.sigmoid(torch.randn(B, T, HV, generator=g)).to(dtype)
+    h0 = torch.randn(1 if shared_h0 else B, HV, K, V, generator=g) * 0.5
+    return q, k, v, gl, beta, h0
+
+
+@pytest.mark.parametrize("name", ["k64", "k128", "zero_init"])
+def test_golden_cases(name):
+    c = golden_case(name)
+    B, T, H, HV, K, V = c["dims"]
+
+    def dev_bf16(x):
+        return torch.from_numpy(x).to(torch.bfloat16).to(DEV)
+
+    q, k, v, beta = (dev_bf16(c[x]) for x in ("q", "k", "v", "beta"))
+    g = torch.from_numpy(c["g"]).to(DEV)
+    h0 = None if c["h0"] is None else torch.from_numpy(c["h0"]).to(DEV).expand(B, -1, -1, -1)
+    o, s = gdn.gated_delta_rule(q, k, v, g=g, beta=beta, initial_state=h0, output_final_state=True)
+    ro, rs = oracle_gdr(c["q"], c["k"], c["v"], c["g"], c["beta"], c["h0"])
+    _close_o(o, ro)
+    _close_s(s, rs)
+    # the reference's repeated q/k and a per-row copy of the state give identical bits
+    rep = HV // H
+    init = None if h0 is None else h0.contiguous()
+    o2, s2 = gdn.recurrent_gated_delta_rule(q.repeat_interleave(rep, 2), k.repeat_interleave(rep, 2), v, g=g,
+                                            beta=beta, initial_state=init, output_final_state=True)
+    assert torch.equal(o, o2) and torch.equal(s, s2)
+    assert _lib.device_error() == 0
+
+
+def test_question_pass_shape():
+    """Question blocks of 48 tokens, 16 q/k heads feeding 48 value heads, one shared state."""
+    B, T, H, HV, K, V = 6, 48, 16, 48, 128, 128
+    q, k, v, gl, beta, h0 = _inputs(B, T, H, HV, K, V, 1)
+    o, s = gdn.chunk_gated_delta_rule(q.to(DEV), k.to(DEV), v.to(DEV), g=gl.to(DEV), beta=beta.to(DEV),
+                                      initial_state=h0.to(DEV).expand(B, -1, -1, -1), output_final_state=True)
+    ro, rs = oracle_gdr(q.float().numpy(), k.float().numpy(), v.float().numpy(), gl.numpy(), beta.float().numpy(),
+                        h0.numpy())
+    _close_o(o, ro)
+    _close_s(s, rs)
+
+
+def test_fp16_fp32_beta_scale_no_l2norm_and_strided_out():
+    B, T, H, HV, K, V = 3, 20, 2, 4, 64, 96
+    q, k, v, gl, beta, h0 = _inputs(B, T, H, HV, K, V, 2, dtype=torch.float16, shared_h0=False)
+    q, k = q * 0.1, k * 0.1  # no normalisation: keep the state bounded
+    big = torch.zeros(B, T, HV, V + 32, dtype=torch.float16, device=DEV)
+    out = big[..., 16:16 + V]
+    o, s = gdn.gated_delta_rule(q.to(DEV), k.to(DEV), v.to(DEV), g=gl.to(DEV), beta=beta.float().to(DEV),
+                                initial_state=h0.to(DEV), output_final_state=True, use_qk_l2norm_in_kernel=False,
+                                scale=0.3, out=out)
+    assert o.data_ptr() == out.data_ptr()
+    ro, rs = oracle_gdr(q.float().numpy(), k.float().numpy(), v.float().numpy(), gl.numpy(), beta.float().numpy(),
+                        h0.numpy(), scale=0.3, l2norm=False)
+    _close_o(o, ro)
+    _close_s(s, rs)
+    assert not big[..., :16].any() and not big[..., 16 + V:].any()
+
+
+def test_empty_and_single_token():
+    B, H, HV, K, V = 2, 1, 2, 128, 64
+    q, k, v, gl, beta, h0 = _inputs(B, 1, H, HV, K, V, 3)
+    h0d = h0.to(DEV).expand(B, -1, -1, -1)
+    o, s = gdn.gated_delta_rule(q[:, :0].to(DEV), k[:, :0].to(DEV), v[:, :0].to(DEV), g=gl[:, :0].to(DEV),
+                                beta=beta[:, :0].to(DEV), initial_state=h0d, output_final_state=True)
+    assert o.shape == (B, 0, HV, V) and torch.equal(s, h0d)  # no tokens: the state passes through
+    o, s = gdn.gated_delta_rule(q.to(DEV), k.to(DEV), v.to(DEV), g=gl.to(DEV), beta=beta.to(DEV),
+                                initial_state=h0d, output_final_state=True)
+    ro, rs = oracle_gdr(q.float().numpy(), k.float().numpy(), v.float().numpy(), gl.numpy(), beta.float().numpy(),
+                        h0.numpy())
+    _close_o(o, ro)
+    _close_s(s, rs)
+
+
+def test_matches_fla_on_the_same_inputs():
+    """Secondary check against the reference's GPU library (FLA fused recurrent kernel)."""
+    fla = pytest.importorskip("fla.ops.gated_delta_rule")
+    B, T, H, HV, K, V = 4, 48, 16, 48, 128, 128
+    q, k, v, gl, beta, h0 = _inputs(B, T, H, HV, K, V, 4)
+    args = [x.to(DEV) for x in (q.repeat_interleave(3, 2), k.repeat_interleave(3, 2), v)]
+    init = h0.to(DEV).expand(B, -1, -1, -1).contiguous()
+    ref, _ = fla.fused_recurrent_gated_delta_rule(*args, g=gl.to(DEV), beta=beta.to(DEV), initial_state=init,
+                                                  output_final_state=False, use_qk_l2norm_in_kernel=True)
+    o, _ = gdn.recurrent_gated_delta_rule(*args, g=gl.to(DEV), beta=beta.to(DEV), initial_state=init,
+                                          output_final_state=False)
+    err = (o.float() - ref.float()).abs()
+    assert float(err.max()) <= 1e-2, float(err.max())
