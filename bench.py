@@ -594,6 +594,9 @@ def secondary(dev, stream, flush, peaks, quant, pb, d3b):
     del at, gt
     # state snapshot of the 64-layer model at a 4096-token state, packed into one arena block
     res["state_snapshot_4k_64_layers"] = snapshot_line(dev, stream, flush, peaks)
+    # one GDN layer's question pass (255 blocks x 48 tokens, 48 value heads), against the
+    # reference's GPU library kernels on the inputs the reference builds for them
+    res["gdn_question_pass_255x48"] = gdn_line(dev, stream, flush)
     # readout: 255 blocks x 5120 x 255 options
     hidden = torch.randn(255, 5120, generator=g).to(torch.bfloat16).to(dev)
     ro = (torch.randn(255, 5120, generator=g) * 0.02).to(dev)
@@ -602,6 +605,44 @@ def secondary(dev, stream, flush, peaks, quant, pb, d3b):
                                      stream, flush))
     res["readout_255x5120x255"] = {"ms": t}
     return res
+
+
+def gdn_line(dev, stream, flush):
+    """d3b_gated_delta_rule on one GDN layer's question pass; FLA's fused recurrent and chunk
+    kernels (the reference's GPU paths, core.py:360-372) timed on the repeated q/k and the
+    per-row copy of the state they are called with (the copy itself timed apart)."""
+    from d3_turbo_trt_b200.model import gdn
+    from d3_turbo_trt_b200.profile import gdn_question_inputs
+
+    x = gdn_question_inputs(dev)
+    B, T, H, K = x["q"].shape
+    HV, V = x["v"].shape[2:]
+    out = torch.empty_like(x["v"])
+    h0 = x["h0"].expand(B, -1, -1, -1)
+    t_ours = statistics.median(time_steps(lambda: gdn.gated_delta_rule(
+        x["q"], x["k"], x["v"], g=x["g"], beta=x["beta"], initial_state=h0, out=out), 5, 3, stream, flush))
+    flops = 2.0 * 3 * B * T * HV * K * V
+    line = {"ours_ms": t_ours, "tflops_fp32": flops / t_ours / 1e9,
+            "workload": f"{B} blocks x {T} tokens, {H} q/k heads -> {HV} value heads, K=V={K}, shared initial state"}
+    t_copy = statistics.median(time_steps(lambda: h0.contiguous(), 5, 3, stream, flush))
+    line["reference_state_copy_ms"] = t_copy
+    try:
+        from fla.ops.gated_delta_rule import chunk_gated_delta_rule, fused_recurrent_gated_delta_rule
+    except Exception as exc:  # noqa: BLE001 - the library is optional on the box
+        line["fla"] = f"unavailable: {type(exc).__name__}"
+        return line
+    rep = HV // H
+    qr, kr = x["q"].repeat_interleave(rep, 2), x["k"].repeat_interleave(rep, 2)
+    init = h0.contiguous()
+    kw = dict(g=x["g"], beta=x["beta"], initial_state=init, output_final_state=False, use_qk_l2norm_in_kernel=True)
+    line["fla_fused_recurrent_ms"] = statistics.median(time_steps(
+        lambda: fused_recurrent_gated_delta_rule(qr, kr, x["v"], **kw), 5, 3, stream, flush))
+    line["fla_chunk_ms"] = statistics.median(time_steps(
+        lambda: chunk_gated_delta_rule(qr, kr, x["v"], **kw), 5, 3, stream, flush))
+    o_ref, _ = fused_recurrent_gated_delta_rule(qr, kr, x["v"], **kw)
+    o, _ = gdn.gated_delta_rule(x["q"], x["k"], x["v"], g=x["g"], beta=x["beta"], initial_state=h0)
+    line["max_abs_diff_vs_fla_recurrent"] = float((o.float() - o_ref.float()).abs().max())
+    return line
 
 
 def snapshot_line(dev, stream, flush, peaks):

@@ -48,10 +48,11 @@ def gated_delta_rule(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, g: to
         raise RuntimeError(f"gated_delta_rule: g and beta must be [B,T,HV] = {(B, T, HV)}")
     if K not in (64, 128) or V % 32 != 0:
         raise RuntimeError(f"gated_delta_rule: head dims K in (64, 128) and V % 32 == 0 supported, got {K}, {V}")
-    if q.stride(-1) != 1:
-        q = q.contiguous()
-    if k.stride(-1) != 1:
-        k = k.contiguous()
+    e = K // 32  # the kernel copies q/k rows e elements (2e bytes) per lane
+    if q.stride(-1) != 1 or q.data_ptr() % (2 * e) or any(st % e for st in q.stride()[:3]):
+        q = q.contiguous() if q.stride(-1) != 1 or any(st % e for st in q.stride()[:3]) else q.clone()
+    if k.stride(-1) != 1 or k.data_ptr() % (2 * e) or any(st % e for st in k.stride()[:3]):
+        k = k.contiguous() if k.stride(-1) != 1 or any(st % e for st in k.stride()[:3]) else k.clone()
     if v.stride(-1) != 1:
         v = v.contiguous()
     g = g.float()

@@ -123,7 +123,7 @@ def test_copy_segments_rejects_bad_arguments():
 def test_gated_delta_rejects_bad_arguments():
     lib = _lib.lib()
     p = ctypes.c_void_p(256)
-    st = _lib.i64_array([1000, 100, 10])
+    st = _lib.i64_array([1024, 128, 64])
 
     def call(B=2, T=3, H=1, HV=2, K=64, V=64, dtype=_lib.BF16, beta_dtype=_lib.BF16, ptr=p, strides=st):
         return lib.d3b_gated_delta_rule(ptr, strides, ptr, strides, ptr, strides, ptr, strides, ptr, beta_dtype,
