@@ -9,15 +9,20 @@
 // initial state may be shared across rows (row stride 0), so the question pass
 // needs no per-row copy of the snapshot's state (core.py:331).
 //
-// One warp per (row, value head, 32-column block of V); lane j owns column j of the
-// state, all K rows of it in registers, so both reductions over K (k.S and q.S)
-// are thread-local: no shuffles, no barriers. The token's normalised q and k are
-// staged once per warp in shared memory (double-buffered, read as broadcasts);
-// the next token's q/k travel to shared memory by cp.async while the current one
-// is computed. The
+// One warp per (row, value head, 16 state columns); each lane holds an (K/16) x 8
+// tile of the state in registers: half-warp lanes split the rows, the two halves
+// split the columns. The column sums over K (k.S and q.S) finish with a
+// reduce-scatter across the 16 row lanes (8 shuffles: every lane ends with one
+// column's total) and v' goes back with the inverse all-gather (7 shuffles), so
+// each lane reads only its K/16 rows of q and k per token: shared-memory traffic
+// stays far below the shuffle and FMA work. No barriers. The token's normalised
+// q and k are staged once per warp in shared memory (double-buffered);
+// q, k and v travel to shared memory by cp.async three tokens ahead of the one
+// being computed, g and beta 32 tokens at a time (one value per lane, shuffled). The
 // state is kept as c * H with a running scalar c, so the decay costs one
 // multiply per token, and the output uses o = S'^T q + (k.q) v' (S' the decayed
-// state before the update), so each state element costs three FMAs per token.
+// state before the update), so each state element costs three FMAs per token,
+// issued as packed fp32x2 FMAs (two rows per instruction).
 #include "common.cuh"
 
 namespace {
@@ -53,153 +58,226 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { retu
 template <>
 __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
 
-__device__ __forceinline__ float warp_sum(float x) {
-#pragma unroll
-  for (int s = 16; s > 0; s >>= 1) x += __shfl_xor_sync(0xffffffffu, x, s);
-  return x;
+// (d0, d1) += (a0, a1) * (b0, b1): one packed fp32x2 FMA, each lane an IEEE fma
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{.reg .b64 x, y, z; mov.b64 x, {%2, %3}; mov.b64 y, {%4, %5}; mov.b64 z, {%0, %1};"
+      " fma.rn.f32x2 z, x, y, z; mov.b64 {%0, %1}, z;}"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
 
 template <int K, typename In, typename BetaT>
 __global__ void __launch_bounds__(32) gdr_recurrent_kernel(const __grid_constant__ GdrParams p) {
-  constexpr int E = K / 32;  // q/k elements each lane loads per token
-  static_assert(E == 2 || E == 4, "K is 64 or 128");
+  constexpr int E = K / 32;   // q/k elements each lane copies per token
+  constexpr int RL = K / 16;  // state rows per lane
+  constexpr unsigned FULL = 0xffffffffu;
+  static_assert(RL == 4 || RL == 8, "K is 64 or 128");
   const int lane = threadIdx.x;
-  const int n_vb = p.V >> 5;
+  const int hl = lane & 15, cb = lane >> 4;  // row block, column half
+  const int bit3 = (hl >> 3) & 1, bit2 = (hl >> 2) & 1, bit1 = (hl >> 1) & 1;
+  const int jj = bit3 * 4 + bit2 * 2 + bit1;  // the column this lane owns after a reduce-scatter
+  const int n_vb = p.V >> 4;                  // 16 columns per warp
   const long long blk = blockIdx.x;
   const int vb = (int)(blk % n_vb);
   const long long bh = blk / n_vb;
   const int b = (int)(bh / p.HV), hv = (int)(bh % p.HV), h = hv / (p.HV / p.H);
-  const int j = vb * 32 + lane;
+  const int col0 = vb * 16 + cb * 8;  // first of this lane's 8 state columns
+  const int row0 = hl * RL;
 
   __shared__ __align__(16) float qk_s[2][2][K];  // [buffer][q, k][K], normalised
 
-  float S[K];
+  float S[RL][8];
   if (p.h0) {
-    const float* src = p.h0 + b * p.h0s[0] + hv * p.h0s[1] + j;
+    const float* src = p.h0 + b * p.h0s[0] + hv * p.h0s[1] + (long long)row0 * p.h0s[2] + col0;
 #pragma unroll
-    for (int r = 0; r < K; ++r) S[r] = src[(long long)r * p.h0s[2]];
+    for (int i = 0; i < RL; ++i)
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) S[i][c8] = src[(long long)i * p.h0s[2] + c8];
   } else {
 #pragma unroll
-    for (int r = 0; r < K; ++r) S[r] = 0.f;
+    for (int i = 0; i < RL; ++i)
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) S[i][c8] = 0.f;
   }
   float c = 1.f;  // the state is c * S
 
   const In* qp = static_cast<const In*>(p.q) + b * p.qs[0] + h * p.qs[2] + lane * E;
   const In* kp = static_cast<const In*>(p.k) + b * p.ks[0] + h * p.ks[2] + lane * E;
-  const In* vp = static_cast<const In*>(p.v) + b * p.vs[0] + hv * p.vs[2] + j;
   const float* gp = p.g + b * p.gs[0] + hv * p.gs[2];
   const BetaT* bp = static_cast<const BetaT*>(p.beta) + b * p.bs[0] + hv * p.bs[2];
-  In* op = static_cast<In*>(p.o) + b * p.os[0] + hv * p.os[2] + j;
+  In* op = static_cast<In*>(p.o) + b * p.os[0] + hv * p.os[2] + col0 + jj;
 
-  // q/k of the next token arrive in shared memory by cp.async, so nothing is held
-  // in registers while they are in flight; each lane copies, and later reads back,
-  // its own E elements.
-  __shared__ __align__(16) In raw_s[2][2][K];  // [buffer][q, k][K] as loaded
-  auto prefetch = [&](int t, int buf) {
-    const uint32_t dq = d3b::smem_u32(&raw_s[buf][0][lane * E]);
-    const uint32_t dk = d3b::smem_u32(&raw_s[buf][1][lane * E]);
-    const In* sq = qp + (long long)t * p.qs[1];
-    const In* sk = kp + (long long)t * p.ks[1];
-    asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(dq), "l"(sq), "n"(E * 2) : "memory");
-    asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(dk), "l"(sk), "n"(E * 2) : "memory");
+  // q, k and v of the next D - 1 tokens travel to shared memory by cp.async, so
+  // nothing is held in registers while they are in flight; each lane copies its
+  // own E elements of q and k, lanes 0-7 two values of v each. Every prefetch
+  // commits one group, empty past the last token, so "token t's copies are done"
+  // is always "at most D - 2 newer groups pending".
+  constexpr int D = 4;
+  __shared__ __align__(16) In raw_s[D][2][K];  // [slot][q, k][K] as loaded
+  __shared__ __align__(16) In raw_v[D][16];    // [slot][this warp's 16 columns]
+  const In* vrow = static_cast<const In*>(p.v) + b * p.vs[0] + hv * p.vs[2] + vb * 16 + 2 * lane;
+  auto prefetch = [&](int t) {
+    if (t < p.T) {
+      const int slot = t % D;
+      const uint32_t dq = d3b::smem_u32(&raw_s[slot][0][lane * E]);
+      const uint32_t dk = d3b::smem_u32(&raw_s[slot][1][lane * E]);
+      const In* sq = qp + (long long)t * p.qs[1];
+      const In* sk = kp + (long long)t * p.ks[1];
+      asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(dq), "l"(sq), "n"(E * 2) : "memory");
+      asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(dk), "l"(sk), "n"(E * 2) : "memory");
+      if (lane < 8) {
+        const uint32_t dv = d3b::smem_u32(&raw_v[slot][2 * lane]);
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dv), "l"(vrow + (long long)t * p.vs[1])
+                     : "memory");
+      }
+    }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  // wait for this lane's copies of one token, normalise, publish to qk_s[buf]; returns k.q
-  auto stage = [&](int buf) -> float {
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
+  // wait for token t's copies, normalise q and k, publish them to qk_s[t & 1]; returns k.q
+  auto stage = [&](int t) -> float {
+    asm volatile("cp.async.wait_group %0;" ::"n"(D - 2) : "memory");
+    const int slot = t % D, buf = t & 1;
     float qr[E], kr[E];
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-      qr[e] = to_f32(raw_s[buf][0][lane * E + e]);
-      kr[e] = to_f32(raw_s[buf][1][lane * E + e]);
+      qr[e] = to_f32(raw_s[slot][0][lane * E + e]);
+      kr[e] = to_f32(raw_s[slot][1][lane * E + e]);
     }
-    float sq = 0.f, sk = 0.f;
+    float sq = 0.f, sk = 0.f, sqk = 0.f;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
       sq = fmaf(qr[e], qr[e], sq);
       sk = fmaf(kr[e], kr[e], sk);
+      sqk = fmaf(qr[e], kr[e], sqk);
     }
-    sq = warp_sum(sq);
-    sk = warp_sum(sk);
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) {  // three independent butterflies
+      sq += __shfl_xor_sync(FULL, sq, m);
+      sk += __shfl_xor_sync(FULL, sk, m);
+      sqk += __shfl_xor_sync(FULL, sqk, m);
+    }
     const float ik = p.l2norm ? 1.f / sqrtf(sk + 1e-6f) : 1.f;
     const float iq = (p.l2norm ? 1.f / sqrtf(sq + 1e-6f) : 1.f) * p.scale;
-    float kq = 0.f;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-      const float qn = qr[e] * iq, kn = kr[e] * ik;
-      qk_s[buf][0][lane * E + e] = qn;
-      qk_s[buf][1][lane * E + e] = kn;
-      kq = fmaf(kn, qn, kq);
+      qk_s[buf][0][lane * E + e] = qr[e] * iq;
+      qk_s[buf][1][lane * E + e] = kr[e] * ik;
     }
-    return warp_sum(kq);
+    return sqk * iq * ik;
+  };
+  // Sum 8 per-column partials over the 16 lanes of a half-warp (row blocks); lane
+  // ends with the total of column jj (lanes hl and hl ^ 1 hold the same one).
+  auto reduce_scatter = [&](const float (&a)[8]) -> float {
+    float b4[4], b2[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float send = bit3 ? a[i] : a[4 + i];
+      b4[i] = (bit3 ? a[4 + i] : a[i]) + __shfl_xor_sync(FULL, send, 8);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float send = bit2 ? b4[i] : b4[2 + i];
+      b2[i] = (bit2 ? b4[2 + i] : b4[i]) + __shfl_xor_sync(FULL, send, 4);
+    }
+    const float send = bit1 ? b2[0] : b2[1];
+    float d = (bit1 ? b2[1] : b2[0]) + __shfl_xor_sync(FULL, send, 2);
+    return d + __shfl_xor_sync(FULL, d, 1);
+  };
+  // The inverse: every lane gets the 8 values of its columns from the owners.
+  auto all_gather = [&](float u, float (&g8)[8]) {
+    const float o1 = __shfl_xor_sync(FULL, u, 2);
+    const float e0 = bit1 ? o1 : u, e1 = bit1 ? u : o1;
+    const float o2a = __shfl_xor_sync(FULL, e0, 4), o2b = __shfl_xor_sync(FULL, e1, 4);
+    const float f0 = bit2 ? o2a : e0, f1 = bit2 ? o2b : e1, f2 = bit2 ? e0 : o2a, f3 = bit2 ? e1 : o2b;
+    const float r0 = __shfl_xor_sync(FULL, f0, 8), r1 = __shfl_xor_sync(FULL, f1, 8);
+    const float r2 = __shfl_xor_sync(FULL, f2, 8), r3 = __shfl_xor_sync(FULL, f3, 8);
+    g8[0] = bit3 ? r0 : f0;
+    g8[1] = bit3 ? r1 : f1;
+    g8[2] = bit3 ? r2 : f2;
+    g8[3] = bit3 ? r3 : f3;
+    g8[4] = bit3 ? f0 : r0;
+    g8[5] = bit3 ? f1 : r1;
+    g8[6] = bit3 ? f2 : r2;
+    g8[7] = bit3 ? f3 : r3;
+  };
+  // g and beta of 32 tokens at a time: lane l holds token 32 * group + l, one group ahead
+  float g_cur = 0.f, b_cur = 0.f, g_nxt = 0.f, b_nxt = 0.f;
+  auto load_scalars = [&](int t0, float& gg, float& bb) {
+    const int t = t0 + lane;
+    if (t < p.T) {
+      gg = gp[(long long)t * p.gs[1]];
+      bb = to_f32(bp[(long long)t * p.bs[1]]);
+    }
   };
 
-  float kq = 0.f, v_t = 0.f, g_t = 0.f, beta_t = 0.f, vv = 0.f, gv = 0.f, bv = 0.f;
-  if (p.T > 0) {
-    prefetch(0, 0);
-    kq = stage(0);
-    v_t = to_f32(vp[0]);
-    g_t = gp[0];
-    beta_t = to_f32(bp[0]);
-    if (p.T > 1) prefetch(1, 1);
-  }
+#pragma unroll
+  for (int i = 0; i < D - 1; ++i) prefetch(i);
+  load_scalars(0, g_cur, b_cur);
+  load_scalars(32, g_nxt, b_nxt);
+  float kq = 0.f;
+  if (p.T > 0) kq = stage(0);
+  __syncwarp();
+  prefetch(D - 1);
   __syncwarp();
   for (int t = 0; t < p.T; ++t) {
     const int buf = t & 1;
-    if (t + 1 < p.T) {  // the next token's scalars, in flight during this token's math
-      vv = to_f32(vp[(long long)(t + 1) * p.vs[1]]);
-      gv = gp[(long long)(t + 1) * p.gs[1]];
-      bv = to_f32(bp[(long long)(t + 1) * p.bs[1]]);
+    if (t > 0 && (t & 31) == 0) {
+      g_cur = g_nxt;
+      b_cur = b_nxt;
+      load_scalars(t + 32, g_nxt, b_nxt);
     }
+    const float g_t = __shfl_sync(FULL, g_cur, t & 31);
+    const float beta_t = __shfl_sync(FULL, b_cur, t & 31);
+    const float v_t = to_f32(raw_v[t % D][cb * 8 + jj]);
     c *= expf(g_t);
     if (c < 1e-20f || c > 1e20f) {  // warp-uniform: every lane holds the same c
 #pragma unroll
-      for (int r = 0; r < K; ++r) S[r] *= c;
+      for (int i = 0; i < RL; ++i)
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) S[i][c8] *= c;
       c = 1.f;
     }
-    const float4* q4 = reinterpret_cast<const float4*>(qk_s[buf][0]);
-    const float4* k4 = reinterpret_cast<const float4*>(qk_s[buf][1]);
-    float ak[4] = {0.f, 0.f, 0.f, 0.f}, aq[4] = {0.f, 0.f, 0.f, 0.f};
+    float kr[RL], qr[RL];
 #pragma unroll
-    for (int r4 = 0; r4 < K / 4; ++r4) {
-      if (r4 % 4 == 0) __syncwarp();  // bounds how far the compiler hoists the shared loads
-      const float4 kk = k4[r4], qq = q4[r4];
-      ak[0] = fmaf(kk.x, S[4 * r4 + 0], ak[0]);
-      ak[1] = fmaf(kk.y, S[4 * r4 + 1], ak[1]);
-      ak[2] = fmaf(kk.z, S[4 * r4 + 2], ak[2]);
-      ak[3] = fmaf(kk.w, S[4 * r4 + 3], ak[3]);
-      aq[0] = fmaf(qq.x, S[4 * r4 + 0], aq[0]);
-      aq[1] = fmaf(qq.y, S[4 * r4 + 1], aq[1]);
-      aq[2] = fmaf(qq.z, S[4 * r4 + 2], aq[2]);
-      aq[3] = fmaf(qq.w, S[4 * r4 + 3], aq[3]);
+    for (int i4 = 0; i4 < RL / 4; ++i4) {
+      const float4 kk = reinterpret_cast<const float4*>(qk_s[buf][1] + row0)[i4];
+      const float4 qq = reinterpret_cast<const float4*>(qk_s[buf][0] + row0)[i4];
+      kr[4 * i4 + 0] = kk.x; kr[4 * i4 + 1] = kk.y; kr[4 * i4 + 2] = kk.z; kr[4 * i4 + 3] = kk.w;
+      qr[4 * i4 + 0] = qq.x; qr[4 * i4 + 1] = qq.y; qr[4 * i4 + 2] = qq.z; qr[4 * i4 + 3] = qq.w;
     }
-    const float kh = ((ak[0] + ak[1]) + (ak[2] + ak[3])) * c;
-    const float qh = ((aq[0] + aq[1]) + (aq[2] + aq[3])) * c;
+    float ak[8], aq[8];
+#pragma unroll
+    for (int c8 = 0; c8 < 8; ++c8) ak[c8] = aq[c8] = 0.f;
+#pragma unroll
+    for (int i = 0; i < RL; ++i)
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        fma2(ak[2 * m], ak[2 * m + 1], kr[i], kr[i], S[i][2 * m], S[i][2 * m + 1]);
+        fma2(aq[2 * m], aq[2 * m + 1], qr[i], qr[i], S[i][2 * m], S[i][2 * m + 1]);
+      }
+    const float kh = reduce_scatter(ak) * c;
+    const float qh = reduce_scatter(aq) * c;
     const float vnew = beta_t * (v_t - kh);
-    op[(long long)t * p.os[1]] = from_f32<In>(fmaf(kq, vnew, qh));
-    const float upd = vnew / c;
+    if ((hl & 1) == 0) op[(long long)t * p.os[1]] = from_f32<In>(fmaf(kq, vnew, qh));
+    float upd[8];
+    all_gather(vnew / c, upd);
 #pragma unroll
-    for (int r4 = 0; r4 < K / 4; ++r4) {
-      if (r4 % 4 == 0) __syncwarp();
-      const float4 kk = k4[r4];
-      S[4 * r4 + 0] = fmaf(kk.x, upd, S[4 * r4 + 0]);
-      S[4 * r4 + 1] = fmaf(kk.y, upd, S[4 * r4 + 1]);
-      S[4 * r4 + 2] = fmaf(kk.z, upd, S[4 * r4 + 2]);
-      S[4 * r4 + 3] = fmaf(kk.w, upd, S[4 * r4 + 3]);
-    }
+    for (int i = 0; i < RL; ++i)
+#pragma unroll
+      for (int m = 0; m < 4; ++m) fma2(S[i][2 * m], S[i][2 * m + 1], kr[i], kr[i], upd[2 * m], upd[2 * m + 1]);
     if (t + 1 < p.T) {
-      kq = stage(buf ^ 1);  // token t+1, copied while token t was computed
-      if (t + 2 < p.T) prefetch(t + 2, buf);  // this lane read token t's raw copy one token ago
-      v_t = vv;
-      g_t = gv;
-      beta_t = bv;
-      __syncwarp();
+      kq = stage(t + 1);  // copied while earlier tokens were computed
+      __syncwarp();       // every lane has read token t's v: its slot may be refilled
+      prefetch(t + D);
+      __syncwarp();       // token t+1's normalised q, k visible to all lanes
     }
   }
   if (p.ht) {
-    float* dst = p.ht + (long long)bh * K * p.V + j;
+    float* dst = p.ht + ((long long)bh * K + row0) * p.V + col0;
 #pragma unroll
-    for (int r = 0; r < K; ++r) dst[(long long)r * p.V] = S[r] * c;
+    for (int i = 0; i < RL; ++i)
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) dst[(long long)i * p.V + c8] = S[i][c8] * c;
   }
 }
 
@@ -230,7 +308,7 @@ extern "C" int d3b_gated_delta_rule(const void* q, const int64_t* q_strides, con
   if (K != 64 && K != 128) return D3B_EUNSUPPORTED;
   if (dtype != D3B_BF16 && dtype != D3B_F16) return D3B_EUNSUPPORTED;
   if (beta_dtype != D3B_F32 && beta_dtype != D3B_BF16 && beta_dtype != D3B_F16) return D3B_EUNSUPPORTED;
-  const long long blocks = (long long)B * HV * (V / 32);
+  const long long blocks = (long long)B * HV * (V / 16);  // one warp per 16 state columns
   if (blocks == 0) return D3B_OK;
   if (blocks >= (1ll << 31)) return D3B_EINVAL;
   if (T > 0 && (!q || !k || !v || !g || !beta || !o)) return D3B_EINVAL;
@@ -240,7 +318,8 @@ extern "C" int d3b_gated_delta_rule(const void* q, const int64_t* q_strides, con
       (h0 && !aligned(h0, 4)) || (ht && !aligned(ht, 4)))
     return D3B_EALIGN;
   for (int i = 0; i < 3; ++i)
-    if (q_strides[i] % E != 0 || k_strides[i] % E != 0) return D3B_EALIGN;
+    if (q_strides[i] % E != 0 || k_strides[i] % E != 0 || v_strides[i] % 2 != 0) return D3B_EALIGN;
+  if (!aligned(v, 4)) return D3B_EALIGN;  // v is copied two values (4 bytes) per lane
   GdrParams p;
   p.q = q;
   p.k = k;
