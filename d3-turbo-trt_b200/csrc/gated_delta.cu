@@ -13,7 +13,8 @@
 // tile of the state in registers: half-warp lanes split the rows, the two halves
 // split the columns. The column sums over K (k.S and q.S) finish with a
 // reduce-scatter across the 16 row lanes (8 shuffles: every lane ends with one
-// column's total) and v' goes back with the inverse all-gather (7 shuffles), so
+// column's total; the tile's columns are kept in a lane-dependent XOR order so no
+// level needs a select) and v' goes back with the inverse all-gather (7 shuffles), so
 // each lane reads only its K/16 rows of q and k per token: shared-memory traffic
 // stays far below the shuffle and FMA work. No barriers. The token's normalised
 // q and k are staged once per warp in shared memory (double-buffered);
@@ -74,8 +75,7 @@ __global__ void __launch_bounds__(32) gdr_recurrent_kernel(const __grid_constant
   static_assert(RL == 4 || RL == 8, "K is 64 or 128");
   const int lane = threadIdx.x;
   const int hl = lane & 15, cb = lane >> 4;  // row block, column half
-  const int bit3 = (hl >> 3) & 1, bit2 = (hl >> 2) & 1, bit1 = (hl >> 1) & 1;
-  const int jj = bit3 * 4 + bit2 * 2 + bit1;  // the column this lane owns after a reduce-scatter
+  const int jj = (hl >> 1) & 7;  // the column this lane owns after a reduce-scatter
   const int n_vb = p.V >> 4;                  // 16 columns per warp
   const long long blk = blockIdx.x;
   const int vb = (int)(blk % n_vb);
@@ -86,13 +86,15 @@ __global__ void __launch_bounds__(32) gdr_recurrent_kernel(const __grid_constant
 
   __shared__ __align__(16) float qk_s[2][2][K];  // [buffer][q, k][K], normalised
 
+  // S[i][p] holds state row row0 + i, column col0 + (p ^ jj): with the columns in this
+  // lane-dependent order the reduce-scatter keeps and sends fixed positions (no selects)
   float S[RL][8];
   if (p.h0) {
     const float* src = p.h0 + b * p.h0s[0] + hv * p.h0s[1] + (long long)row0 * p.h0s[2] + col0;
 #pragma unroll
     for (int i = 0; i < RL; ++i)
 #pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) S[i][c8] = src[(long long)i * p.h0s[2] + c8];
+      for (int c8 = 0; c8 < 8; ++c8) S[i][c8] = src[(long long)i * p.h0s[2] + (c8 ^ jj)];
   } else {
 #pragma unroll
     for (int i = 0; i < RL; ++i)
@@ -156,8 +158,8 @@ __global__ void __launch_bounds__(32) gdr_recurrent_kernel(const __grid_constant
       sk += __shfl_xor_sync(FULL, sk, m);
       sqk += __shfl_xor_sync(FULL, sqk, m);
     }
-    const float ik = p.l2norm ? 1.f / sqrtf(sk + 1e-6f) : 1.f;
-    const float iq = (p.l2norm ? 1.f / sqrtf(sq + 1e-6f) : 1.f) * p.scale;
+    const float ik = p.l2norm ? rsqrtf(sk + 1e-6f) : 1.f;
+    const float iq = (p.l2norm ? rsqrtf(sq + 1e-6f) : 1.f) * p.scale;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
       qk_s[buf][0][lane * E + e] = qr[e] * iq;
@@ -165,40 +167,28 @@ __global__ void __launch_bounds__(32) gdr_recurrent_kernel(const __grid_constant
     }
     return sqk * iq * ik;
   };
-  // Sum 8 per-column partials over the 16 lanes of a half-warp (row blocks); lane
-  // ends with the total of column jj (lanes hl and hl ^ 1 hold the same one).
+  // Sum 8 per-column partials (positions p, columns p ^ jj) over the 16 lanes of a
+  // half-warp; the partner at lane distance 8 (4, 2) holds my kept columns at
+  // positions p ^ 4 (p ^ 2, p ^ 1), so each level sends the upper positions and
+  // adds into the lower ones. The lane ends with the total of column jj (lanes hl
+  // and hl ^ 1 hold the same one).
   auto reduce_scatter = [&](const float (&a)[8]) -> float {
     float b4[4], b2[2];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float send = bit3 ? a[i] : a[4 + i];
-      b4[i] = (bit3 ? a[4 + i] : a[i]) + __shfl_xor_sync(FULL, send, 8);
-    }
+    for (int i = 0; i < 4; ++i) b4[i] = a[i] + __shfl_xor_sync(FULL, a[4 + i], 8);
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const float send = bit2 ? b4[i] : b4[2 + i];
-      b2[i] = (bit2 ? b4[2 + i] : b4[i]) + __shfl_xor_sync(FULL, send, 4);
-    }
-    const float send = bit1 ? b2[0] : b2[1];
-    float d = (bit1 ? b2[1] : b2[0]) + __shfl_xor_sync(FULL, send, 2);
+    for (int i = 0; i < 2; ++i) b2[i] = b4[i] + __shfl_xor_sync(FULL, b4[2 + i], 4);
+    const float d = b2[0] + __shfl_xor_sync(FULL, b2[1], 2);
     return d + __shfl_xor_sync(FULL, d, 1);
   };
-  // The inverse: every lane gets the 8 values of its columns from the owners.
+  // The inverse: every lane gets the values of its 8 columns, in its own order.
   auto all_gather = [&](float u, float (&g8)[8]) {
-    const float o1 = __shfl_xor_sync(FULL, u, 2);
-    const float e0 = bit1 ? o1 : u, e1 = bit1 ? u : o1;
-    const float o2a = __shfl_xor_sync(FULL, e0, 4), o2b = __shfl_xor_sync(FULL, e1, 4);
-    const float f0 = bit2 ? o2a : e0, f1 = bit2 ? o2b : e1, f2 = bit2 ? e0 : o2a, f3 = bit2 ? e1 : o2b;
-    const float r0 = __shfl_xor_sync(FULL, f0, 8), r1 = __shfl_xor_sync(FULL, f1, 8);
-    const float r2 = __shfl_xor_sync(FULL, f2, 8), r3 = __shfl_xor_sync(FULL, f3, 8);
-    g8[0] = bit3 ? r0 : f0;
-    g8[1] = bit3 ? r1 : f1;
-    g8[2] = bit3 ? r2 : f2;
-    g8[3] = bit3 ? r3 : f3;
-    g8[4] = bit3 ? f0 : r0;
-    g8[5] = bit3 ? f1 : r1;
-    g8[6] = bit3 ? f2 : r2;
-    g8[7] = bit3 ? f3 : r3;
+    g8[0] = u;
+    g8[1] = __shfl_xor_sync(FULL, g8[0], 2);
+    g8[2] = __shfl_xor_sync(FULL, g8[0], 4);
+    g8[3] = __shfl_xor_sync(FULL, g8[1], 4);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) g8[4 + i] = __shfl_xor_sync(FULL, g8[i], 8);
   };
   // g and beta of 32 tokens at a time: lane l holds token 32 * group + l, one group ahead
   float g_cur = 0.f, b_cur = 0.f, g_nxt = 0.f, b_nxt = 0.f;
@@ -229,7 +219,7 @@ __global__ void __launch_bounds__(32) gdr_recurrent_kernel(const __grid_constant
     const float g_t = __shfl_sync(FULL, g_cur, t & 31);
     const float beta_t = __shfl_sync(FULL, b_cur, t & 31);
     const float v_t = to_f32(raw_v[t % D][cb * 8 + jj]);
-    c *= expf(g_t);
+    c *= __expf(g_t);
     if (c < 1e-20f || c > 1e20f) {  // warp-uniform: every lane holds the same c
 #pragma unroll
       for (int i = 0; i < RL; ++i)
@@ -260,7 +250,7 @@ __global__ void __launch_bounds__(32) gdr_recurrent_kernel(const __grid_constant
     const float vnew = beta_t * (v_t - kh);
     if ((hl & 1) == 0) op[(long long)t * p.os[1]] = from_f32<In>(fmaf(kq, vnew, qh));
     float upd[8];
-    all_gather(vnew / c, upd);
+    all_gather(vnew * __frcp_rn(c), upd);
 #pragma unroll
     for (int i = 0; i < RL; ++i)
 #pragma unroll
@@ -277,7 +267,7 @@ __global__ void __launch_bounds__(32) gdr_recurrent_kernel(const __grid_constant
 #pragma unroll
     for (int i = 0; i < RL; ++i)
 #pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) dst[(long long)i * p.V + c8] = S[i][c8] * c;
+      for (int c8 = 0; c8 < 8; ++c8) dst[(long long)i * p.V + (c8 ^ jj)] = S[i][c8] * c;
   }
 }
 
