@@ -282,6 +282,376 @@ int launch_k(const GdrParams& p, int beta_dtype, long long blocks, cudaStream_t 
   return d3b_host::check_launch();
 }
 
+// ---------------------------------------------------------------------------
+// Chunked form for blocks of at most 64 tokens (the question pass), K = V = 128,
+// one initial state shared by all rows, no final state. With gamma the running
+// sum of g inside the block (WY form of the same recurrence):
+//   A  = strictly-lower( beta_i (k_i . k_j) e^(gamma_i - gamma_j) )
+//   R  = beta_i (v_i - e^gamma_i S0^T k_i)        (rows i)
+//   V' = (I + A)^-1 R                             (forward substitution)
+//   O  = e^gamma_i S0^T q_i + lower-incl( (q_i . k_j) e^(gamma_i - gamma_j) ) V'
+// One CTA = two blocks (M = 128 rows) and one value head; 128 threads. The four
+// products K K^T, K S0, Q K^T, Q S0 run on tcgen05 into TMEM (bf16 operands,
+// fp32 accumulate: 512 columns), the epilogue (thread = row) forms A, R and the
+// decayed P = lower(Q K^T) as bf16, the solve runs with thread = state column in
+// fp32 registers, then P V' runs on tcgen05 into the freed columns 0..127.
+// ---------------------------------------------------------------------------
+namespace gdc {
+
+constexpr int KD = 128;             // K = V = 128
+constexpr int M = 128;              // two blocks of up to 64 tokens
+constexpr int THREADS = 128;
+constexpr int CHUNK = M * 128;      // one [128 rows x 64 bf16] 128B-swizzled chunk
+constexpr int TILE = 2 * CHUNK;     // a [128 x 128] bf16 operand tile
+constexpr int OFF_KN = 0, OFF_QN = TILE, OFF_S0 = 2 * TILE, OFF_P = 3 * TILE, OFF_V = 4 * TILE;
+constexpr int R_STRIDE = 132;       // fp32 row stride of R (conflict-free row writes)
+constexpr int A_STRIDE = 68;        // fp32 row stride of A
+constexpr int OFF_R = 0;            // aliases the K/Q/S0 tiles once their products are done
+constexpr int OFF_A = 5 * TILE;
+constexpr int SMEM_BYTES = OFF_A + M * A_STRIDE * 4 + 1024;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr int COL_KK = 0, COL_KS = 128, COL_QK = 256, COL_QS = 384, COL_PV = 0;
+
+enum : int { kSiteChunkMma1 = 3001, kSiteChunkMma2 = 3002, kSiteChunkDrain = 3003 };
+
+// Byte offset of element (r, c) of a [128 x 128] bf16 tile held as two [128 x 64]
+// chunks in the 128B-swizzle layout (16-byte granule index XOR row % 8); for a
+// K-major operand r is the M/N row and c the K index, for an MN-major one r is the
+// K index and c the N column.
+__device__ __forceinline__ uint32_t sw_off(int r, int c) {
+  return (uint32_t)((c >> 6) * CHUNK + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) + (c & 7) * 2);
+}
+
+struct Bars {
+  uint64_t mma1, mma2, drain;
+  uint32_t tmem_slot;
+  int abort_flag;
+  float gam[M];   // running sum of g within each block
+  float beta[M];
+};
+
+template <typename In>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <typename In>
+__device__ __forceinline__ void unpack8(const uint4& u, float* f) {
+  const In* h = reinterpret_cast<const In*>(&u);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) f[e] = to_f32(h[e]);
+}
+
+template <typename In, typename BetaT>
+__global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_constant__ GdrParams p, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ Bars bars;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int hv = blockIdx.y, h = hv / (p.HV / p.H);
+  const int blk = tid >> 6, tl = tid & 63;  // this thread's row: token tl of block blk
+  const int b = blockIdx.x * 2 + blk;
+  const bool valid = b < p.B && tl < p.T;
+  volatile int* abort_flag = &bars.abort_flag;
+
+  if (tid == 0) {
+    d3b::mbar_init(&bars.mma1, 1);
+    d3b::mbar_init(&bars.mma2, 1);
+    d3b::mbar_init(&bars.drain, 1);
+    bars.abort_flag = 0;
+    d3b::fence_barrier_init();
+  }
+  // ---- phase 1: g -> gamma, beta; normalised q, k rows; S0 in bf16 ----------
+  bars.gam[tid] = valid ? p.g[b * p.gs[0] + (long long)tl * p.gs[1] + hv * p.gs[2]] : 0.f;
+  bars.beta[tid] = valid ? to_f32(static_cast<const BetaT*>(p.beta)[b * p.bs[0] + (long long)tl * p.bs[1] +
+                                                                     hv * p.bs[2]])
+                         : 0.f;
+  __syncthreads();
+  float gam = 0.f;
+  for (int s = blk * 64; s <= tid; ++s) gam += bars.gam[s];
+  __syncthreads();
+  bars.gam[tid] = gam;
+
+  {
+    const In* qrow = static_cast<const In*>(p.q) + b * p.qs[0] + (long long)tl * p.qs[1] + h * p.qs[2];
+    const In* krow = static_cast<const In*>(p.k) + b * p.ks[0] + (long long)tl * p.ks[1] + h * p.ks[2];
+    float sq = 0.f, sk = 0.f;
+    if (valid) {
+#pragma unroll 4
+      for (int c8 = 0; c8 < KD / 8; ++c8) {
+        float fq[8], fk[8];
+        unpack8<In>(reinterpret_cast<const uint4*>(qrow)[c8], fq);
+        unpack8<In>(reinterpret_cast<const uint4*>(krow)[c8], fk);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          sq = fmaf(fq[e], fq[e], sq);
+          sk = fmaf(fk[e], fk[e], sk);
+        }
+      }
+    }
+    const float iq = (p.l2norm ? 1.f / sqrtf(sq + 1e-6f) : 1.f) * p.scale;
+    const float ik = p.l2norm ? 1.f / sqrtf(sk + 1e-6f) : 1.f;
+#pragma unroll 4
+    for (int c8 = 0; c8 < KD / 8; ++c8) {
+      uint4 oq = make_uint4(0, 0, 0, 0), ok = make_uint4(0, 0, 0, 0);
+      if (valid) {
+        float fq[8], fk[8];
+        unpack8<In>(reinterpret_cast<const uint4*>(qrow)[c8], fq);
+        unpack8<In>(reinterpret_cast<const uint4*>(krow)[c8], fk);
+        oq = make_uint4(pack2<__nv_bfloat16>(fq[0] * iq, fq[1] * iq), pack2<__nv_bfloat16>(fq[2] * iq, fq[3] * iq),
+                        pack2<__nv_bfloat16>(fq[4] * iq, fq[5] * iq), pack2<__nv_bfloat16>(fq[6] * iq, fq[7] * iq));
+        ok = make_uint4(pack2<__nv_bfloat16>(fk[0] * ik, fk[1] * ik), pack2<__nv_bfloat16>(fk[2] * ik, fk[3] * ik),
+                        pack2<__nv_bfloat16>(fk[4] * ik, fk[5] * ik), pack2<__nv_bfloat16>(fk[6] * ik, fk[7] * ik));
+      }
+      *reinterpret_cast<uint4*>(smem + OFF_QN + sw_off(tid, c8 * 8)) = oq;
+      *reinterpret_cast<uint4*>(smem + OFF_KN + sw_off(tid, c8 * 8)) = ok;
+    }
+    // S0 row tid (the K index) as the MN-major B operand, bf16
+    const float* srow = p.h0 ? p.h0 + hv * p.h0s[1] + (long long)tid * p.h0s[2] : nullptr;
+#pragma unroll 4
+    for (int c8 = 0; c8 < KD / 8; ++c8) {
+      uint4 os = make_uint4(0, 0, 0, 0);
+      if (srow) {
+        const float4 a = reinterpret_cast<const float4*>(srow)[2 * c8];
+        const float4 z = reinterpret_cast<const float4*>(srow)[2 * c8 + 1];
+        os = make_uint4(pack2<__nv_bfloat16>(a.x, a.y), pack2<__nv_bfloat16>(a.z, a.w),
+                        pack2<__nv_bfloat16>(z.x, z.y), pack2<__nv_bfloat16>(z.z, z.w));
+      }
+      *reinterpret_cast<uint4*>(smem + OFF_S0 + sw_off(tid, c8 * 8)) = os;
+    }
+  }
+  d3b::fence_proxy_async_smem();
+  if (warp == 0) d3b::tmem_alloc(&bars.tmem_slot, TMEM_COLS);
+  d3b::tc_fence_before();
+  __syncthreads();
+  d3b::tc_fence_after();
+  const uint32_t tmem = bars.tmem_slot;
+  const uint32_t s_base = d3b::smem_u32(smem);
+
+  // ---- phase 2: K K^T, K S0, Q K^T, Q S0 -------------------------------------
+  if (tid == 0) {
+    constexpr uint32_t id_kk = d3b::make_idesc(1, 1, 1, 0, 0, M, KD);  // both K-major
+    constexpr uint32_t id_ks = d3b::make_idesc(1, 1, 1, 0, 1, M, KD);  // B (S0) MN-major
+#pragma unroll
+    for (int k = 0; k < KD / 16; ++k) {
+      const uint32_t koff = (uint32_t)((k >> 2) * CHUNK + (k & 3) * 32);
+      const uint64_t a_k = d3b::make_smem_desc(s_base + OFF_KN + koff, 16, 1024, d3b::kLayoutSW128);
+      const uint64_t a_q = d3b::make_smem_desc(s_base + OFF_QN + koff, 16, 1024, d3b::kLayoutSW128);
+      const uint64_t b_s = d3b::make_smem_desc(s_base + OFF_S0 + k * 16 * 128, CHUNK, 1024, d3b::kLayoutSW128);
+      d3b::mma_f16_ss(tmem + COL_KK, a_k, a_k, id_kk, k > 0);
+      d3b::mma_f16_ss(tmem + COL_KS, a_k, b_s, id_ks, k > 0);
+      d3b::mma_f16_ss(tmem + COL_QK, a_q, a_k, id_kk, k > 0);
+      d3b::mma_f16_ss(tmem + COL_QS, a_q, b_s, id_ks, k > 0);
+    }
+    d3b::mma_commit(&bars.mma1);
+  }
+  bool ok = d3b::warp_wait(&bars.mma1, 0, abort_flag, err, kSiteChunkMma1);
+  d3b::tc_fence_after();
+
+  // ---- phase 3 (thread = row): A, R, P --------------------------------------
+  float* Rm = reinterpret_cast<float*>(smem + OFF_R);
+  float* Am = reinterpret_cast<float*>(smem + OFF_A);
+  const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+  if (ok) {
+    const float beta_i = bars.beta[tid];
+    uint32_t r[32];
+    // A: own block's 64 columns of K K^T
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+      const int j0 = blk * 64 + half * 32;
+      d3b::tmem_ld32(lane_addr + COL_KK + j0, r);
+      d3b::tmem_wait_ld();
+#pragma unroll
+      for (int x = 0; x < 32; x += 4) {
+        float4 av;
+        float* a = reinterpret_cast<float*>(&av);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int jl = half * 32 + x + e;
+          a[e] = jl < tl ? beta_i * __uint_as_float(r[x + e]) * __expf(gam - bars.gam[blk * 64 + jl]) : 0.f;
+        }
+        *reinterpret_cast<float4*>(Am + tid * A_STRIDE + half * 32 + x) = av;
+      }
+    }
+    // P: the decayed lower triangle (diagonal included) of Q K^T, both blocks' columns (zero off-block)
+#pragma unroll 1
+    for (int q4 = 0; q4 < 4; ++q4) {
+      d3b::tmem_ld32(lane_addr + COL_QK + q4 * 32, r);
+      d3b::tmem_wait_ld();
+#pragma unroll
+      for (int x = 0; x < 32; x += 8) {
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int j = q4 * 32 + x + e;
+          const bool keep = (j >> 6) == blk && (j & 63) <= tl;
+          f[e] = keep ? __uint_as_float(r[x + e]) * __expf(gam - bars.gam[j]) : 0.f;
+        }
+        *reinterpret_cast<uint4*>(smem + OFF_P + sw_off(tid, q4 * 32 + x)) =
+            make_uint4(pack2<__nv_bfloat16>(f[0], f[1]), pack2<__nv_bfloat16>(f[2], f[3]),
+                       pack2<__nv_bfloat16>(f[4], f[5]), pack2<__nv_bfloat16>(f[6], f[7]));
+      }
+    }
+  }
+  // the K/Q/S0 tiles are free (their products completed): R overwrites them
+  __syncthreads();
+  if (ok) {
+    const float beta_i = bars.beta[tid];
+    const float eg = __expf(gam);
+    const In* vrow = static_cast<const In*>(p.v) + b * p.vs[0] + (long long)tl * p.vs[1] + hv * p.vs[2];
+    uint32_t r[32];
+#pragma unroll 1
+    for (int q4 = 0; q4 < 4; ++q4) {
+      d3b::tmem_ld32(lane_addr + COL_KS + q4 * 32, r);
+      d3b::tmem_wait_ld();
+#pragma unroll
+      for (int x = 0; x < 32; x += 8) {
+        float fv[8];
+        if (valid) {
+          unpack8<In>(reinterpret_cast<const uint4*>(vrow)[(q4 * 32 + x) / 8], fv);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) fv[e] = 0.f;
+        }
+        float4 r0, r1;
+        r0.x = beta_i * (fv[0] - eg * __uint_as_float(r[x + 0]));
+        r0.y = beta_i * (fv[1] - eg * __uint_as_float(r[x + 1]));
+        r0.z = beta_i * (fv[2] - eg * __uint_as_float(r[x + 2]));
+        r0.w = beta_i * (fv[3] - eg * __uint_as_float(r[x + 3]));
+        r1.x = beta_i * (fv[4] - eg * __uint_as_float(r[x + 4]));
+        r1.y = beta_i * (fv[5] - eg * __uint_as_float(r[x + 5]));
+        r1.z = beta_i * (fv[6] - eg * __uint_as_float(r[x + 6]));
+        r1.w = beta_i * (fv[7] - eg * __uint_as_float(r[x + 7]));
+        *reinterpret_cast<float4*>(Rm + tid * R_STRIDE + q4 * 32 + x) = r0;
+        *reinterpret_cast<float4*>(Rm + tid * R_STRIDE + q4 * 32 + x + 4) = r1;
+      }
+    }
+  }
+  d3b::tc_fence_before();
+  __syncthreads();
+
+  // ---- phase 4 (thread = state column c): V' = (I + A)^-1 R per block -------
+  if (ok) {
+    const int c = tid;
+#pragma unroll 1
+    for (int bk = 0; bk < 2; ++bk) {
+      float x[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float* arow = Am + (bk * 64 + i) * A_STRIDE;
+        float acc0 = Rm[(bk * 64 + i) * R_STRIDE + c], acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+#pragma unroll
+        for (int j = 0; j + 4 <= i; j += 4) {
+          const float4 a4 = *reinterpret_cast<const float4*>(arow + j);
+          acc0 = fmaf(-a4.x, x[j], acc0);
+          acc1 = fmaf(-a4.y, x[j + 1], acc1);
+          acc2 = fmaf(-a4.z, x[j + 2], acc2);
+          acc3 = fmaf(-a4.w, x[j + 3], acc3);
+        }
+#pragma unroll
+        for (int j = i & ~3; j < i; ++j) acc0 = fmaf(-arow[j], x[j], acc0);
+        x[i] = (acc0 + acc1) + (acc2 + acc3);
+      }
+#pragma unroll
+      for (int i = 0; i < 64; ++i)
+        *reinterpret_cast<__nv_bfloat16*>(smem + OFF_V + sw_off(bk * 64 + i, c)) = __float2bfloat16_rn(x[i]);
+    }
+  }
+  d3b::fence_proxy_async_smem();
+  d3b::tc_fence_before();
+  __syncthreads();
+  d3b::tc_fence_after();
+
+  // ---- phase 5: P V' into columns 0..127 --------------------------------------
+  if (tid == 0 && ok) {
+    constexpr uint32_t id_pv = d3b::make_idesc(1, 1, 1, 0, 1, M, KD);
+#pragma unroll
+    for (int k = 0; k < M / 16; ++k) {
+      const uint32_t koff = (uint32_t)((k >> 2) * CHUNK + (k & 3) * 32);
+      const uint64_t a_p = d3b::make_smem_desc(s_base + OFF_P + koff, 16, 1024, d3b::kLayoutSW128);
+      const uint64_t b_v = d3b::make_smem_desc(s_base + OFF_V + k * 16 * 128, CHUNK, 1024, d3b::kLayoutSW128);
+      d3b::mma_f16_ss(tmem + COL_PV, a_p, b_v, id_pv, k > 0);
+    }
+    d3b::mma_commit(&bars.mma2);
+  }
+  if (ok) ok = d3b::warp_wait(&bars.mma2, 0, abort_flag, err, kSiteChunkMma2);
+  d3b::tc_fence_after();
+
+  // ---- phase 6 (thread = row): O = e^gamma (Q S0) + P V' ----------------------
+  if (ok) {  // warp-uniform: every lane loads (tcgen05.ld is warp-collective), valid rows store
+    const float eg = __expf(gam);
+    In* orow = static_cast<In*>(p.o) + b * p.os[0] + (long long)tl * p.os[1] + hv * p.os[2];
+    uint32_t rs[32], rp[32];
+#pragma unroll 1
+    for (int q4 = 0; q4 < 4; ++q4) {
+      d3b::tmem_ld32(lane_addr + COL_QS + q4 * 32, rs);
+      d3b::tmem_ld32(lane_addr + COL_PV + q4 * 32, rp);
+      d3b::tmem_wait_ld();
+      if (valid) {
+#pragma unroll
+        for (int x = 0; x < 32; x += 8) {
+          float f[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] = fmaf(eg, __uint_as_float(rs[x + e]), __uint_as_float(rp[x + e]));
+          reinterpret_cast<uint4*>(orow)[(q4 * 32 + x) / 8] = make_uint4(pack2<In>(f[0], f[1]), pack2<In>(f[2], f[3]),
+                                                                         pack2<In>(f[4], f[5]), pack2<In>(f[6], f[7]));
+        }
+      }
+    }
+  }
+
+  // ---- teardown: every issued MMA has completed before TMEM is freed ---------
+  if (tid == 0) {
+    d3b::mma_commit(&bars.drain);
+    const uint32_t addr = d3b::smem_u32(&bars.drain);
+    const uint64_t t0 = d3b::globaltimer_ns();
+    while (!d3b::mbar_try_wait(addr, 0)) {
+      if (d3b::globaltimer_ns() - t0 > D3B_WAIT_LIMIT_NS) {
+        d3b::record_device_error(err, kSiteChunkDrain);
+        break;
+      }
+    }
+  }
+  d3b::tc_fence_before();
+  __syncthreads();
+  d3b::tc_fence_after();
+  if (warp == 0) d3b::tmem_dealloc(tmem, TMEM_COLS);
+}
+
+}  // namespace gdc
+
+template <typename In>
+int launch_chunk(const GdrParams& p, int beta_dtype, cudaStream_t s) {
+  static int attr_set[64][3] = {{0}};
+  const int dev = d3b_host::current_device();
+  int* err = d3b_host::device_error_word();
+  if (!err) return D3B_ECUDA;
+  const dim3 grid((unsigned)((p.B + 1) / 2), (unsigned)p.HV);
+  auto go = [&](auto kernel, int which) -> int {
+    if (dev >= 0 && dev < 64 && !attr_set[dev][which]) {
+      if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gdc::SMEM_BYTES) != cudaSuccess)
+        return D3B_ECUDA;
+      attr_set[dev][which] = 1;
+    }
+    kernel<<<grid, gdc::THREADS, gdc::SMEM_BYTES, s>>>(p, err);
+    return d3b_host::check_launch();
+  };
+  switch (beta_dtype) {
+    case D3B_F32: return go(gdc::gdr_chunk_kernel<In, float>, 0);
+    case D3B_BF16: return go(gdc::gdr_chunk_kernel<In, __nv_bfloat16>, 1);
+    case D3B_F16: return go(gdc::gdr_chunk_kernel<In, __half>, 2);
+    default: return D3B_EUNSUPPORTED;
+  }
+}
+
 bool aligned(const void* ptr, int bytes) { return reinterpret_cast<uintptr_t>(ptr) % bytes == 0; }
 
 }  // namespace
@@ -291,7 +661,8 @@ extern "C" int d3b_gated_delta_rule(const void* q, const int64_t* q_strides, con
                                     const int64_t* g_strides, const void* beta, int beta_dtype,
                                     const int64_t* beta_strides, const float* h0, const int64_t* h0_strides,
                                     void* o, const int64_t* o_strides, float* ht, int B, int T, int H, int HV,
-                                    int K, int V, int dtype, float scale, int l2norm, d3b_stream_t stream) {
+                                    int K, int V, int dtype, float scale, int l2norm, int algo,
+                                    d3b_stream_t stream) {
   if (B < 0 || T < 0 || H <= 0 || HV <= 0 || HV % H != 0 || V <= 0 || V % 32 != 0) return D3B_EINVAL;
   if (!q_strides || !k_strides || !v_strides || !g_strides || !beta_strides || !o_strides) return D3B_EINVAL;
   if (h0 && !h0_strides) return D3B_EINVAL;
@@ -336,6 +707,18 @@ extern "C" int d3b_gated_delta_rule(const void* q, const int64_t* q_strides, con
   p.scale = scale;
   p.l2norm = l2norm ? 1 : 0;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (algo < 0 || algo > 2) return D3B_EINVAL;
+  // the chunked form: blocks of <= 64 tokens, K = V = 128, one state for all rows, no final state,
+  // 16-byte rows (q, k, v, o: strides in multiples of 8 elements; h0: of 4)
+  bool rows16 = aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(o, 16) && (!h0 || aligned(h0, 16));
+  for (int i = 0; i < 3; ++i)
+    rows16 = rows16 && q_strides[i] % 8 == 0 && k_strides[i] % 8 == 0 && v_strides[i] % 8 == 0 &&
+             o_strides[i] % 8 == 0;
+  if (h0) rows16 = rows16 && h0_strides[1] % 4 == 0 && h0_strides[2] % 4 == 0;
+  const bool chunk_ok = K == 128 && V == 128 && T <= 64 && !ht && (!h0 || h0_strides[0] == 0 || B == 1) && rows16;
+  if (algo == 2 && !chunk_ok) return D3B_EUNSUPPORTED;
+  if (algo == 2 || (algo == 0 && chunk_ok && T > 0))
+    return dtype == D3B_BF16 ? launch_chunk<__nv_bfloat16>(p, beta_dtype, s) : launch_chunk<__half>(p, beta_dtype, s);
   if (K == 128)
     return dtype == D3B_BF16 ? launch_k<128, __nv_bfloat16>(p, beta_dtype, blocks, s)
                              : launch_k<128, __half>(p, beta_dtype, blocks, s);

@@ -2,10 +2,11 @@
 ``ops.recurrent_gated_delta_rule`` and ``ops.chunk_gated_delta_rule``
 (d3trt/model/ops.py:287-360), which D3Core calls per GDN layer (core.py:348-372).
 
-Both names run ``d3b_gated_delta_rule`` (``csrc/gated_delta.cu``): the token-recurrent
-form with an fp32 state, which is the math of FLA's fused recurrent kernel (the
-reference's ``recurrent`` path) and, up to rounding, of its chunked kernel. Differences
-from the reference's call, all optional for the caller:
+Both names run ``d3b_gated_delta_rule`` (``csrc/gated_delta.cu``): ``recurrent_...`` the
+token-recurrent form with an fp32 state (the math of FLA's fused recurrent kernel, the
+reference's path for question blocks), ``chunk_...`` the chunked (WY) form on the tensor
+cores for blocks of <= 64 tokens sharing one initial state, falling back to the
+recurrence elsewhere. Differences from the reference's call, all optional for the caller:
 
 * q/k may keep H < HV heads (value head hv reads q/k head hv // (HV // H)), so the
   ``repeat_interleave`` of core.py:345-347 can be dropped;
@@ -28,11 +29,21 @@ def _strides3(t: torch.Tensor, what: str) -> object:
     return _lib.i64_array(t.stride()[:3])
 
 
+ALGOS = {"auto": 0, "recurrent": 1, "chunk": 2}
+
+
 def gated_delta_rule(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, g: torch.Tensor, beta: torch.Tensor,
                      initial_state: torch.Tensor | None = None, output_final_state: bool = False,
                      use_qk_l2norm_in_kernel: bool = True, scale: float | None = None,
-                     out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor | None]:
-    """(o [B,T,HV,V] in v's dtype, final state [B,HV,K,V] fp32 or None)."""
+                     out: torch.Tensor | None = None, algo: str = "auto") -> tuple[torch.Tensor, torch.Tensor | None]:
+    """(o [B,T,HV,V] in v's dtype, final state [B,HV,K,V] fp32 or None).
+
+    ``algo``: "recurrent" (token recurrence, fp32 throughout), "chunk" (the chunked form on
+    the tensor cores: blocks of <= 64 tokens, K = V = 128, one initial state for all rows,
+    no final state) or "auto" (the chunked form where it applies).
+    """
+    if algo not in ALGOS:
+        raise ValueError(f"algo must be one of {sorted(ALGOS)}, got {algo!r}")
     for t, name in ((q, "q"), (k, "k"), (v, "v"), (g, "g"), (beta, "beta")):
         _lib.require_cuda(t, f"gated_delta_rule {name}")
     if q.dim() != 4 or k.shape != q.shape or v.dim() != 4:
@@ -78,19 +89,21 @@ def gated_delta_rule(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, g: to
             _lib.ptr(g), _lib.i64_array(g.stride()), _lib.ptr(beta), _lib.dtype_code(beta.dtype),
             _lib.i64_array(beta.stride()), _lib.ptr(h0), h0s, _lib.ptr(out), _strides3(out, "out"), _lib.ptr(ht),
             B, T, H, HV, K, V, _lib.dtype_code(v.dtype), float(K ** -0.5 if scale is None else scale),
-            1 if use_qk_l2norm_in_kernel else 0, _lib.stream_of(v))
+            1 if use_qk_l2norm_in_kernel else 0, ALGOS[algo], _lib.stream_of(v))
     _lib.check(st, "d3b_gated_delta_rule")
     return out, ht
 
 
 def recurrent_gated_delta_rule(q, k, v, *, g, beta, initial_state, output_final_state,
                                use_qk_l2norm_in_kernel=True):
-    """Drop-in for d3trt/model/ops.py:327-360 (FLA fused_recurrent_gated_delta_rule)."""
+    """Drop-in for d3trt/model/ops.py:327-360 (FLA fused_recurrent_gated_delta_rule): the token recurrence."""
     return gated_delta_rule(q, k, v, g=g, beta=beta, initial_state=initial_state,
-                            output_final_state=output_final_state, use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel)
+                            output_final_state=output_final_state, use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel,
+                            algo="recurrent")
 
 
 def chunk_gated_delta_rule(q, k, v, *, g, beta, initial_state, output_final_state, use_qk_l2norm_in_kernel=True):
-    """Drop-in for d3trt/model/ops.py:287-324 (FLA chunk_gated_delta_rule): the same math, recurrent form."""
+    """Drop-in for d3trt/model/ops.py:287-324 (FLA chunk_gated_delta_rule): the chunked form on the tensor
+    cores where it applies (question blocks), else the token recurrence."""
     return gated_delta_rule(q, k, v, g=g, beta=beta, initial_state=initial_state,
                             output_final_state=output_final_state, use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel)

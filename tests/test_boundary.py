@@ -125,10 +125,10 @@ def test_gated_delta_rejects_bad_arguments():
     p = ctypes.c_void_p(256)
     st = _lib.i64_array([1024, 128, 64])
 
-    def call(B=2, T=3, H=1, HV=2, K=64, V=64, dtype=_lib.BF16, beta_dtype=_lib.BF16, ptr=p, strides=st):
+    def call(B=2, T=3, H=1, HV=2, K=64, V=64, dtype=_lib.BF16, beta_dtype=_lib.BF16, ptr=p, strides=st, algo=0):
         return lib.d3b_gated_delta_rule(ptr, strides, ptr, strides, ptr, strides, ptr, strides, ptr, beta_dtype,
                                         strides, None, None, ptr, strides, None, B, T, H, HV, K, V, dtype, 0.125,
-                                        1, None)
+                                        1, algo, None)
 
     assert call(K=96) == _lib.EUNSUPPORTED
     assert call(V=48) == _lib.EINVAL
@@ -138,6 +138,9 @@ def test_gated_delta_rejects_bad_arguments():
     assert call(strides=None) == _lib.EINVAL
     assert call(ptr=ctypes.c_void_p(257)) == _lib.EALIGN
     assert call(B=0) == _lib.OK  # nothing to do: no launch
+    assert call(algo=3) == _lib.EINVAL
+    assert call(algo=2) == _lib.EUNSUPPORTED  # the chunked form needs K = V = 128
+    assert call(algo=2, K=128, V=128, T=65) == _lib.EUNSUPPORTED  # and blocks of <= 64 tokens
 
 
 def test_wait_selftest_rejects_bad_limit():

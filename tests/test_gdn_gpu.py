@@ -120,3 +120,57 @@ def test_matches_fla_on_the_same_inputs():
                                           output_final_state=False)
     err = (o.float() - ref.float()).abs()
     assert float(err.max()) <= 1e-2, float(err.max())
+
+
+# The chunked form (tcgen05, bf16 products with fp32 accumulation and an fp32 solve) against the
+# same fp64 oracle: bf16 operand rounding bounds it at |err| <= 1e-2 + 2e-2 |ref|.
+def _close_chunk(got, ref):
+    got = got.float().cpu().numpy()
+    assert np.all(np.abs(got - ref) <= 1e-2 + 2e-2 * np.abs(ref)), np.abs(got - ref).max()
+
+
+@pytest.mark.parametrize("B,T", [(5, 48), (2, 64), (3, 1), (1, 17)])
+def test_chunk_form_question_blocks(B, T):
+    H, HV, K, V = 4, 12, 128, 128
+    q, k, v, gl, beta, h0 = _inputs(B, T, H, HV, K, V, 10 + T)
+    o, s = gdn.gated_delta_rule(q.to(DEV), k.to(DEV), v.to(DEV), g=gl.to(DEV), beta=beta.to(DEV),
+                                initial_state=h0.to(DEV).expand(B, -1, -1, -1), algo="chunk")
+    assert s is None
+    ro, _ = oracle_gdr(q.float().numpy(), k.float().numpy(), v.float().numpy(), gl.numpy(), beta.float().numpy(),
+                       h0.numpy())
+    _close_chunk(o, ro)
+    assert _lib.device_error() == 0
+
+
+def test_chunk_form_no_state_fp16_and_auto_dispatch():
+    B, T, H, HV, K, V = 4, 40, 2, 2, 128, 128
+    q, k, v, gl, beta, _ = _inputs(B, T, H, HV, K, V, 21, dtype=torch.float16)
+    args = (q.to(DEV), k.to(DEV), v.to(DEV))
+    o, _ = gdn.gated_delta_rule(*args, g=gl.to(DEV), beta=beta.to(DEV), algo="chunk")
+    ro, _ = oracle_gdr(q.float().numpy(), k.float().numpy(), v.float().numpy(), gl.numpy(), beta.float().numpy())
+    _close_chunk(o, ro)
+    # "auto" takes the chunked form here and the recurrence when a final state is asked for
+    oa, _ = gdn.chunk_gated_delta_rule(*args, g=gl.to(DEV), beta=beta.to(DEV), initial_state=None,
+                                       output_final_state=False)
+    assert torch.equal(o, oa)
+    orc, st = gdn.chunk_gated_delta_rule(*args, g=gl.to(DEV), beta=beta.to(DEV), initial_state=None,
+                                         output_final_state=True)
+    _close_o(orc, ro)
+    assert st is not None
+    with pytest.raises(RuntimeError):
+        gdn.gated_delta_rule(*args, g=gl.to(DEV), beta=beta.to(DEV), output_final_state=True, algo="chunk")
+
+
+def test_chunk_form_matches_fla_chunk():
+    """Secondary check against the reference's GPU library (FLA chunked kernel)."""
+    fla = pytest.importorskip("fla.ops.gated_delta_rule")
+    B, T, H, HV, K, V = 6, 48, 16, 48, 128, 128
+    q, k, v, gl, beta, h0 = _inputs(B, T, H, HV, K, V, 22)
+    init = h0.to(DEV).expand(B, -1, -1, -1)
+    qr, kr = q.repeat_interleave(3, 2).to(DEV), k.repeat_interleave(3, 2).to(DEV)
+    ref, _ = fla.chunk_gated_delta_rule(qr, kr, v.to(DEV), g=gl.to(DEV), beta=beta.to(DEV),
+                                        initial_state=init.contiguous(), output_final_state=False,
+                                        use_qk_l2norm_in_kernel=True)
+    o, _ = gdn.gated_delta_rule(q.to(DEV), k.to(DEV), v.to(DEV), g=gl.to(DEV), beta=beta.to(DEV),
+                                initial_state=init, algo="chunk")
+    assert float((o.float() - ref.float()).abs().max()) <= 2e-2
