@@ -620,9 +620,12 @@ def gdn_line(dev, stream, flush):
     out = torch.empty_like(x["v"])
     h0 = x["h0"].expand(B, -1, -1, -1)
     t_ours = statistics.median(time_steps(lambda: gdn.gated_delta_rule(
-        x["q"], x["k"], x["v"], g=x["g"], beta=x["beta"], initial_state=h0, out=out), 5, 3, stream, flush))
-    flops = 2.0 * 3 * B * T * HV * K * V
-    line = {"ours_ms": t_ours, "tflops_fp32": flops / t_ours / 1e9,
+        x["q"], x["k"], x["v"], g=x["g"], beta=x["beta"], initial_state=h0, out=out, algo="chunk"),
+        5, 3, stream, flush))
+    t_rec = statistics.median(time_steps(lambda: gdn.gated_delta_rule(
+        x["q"], x["k"], x["v"], g=x["g"], beta=x["beta"], initial_state=h0, out=out, algo="recurrent"),
+        5, 3, stream, flush))
+    line = {"ours_chunk_ms": t_ours, "ours_recurrent_ms": t_rec,
             "workload": f"{B} blocks x {T} tokens, {H} q/k heads -> {HV} value heads, K=V={K}, shared initial state"}
     t_copy = statistics.median(time_steps(lambda: h0.contiguous(), 5, 3, stream, flush))
     line["reference_state_copy_ms"] = t_copy
@@ -640,8 +643,12 @@ def gdn_line(dev, stream, flush):
     line["fla_chunk_ms"] = statistics.median(time_steps(
         lambda: chunk_gated_delta_rule(qr, kr, x["v"], **kw), 5, 3, stream, flush))
     o_ref, _ = fused_recurrent_gated_delta_rule(qr, kr, x["v"], **kw)
-    o, _ = gdn.gated_delta_rule(x["q"], x["k"], x["v"], g=x["g"], beta=x["beta"], initial_state=h0)
-    line["max_abs_diff_vs_fla_recurrent"] = float((o.float() - o_ref.float()).abs().max())
+    o, _ = gdn.gated_delta_rule(x["q"], x["k"], x["v"], g=x["g"], beta=x["beta"], initial_state=h0,
+                                algo="recurrent")
+    line["max_abs_diff_recurrent_vs_fla_recurrent"] = float((o.float() - o_ref.float()).abs().max())
+    o_chk, _ = chunk_gated_delta_rule(qr, kr, x["v"], **kw)
+    o, _ = gdn.gated_delta_rule(x["q"], x["k"], x["v"], g=x["g"], beta=x["beta"], initial_state=h0, algo="chunk")
+    line["max_abs_diff_chunk_vs_fla_chunk"] = float((o.float() - o_chk.float()).abs().max())
     return line
 
 

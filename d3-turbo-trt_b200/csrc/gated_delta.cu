@@ -290,17 +290,18 @@ int launch_k(const GdrParams& p, int beta_dtype, long long blocks, cudaStream_t 
 //   R  = beta_i (v_i - e^gamma_i S0^T k_i)        (rows i)
 //   V' = (I + A)^-1 R                             (forward substitution)
 //   O  = e^gamma_i S0^T q_i + lower-incl( (q_i . k_j) e^(gamma_i - gamma_j) ) V'
-// One CTA = two blocks (M = 128 rows) and one value head; 128 threads. The four
+// One CTA = two blocks (M = 128 rows) and one value head; 256 threads. The four
 // products K K^T, K S0, Q K^T, Q S0 run on tcgen05 into TMEM (bf16 operands,
-// fp32 accumulate: 512 columns), the epilogue (thread = row) forms A, R and the
-// decayed P = lower(Q K^T) as bf16, the solve runs with thread = state column in
-// fp32 registers, then P V' runs on tcgen05 into the freed columns 0..127.
+// fp32 accumulate: 512 columns), the epilogue (two threads per row) forms A, R and
+// the decayed P = lower(Q K^T) as bf16, the solve runs with one thread per (state
+// column, block) in fp32 registers, then P V' runs on tcgen05 into the freed
+// columns 0..127. v rows travel to shared memory by cp.async during the first phase.
 // ---------------------------------------------------------------------------
 namespace gdc {
 
 constexpr int KD = 128;             // K = V = 128
 constexpr int M = 128;              // two blocks of up to 64 tokens
-constexpr int THREADS = 128;
+constexpr int THREADS = 256;          // row phases: two threads per row (64 columns each)
 constexpr int CHUNK = M * 128;      // one [128 rows x 64 bf16] 128B-swizzled chunk
 constexpr int TILE = 2 * CHUNK;     // a [128 x 128] bf16 operand tile
 constexpr int OFF_KN = 0, OFF_QN = TILE, OFF_S0 = 2 * TILE, OFF_P = 3 * TILE, OFF_V = 4 * TILE;
@@ -354,13 +355,16 @@ template <typename In, typename BetaT>
 __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_constant__ GdrParams p, int* err) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ Bars bars;
+  __shared__ float part[2][2][M];  // [q, k][column half][row] partial sums of squares
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = tid & (M - 1), half = tid >> 7;  // row phases: one row, 64 of its 128 columns
   const int hv = blockIdx.y, h = hv / (p.HV / p.H);
-  const int blk = tid >> 6, tl = tid & 63;  // this thread's row: token tl of block blk
+  const int blk = row >> 6, tl = row & 63;  // the row's token tl of block blk
   const int b = blockIdx.x * 2 + blk;
   const bool valid = b < p.B && tl < p.T;
   volatile int* abort_flag = &bars.abort_flag;
+  const int c0 = half * 64;
 
   if (tid == 0) {
     d3b::mbar_init(&bars.mma1, 1);
@@ -369,65 +373,85 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
     bars.abort_flag = 0;
     d3b::fence_barrier_init();
   }
-  // ---- phase 1: g -> gamma, beta; normalised q, k rows; S0 in bf16 ----------
-  bars.gam[tid] = valid ? p.g[b * p.gs[0] + (long long)tl * p.gs[1] + hv * p.gs[2]] : 0.f;
-  bars.beta[tid] = valid ? to_f32(static_cast<const BetaT*>(p.beta)[b * p.bs[0] + (long long)tl * p.bs[1] +
-                                                                     hv * p.bs[2]])
-                         : 0.f;
+  // ---- phase 1: v rows in flight to shared memory; g -> gamma, beta; normalised q, k; S0 in bf16
+  const In* vrow = static_cast<const In*>(p.v) + b * p.vs[0] + (long long)tl * p.vs[1] + hv * p.vs[2];
+  uint8_t* vstage = smem + OFF_V + row * 256 + half * 128;  // raw v rows, read in phase 3
+  if (valid) {
+#pragma unroll
+    for (int x = 0; x < 8; ++x)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d3b::smem_u32(vstage + x * 16)),
+                   "l"(vrow + c0 + x * 8)
+                   : "memory");
+  } else {  // padding rows: zeros, so R and V' stay finite there
+#pragma unroll
+    for (int x = 0; x < 8; ++x) *reinterpret_cast<uint4*>(vstage + x * 16) = make_uint4(0, 0, 0, 0);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  if (half == 0) {
+    bars.gam[row] = valid ? p.g[b * p.gs[0] + (long long)tl * p.gs[1] + hv * p.gs[2]] : 0.f;
+    bars.beta[row] = valid ? to_f32(static_cast<const BetaT*>(p.beta)[b * p.bs[0] + (long long)tl * p.bs[1] +
+                                                                       hv * p.bs[2]])
+                           : 0.f;
+  }
+  const In* qrow = static_cast<const In*>(p.q) + b * p.qs[0] + (long long)tl * p.qs[1] + h * p.qs[2] + c0;
+  const In* krow = static_cast<const In*>(p.k) + b * p.ks[0] + (long long)tl * p.ks[1] + h * p.ks[2] + c0;
+  uint4 rq[8], rk[8];
+#pragma unroll
+  for (int x = 0; x < 8; ++x) {
+    rq[x] = valid ? reinterpret_cast<const uint4*>(qrow)[x] : make_uint4(0, 0, 0, 0);
+    rk[x] = valid ? reinterpret_cast<const uint4*>(krow)[x] : make_uint4(0, 0, 0, 0);
+  }
+  {
+    float sq = 0.f, sk = 0.f;
+#pragma unroll
+    for (int x = 0; x < 8; ++x) {
+      float fq[8], fk[8];
+      unpack8<In>(rq[x], fq);
+      unpack8<In>(rk[x], fk);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        sq = fmaf(fq[e], fq[e], sq);
+        sk = fmaf(fk[e], fk[e], sk);
+      }
+    }
+    part[0][half][row] = sq;
+    part[1][half][row] = sk;
+  }
+  // S0 row `row` (the K index), columns c0..c0+63, as the MN-major B operand in bf16
+  {
+    const float* srow = p.h0 ? p.h0 + hv * p.h0s[1] + (long long)row * p.h0s[2] + c0 : nullptr;
+    float4 s4[16];
+#pragma unroll
+    for (int x = 0; x < 16; ++x) s4[x] = srow ? reinterpret_cast<const float4*>(srow)[x] : make_float4(0, 0, 0, 0);
+#pragma unroll
+    for (int x = 0; x < 8; ++x)
+      *reinterpret_cast<uint4*>(smem + OFF_S0 + sw_off(row, c0 + x * 8)) =
+          make_uint4(pack2<__nv_bfloat16>(s4[2 * x].x, s4[2 * x].y), pack2<__nv_bfloat16>(s4[2 * x].z, s4[2 * x].w),
+                     pack2<__nv_bfloat16>(s4[2 * x + 1].x, s4[2 * x + 1].y),
+                     pack2<__nv_bfloat16>(s4[2 * x + 1].z, s4[2 * x + 1].w));
+  }
   __syncthreads();
   float gam = 0.f;
-  for (int s = blk * 64; s <= tid; ++s) gam += bars.gam[s];
-  __syncthreads();
-  bars.gam[tid] = gam;
-
+  for (int s = blk * 64; s <= row; ++s) gam += bars.gam[s];
   {
-    const In* qrow = static_cast<const In*>(p.q) + b * p.qs[0] + (long long)tl * p.qs[1] + h * p.qs[2];
-    const In* krow = static_cast<const In*>(p.k) + b * p.ks[0] + (long long)tl * p.ks[1] + h * p.ks[2];
-    float sq = 0.f, sk = 0.f;
-    if (valid) {
-#pragma unroll 4
-      for (int c8 = 0; c8 < KD / 8; ++c8) {
-        float fq[8], fk[8];
-        unpack8<In>(reinterpret_cast<const uint4*>(qrow)[c8], fq);
-        unpack8<In>(reinterpret_cast<const uint4*>(krow)[c8], fk);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          sq = fmaf(fq[e], fq[e], sq);
-          sk = fmaf(fk[e], fk[e], sk);
-        }
-      }
-    }
+    const float sq = part[0][0][row] + part[0][1][row], sk = part[1][0][row] + part[1][1][row];
     const float iq = (p.l2norm ? 1.f / sqrtf(sq + 1e-6f) : 1.f) * p.scale;
     const float ik = p.l2norm ? 1.f / sqrtf(sk + 1e-6f) : 1.f;
-#pragma unroll 4
-    for (int c8 = 0; c8 < KD / 8; ++c8) {
-      uint4 oq = make_uint4(0, 0, 0, 0), ok = make_uint4(0, 0, 0, 0);
-      if (valid) {
-        float fq[8], fk[8];
-        unpack8<In>(reinterpret_cast<const uint4*>(qrow)[c8], fq);
-        unpack8<In>(reinterpret_cast<const uint4*>(krow)[c8], fk);
-        oq = make_uint4(pack2<__nv_bfloat16>(fq[0] * iq, fq[1] * iq), pack2<__nv_bfloat16>(fq[2] * iq, fq[3] * iq),
-                        pack2<__nv_bfloat16>(fq[4] * iq, fq[5] * iq), pack2<__nv_bfloat16>(fq[6] * iq, fq[7] * iq));
-        ok = make_uint4(pack2<__nv_bfloat16>(fk[0] * ik, fk[1] * ik), pack2<__nv_bfloat16>(fk[2] * ik, fk[3] * ik),
-                        pack2<__nv_bfloat16>(fk[4] * ik, fk[5] * ik), pack2<__nv_bfloat16>(fk[6] * ik, fk[7] * ik));
-      }
-      *reinterpret_cast<uint4*>(smem + OFF_QN + sw_off(tid, c8 * 8)) = oq;
-      *reinterpret_cast<uint4*>(smem + OFF_KN + sw_off(tid, c8 * 8)) = ok;
-    }
-    // S0 row tid (the K index) as the MN-major B operand, bf16
-    const float* srow = p.h0 ? p.h0 + hv * p.h0s[1] + (long long)tid * p.h0s[2] : nullptr;
-#pragma unroll 4
-    for (int c8 = 0; c8 < KD / 8; ++c8) {
-      uint4 os = make_uint4(0, 0, 0, 0);
-      if (srow) {
-        const float4 a = reinterpret_cast<const float4*>(srow)[2 * c8];
-        const float4 z = reinterpret_cast<const float4*>(srow)[2 * c8 + 1];
-        os = make_uint4(pack2<__nv_bfloat16>(a.x, a.y), pack2<__nv_bfloat16>(a.z, a.w),
-                        pack2<__nv_bfloat16>(z.x, z.y), pack2<__nv_bfloat16>(z.z, z.w));
-      }
-      *reinterpret_cast<uint4*>(smem + OFF_S0 + sw_off(tid, c8 * 8)) = os;
+#pragma unroll
+    for (int x = 0; x < 8; ++x) {
+      float fq[8], fk[8];
+      unpack8<In>(rq[x], fq);
+      unpack8<In>(rk[x], fk);
+      *reinterpret_cast<uint4*>(smem + OFF_QN + sw_off(row, c0 + x * 8)) =
+          make_uint4(pack2<__nv_bfloat16>(fq[0] * iq, fq[1] * iq), pack2<__nv_bfloat16>(fq[2] * iq, fq[3] * iq),
+                     pack2<__nv_bfloat16>(fq[4] * iq, fq[5] * iq), pack2<__nv_bfloat16>(fq[6] * iq, fq[7] * iq));
+      *reinterpret_cast<uint4*>(smem + OFF_KN + sw_off(row, c0 + x * 8)) =
+          make_uint4(pack2<__nv_bfloat16>(fk[0] * ik, fk[1] * ik), pack2<__nv_bfloat16>(fk[2] * ik, fk[3] * ik),
+                     pack2<__nv_bfloat16>(fk[4] * ik, fk[5] * ik), pack2<__nv_bfloat16>(fk[6] * ik, fk[7] * ik));
     }
   }
+  __syncthreads();  // every thread has read the raw g values
+  if (half == 0) bars.gam[row] = gam;
   d3b::fence_proxy_async_smem();
   if (warp == 0) d3b::tmem_alloc(&bars.tmem_slot, TMEM_COLS);
   d3b::tc_fence_before();
@@ -456,18 +480,17 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
   bool ok = d3b::warp_wait(&bars.mma1, 0, abort_flag, err, kSiteChunkMma1);
   d3b::tc_fence_after();
 
-  // ---- phase 3 (thread = row): A, R, P --------------------------------------
+  // ---- phase 3 (row, column half): A, P, R -------------------------------------
   float* Rm = reinterpret_cast<float*>(smem + OFF_R);
   float* Am = reinterpret_cast<float*>(smem + OFF_A);
-  const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+  const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+  asm volatile("cp.async.wait_group 0;" ::: "memory");  // this thread's v copies
   if (ok) {
-    const float beta_i = bars.beta[tid];
+    const float beta_i = bars.beta[row];
     uint32_t r[32];
-    // A: own block's 64 columns of K K^T
-#pragma unroll 1
-    for (int half = 0; half < 2; ++half) {
-      const int j0 = blk * 64 + half * 32;
-      d3b::tmem_ld32(lane_addr + COL_KK + j0, r);
+    {  // A: 32 of the own block's 64 columns of K K^T
+      const int jl0 = half * 32;
+      d3b::tmem_ld32(lane_addr + COL_KK + blk * 64 + jl0, r);
       d3b::tmem_wait_ld();
 #pragma unroll
       for (int x = 0; x < 32; x += 4) {
@@ -475,52 +498,47 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
         float* a = reinterpret_cast<float*>(&av);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int jl = half * 32 + x + e;
+          const int jl = jl0 + x + e;
           a[e] = jl < tl ? beta_i * __uint_as_float(r[x + e]) * __expf(gam - bars.gam[blk * 64 + jl]) : 0.f;
         }
-        *reinterpret_cast<float4*>(Am + tid * A_STRIDE + half * 32 + x) = av;
+        *reinterpret_cast<float4*>(Am + row * A_STRIDE + jl0 + x) = av;
       }
     }
-    // P: the decayed lower triangle (diagonal included) of Q K^T, both blocks' columns (zero off-block)
+    // P: the decayed lower triangle (diagonal included) of Q K^T, zero off the own block
 #pragma unroll 1
-    for (int q4 = 0; q4 < 4; ++q4) {
-      d3b::tmem_ld32(lane_addr + COL_QK + q4 * 32, r);
+    for (int q2 = 0; q2 < 2; ++q2) {
+      const int j0 = c0 + q2 * 32;
+      d3b::tmem_ld32(lane_addr + COL_QK + j0, r);
       d3b::tmem_wait_ld();
 #pragma unroll
       for (int x = 0; x < 32; x += 8) {
         float f[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const int j = q4 * 32 + x + e;
+          const int j = j0 + x + e;
           const bool keep = (j >> 6) == blk && (j & 63) <= tl;
           f[e] = keep ? __uint_as_float(r[x + e]) * __expf(gam - bars.gam[j]) : 0.f;
         }
-        *reinterpret_cast<uint4*>(smem + OFF_P + sw_off(tid, q4 * 32 + x)) =
+        *reinterpret_cast<uint4*>(smem + OFF_P + sw_off(row, j0 + x)) =
             make_uint4(pack2<__nv_bfloat16>(f[0], f[1]), pack2<__nv_bfloat16>(f[2], f[3]),
                        pack2<__nv_bfloat16>(f[4], f[5]), pack2<__nv_bfloat16>(f[6], f[7]));
       }
     }
   }
-  // the K/Q/S0 tiles are free (their products completed): R overwrites them
-  __syncthreads();
+  __syncthreads();  // the K/Q/S0 tiles are free (their products completed): R overwrites them
   if (ok) {
-    const float beta_i = bars.beta[tid];
+    const float beta_i = bars.beta[row];
     const float eg = __expf(gam);
-    const In* vrow = static_cast<const In*>(p.v) + b * p.vs[0] + (long long)tl * p.vs[1] + hv * p.vs[2];
     uint32_t r[32];
 #pragma unroll 1
-    for (int q4 = 0; q4 < 4; ++q4) {
-      d3b::tmem_ld32(lane_addr + COL_KS + q4 * 32, r);
+    for (int q2 = 0; q2 < 2; ++q2) {
+      const int j0 = c0 + q2 * 32;
+      d3b::tmem_ld32(lane_addr + COL_KS + j0, r);
       d3b::tmem_wait_ld();
 #pragma unroll
       for (int x = 0; x < 32; x += 8) {
         float fv[8];
-        if (valid) {
-          unpack8<In>(reinterpret_cast<const uint4*>(vrow)[(q4 * 32 + x) / 8], fv);
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) fv[e] = 0.f;
-        }
+        unpack8<In>(*reinterpret_cast<const uint4*>(smem + OFF_V + row * 256 + (j0 + x) * 2), fv);
         float4 r0, r1;
         r0.x = beta_i * (fv[0] - eg * __uint_as_float(r[x + 0]));
         r0.y = beta_i * (fv[1] - eg * __uint_as_float(r[x + 1]));
@@ -530,40 +548,37 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
         r1.y = beta_i * (fv[5] - eg * __uint_as_float(r[x + 5]));
         r1.z = beta_i * (fv[6] - eg * __uint_as_float(r[x + 6]));
         r1.w = beta_i * (fv[7] - eg * __uint_as_float(r[x + 7]));
-        *reinterpret_cast<float4*>(Rm + tid * R_STRIDE + q4 * 32 + x) = r0;
-        *reinterpret_cast<float4*>(Rm + tid * R_STRIDE + q4 * 32 + x + 4) = r1;
+        *reinterpret_cast<float4*>(Rm + row * R_STRIDE + j0 + x) = r0;
+        *reinterpret_cast<float4*>(Rm + row * R_STRIDE + j0 + x + 4) = r1;
       }
     }
   }
   d3b::tc_fence_before();
-  __syncthreads();
+  __syncthreads();  // R, A complete; the staged v rows are consumed (V' overwrites them)
 
-  // ---- phase 4 (thread = state column c): V' = (I + A)^-1 R per block -------
+  // ---- phase 4 (thread = state column c of block bk): V' = (I + A)^-1 R --------
   if (ok) {
-    const int c = tid;
-#pragma unroll 1
-    for (int bk = 0; bk < 2; ++bk) {
-      float x[64];
+    const int c = tid & (M - 1), bk = tid >> 7;
+    float x[64];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float* arow = Am + (bk * 64 + i) * A_STRIDE;
-        float acc0 = Rm[(bk * 64 + i) * R_STRIDE + c], acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+    for (int i = 0; i < 64; ++i) {
+      const float* arow = Am + (bk * 64 + i) * A_STRIDE;
+      float acc0 = Rm[(bk * 64 + i) * R_STRIDE + c], acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
 #pragma unroll
-        for (int j = 0; j + 4 <= i; j += 4) {
-          const float4 a4 = *reinterpret_cast<const float4*>(arow + j);
-          acc0 = fmaf(-a4.x, x[j], acc0);
-          acc1 = fmaf(-a4.y, x[j + 1], acc1);
-          acc2 = fmaf(-a4.z, x[j + 2], acc2);
-          acc3 = fmaf(-a4.w, x[j + 3], acc3);
-        }
-#pragma unroll
-        for (int j = i & ~3; j < i; ++j) acc0 = fmaf(-arow[j], x[j], acc0);
-        x[i] = (acc0 + acc1) + (acc2 + acc3);
+      for (int j = 0; j + 4 <= i; j += 4) {
+        const float4 a4 = *reinterpret_cast<const float4*>(arow + j);
+        acc0 = fmaf(-a4.x, x[j], acc0);
+        acc1 = fmaf(-a4.y, x[j + 1], acc1);
+        acc2 = fmaf(-a4.z, x[j + 2], acc2);
+        acc3 = fmaf(-a4.w, x[j + 3], acc3);
       }
 #pragma unroll
-      for (int i = 0; i < 64; ++i)
-        *reinterpret_cast<__nv_bfloat16*>(smem + OFF_V + sw_off(bk * 64 + i, c)) = __float2bfloat16_rn(x[i]);
+      for (int j = i & ~3; j < i; ++j) acc0 = fmaf(-arow[j], x[j], acc0);
+      x[i] = (acc0 + acc1) + (acc2 + acc3);
     }
+#pragma unroll
+    for (int i = 0; i < 64; ++i)
+      *reinterpret_cast<__nv_bfloat16*>(smem + OFF_V + sw_off(bk * 64 + i, c)) = __float2bfloat16_rn(x[i]);
   }
   d3b::fence_proxy_async_smem();
   d3b::tc_fence_before();
@@ -585,15 +600,16 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
   if (ok) ok = d3b::warp_wait(&bars.mma2, 0, abort_flag, err, kSiteChunkMma2);
   d3b::tc_fence_after();
 
-  // ---- phase 6 (thread = row): O = e^gamma (Q S0) + P V' ----------------------
+  // ---- phase 6 (row, column half): O = e^gamma (Q S0) + P V' ------------------
   if (ok) {  // warp-uniform: every lane loads (tcgen05.ld is warp-collective), valid rows store
     const float eg = __expf(gam);
     In* orow = static_cast<In*>(p.o) + b * p.os[0] + (long long)tl * p.os[1] + hv * p.os[2];
     uint32_t rs[32], rp[32];
 #pragma unroll 1
-    for (int q4 = 0; q4 < 4; ++q4) {
-      d3b::tmem_ld32(lane_addr + COL_QS + q4 * 32, rs);
-      d3b::tmem_ld32(lane_addr + COL_PV + q4 * 32, rp);
+    for (int q2 = 0; q2 < 2; ++q2) {
+      const int j0 = c0 + q2 * 32;
+      d3b::tmem_ld32(lane_addr + COL_QS + j0, rs);
+      d3b::tmem_ld32(lane_addr + COL_PV + j0, rp);
       d3b::tmem_wait_ld();
       if (valid) {
 #pragma unroll
@@ -601,8 +617,8 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
           float f[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) f[e] = fmaf(eg, __uint_as_float(rs[x + e]), __uint_as_float(rp[x + e]));
-          reinterpret_cast<uint4*>(orow)[(q4 * 32 + x) / 8] = make_uint4(pack2<In>(f[0], f[1]), pack2<In>(f[2], f[3]),
-                                                                         pack2<In>(f[4], f[5]), pack2<In>(f[6], f[7]));
+          reinterpret_cast<uint4*>(orow)[(j0 + x) / 8] = make_uint4(pack2<In>(f[0], f[1]), pack2<In>(f[2], f[3]),
+                                                                    pack2<In>(f[4], f[5]), pack2<In>(f[6], f[7]));
         }
       }
     }

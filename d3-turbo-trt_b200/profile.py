@@ -136,15 +136,17 @@ def gdn_question_inputs(dev: torch.device, B: int = 255, T: int = 48, H: int = 1
     }
 
 
-def _gdn(dev: torch.device):
+def _gdn(dev: torch.device, algo: str):
     x = gdn_question_inputs(dev)
     B = x["q"].shape[0]
     out = torch.empty_like(x["v"])
     fn = lambda: gdn.gated_delta_rule(x["q"], x["k"], x["v"], g=x["g"], beta=x["beta"],
-                                      initial_state=x["h0"].expand(B, -1, -1, -1), out=out)
+                                      initial_state=x["h0"].expand(B, -1, -1, -1), out=out, algo=algo)
     B, T, H, K = x["q"].shape
     HV, V = x["v"].shape[2:]
-    return fn, {"flops": 2.0 * 3 * B * T * HV * K * V}
+    # chunked form: K K^T, K S0, Q K^T, Q S0 and P V' on two 64-token blocks per 128-row tile
+    flops = 2.0 * 5 * 128 * 128 * 128 * ((B + 1) // 2) * HV if algo == "chunk" else 2.0 * 3 * B * T * HV * K * V
+    return fn, {"flops": flops}
 
 
 def build(kernel: str, config: str, dev: torch.device):
@@ -163,7 +165,9 @@ def build(kernel: str, config: str, dev: torch.device):
     if kernel == "snapshot":
         return _snapshot(dev)
     if kernel == "gdn":
-        return _gdn(dev)
+        return _gdn(dev, "chunk")
+    if kernel == "gdn_recurrent":
+        return _gdn(dev, "recurrent")
     raise SystemExit(f"unknown kernel {kernel!r}")
 
 
@@ -171,7 +175,7 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", required=True,
                     choices=["attention", "gemm_fp8", "gemm_int8", "act_quant_fp8", "act_quant_int8", "readout",
-                             "snapshot", "gdn"])
+                             "snapshot", "gdn", "gdn_recurrent"])
     ap.add_argument("--config", default="cfg3a", choices=[*ATTN, "state4k", "cfg2", "cfg4"])
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=1)
