@@ -67,8 +67,9 @@ SIGNATURES: list[tuple[str, Any, list[Any]]] = [
         "d3b_gated_delta_rule",
         _I,
         [_VP, _I64P, _VP, _I64P, _VP, _I64P, _VP, _I64P, _VP, _I, _I64P, _VP, _I64P, _VP, _I64P, _VP,
-         _I, _I, _I, _I, _I, _I, _I, _F, _I, _I, _VP],
+         _I, _I, _I, _I, _I, _I, _I, _F, _I, _I, _VP, _SZ, _VP],
     ),
+    ("d3b_gated_delta_workspace_size", _SZ, [_I, _I, _I]),
     ("d3b_copy_segments", _I, [ctypes.POINTER(CopySegment), _I, _VP]),
     ("d3b_arena_create", _I, [_U64, _U64, ctypes.POINTER(ctypes.c_void_p)]),
     ("d3b_arena_alloc", _I, [_VP, _U64, _U64P]),

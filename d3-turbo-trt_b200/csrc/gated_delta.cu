@@ -313,7 +313,7 @@ constexpr int SMEM_BYTES = OFF_A + M * A_STRIDE * 4 + 1024;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int COL_KK = 0, COL_KS = 128, COL_QK = 256, COL_QS = 384, COL_PV = 0;
 
-enum : int { kSiteChunkMma1 = 3001, kSiteChunkMma2 = 3002, kSiteChunkDrain = 3003 };
+enum : int { kSiteChunkMma1 = 3001, kSiteChunkMma2 = 3002, kSiteChunkDrain = 3003, kSiteChunkLoad = 3004 };
 
 // Byte offset of element (r, c) of a [128 x 128] bf16 tile held as two [128 x 64]
 // chunks in the 128B-swizzle layout (16-byte granule index XOR row % 8); for a
@@ -324,7 +324,7 @@ __device__ __forceinline__ uint32_t sw_off(int r, int c) {
 }
 
 struct Bars {
-  uint64_t mma1, mma2, drain;
+  uint64_t load, mma1, mma2, drain;
   uint32_t tmem_slot;
   int abort_flag;
   float gam[M];   // running sum of g within each block
@@ -351,8 +351,33 @@ __device__ __forceinline__ void unpack8(const uint4& u, float* f) {
   for (int e = 0; e < 8; ++e) f[e] = to_f32(h[e]);
 }
 
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   d3b::smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(d3b::smem_u32(bar))
+               : "memory");
+}
+
+// The initial state of each value head as the bf16 MN-major operand tile the chunk
+// kernel copies into shared memory with one bulk copy (the shared image of S0).
+__global__ void __launch_bounds__(THREADS) s0_tiles_kernel(const float* h0, long long s_hv, long long s_row,
+                                                           uint8_t* tiles) {
+  const int hv = blockIdx.x, row = threadIdx.x & (M - 1), c0 = (threadIdx.x >> 7) * 64;
+  const float* src = h0 + hv * s_hv + row * s_row + c0;
+  uint8_t* tile = tiles + (size_t)hv * TILE;
+#pragma unroll
+  for (int x = 0; x < 8; ++x) {
+    const float4 a = reinterpret_cast<const float4*>(src)[2 * x];
+    const float4 z = reinterpret_cast<const float4*>(src)[2 * x + 1];
+    *reinterpret_cast<uint4*>(tile + sw_off(row, c0 + x * 8)) =
+        make_uint4(pack2<__nv_bfloat16>(a.x, a.y), pack2<__nv_bfloat16>(a.z, a.w), pack2<__nv_bfloat16>(z.x, z.y),
+                   pack2<__nv_bfloat16>(z.z, z.w));
+  }
+}
+
 template <typename In, typename BetaT>
-__global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_constant__ GdrParams p, int* err) {
+__global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_constant__ GdrParams p,
+                                                             const uint8_t* s0_tiles, int* err) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ Bars bars;
   __shared__ float part[2][2][M];  // [q, k][column half][row] partial sums of squares
@@ -367,39 +392,59 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
   const int c0 = half * 64;
 
   if (tid == 0) {
+    d3b::mbar_init(&bars.load, THREADS);
     d3b::mbar_init(&bars.mma1, 1);
     d3b::mbar_init(&bars.mma2, 1);
     d3b::mbar_init(&bars.drain, 1);
     bars.abort_flag = 0;
     d3b::fence_barrier_init();
   }
-  // ---- phase 1: v rows in flight to shared memory; g -> gamma, beta; normalised q, k; S0 in bf16
-  const In* vrow = static_cast<const In*>(p.v) + b * p.vs[0] + (long long)tl * p.vs[1] + hv * p.vs[2];
-  uint8_t* vstage = smem + OFF_V + row * 256 + half * 128;  // raw v rows, read in phase 3
-  if (valid) {
+  // ---- phase 1: q, k, v rows and the head's S0 tile arrive by bulk copies on one
+  // mbarrier (one arrival per thread, each with the bytes it copies); g -> gamma, beta
+  uint8_t* stage_q = smem + OFF_P;  // raw rows, [128][256 B] each; free until phase 3
+  uint8_t* stage_k = smem + OFF_A;
+  uint8_t* stage_v = smem + OFF_V;
+  if (!s0_tiles) {  // no initial state: a zero S0 tile
 #pragma unroll
-    for (int x = 0; x < 8; ++x)
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d3b::smem_u32(vstage + x * 16)),
-                   "l"(vrow + c0 + x * 8)
-                   : "memory");
-  } else {  // padding rows: zeros, so R and V' stay finite there
-#pragma unroll
-    for (int x = 0; x < 8; ++x) *reinterpret_cast<uint4*>(vstage + x * 16) = make_uint4(0, 0, 0, 0);
+    for (int x = 0; x < TILE / 16 / THREADS; ++x)
+      reinterpret_cast<uint4*>(smem + OFF_S0)[x * THREADS + tid] = make_uint4(0, 0, 0, 0);
   }
-  asm volatile("cp.async.commit_group;" ::: "memory");
+  if (half == 0 && !valid) {  // padding rows: zeros, so every product and R stay finite there
+#pragma unroll
+    for (int x = 0; x < 16; ++x) {
+      reinterpret_cast<uint4*>(stage_q + row * 256)[x] = make_uint4(0, 0, 0, 0);
+      reinterpret_cast<uint4*>(stage_k + row * 256)[x] = make_uint4(0, 0, 0, 0);
+      reinterpret_cast<uint4*>(stage_v + row * 256)[x] = make_uint4(0, 0, 0, 0);
+    }
+  }
+  __syncthreads();  // barrier init visible
+  if (half == 0 && valid) {
+    d3b::mbar_arrive_expect_tx(&bars.load, 3 * 256);
+    bulk_load(stage_q + row * 256, static_cast<const In*>(p.q) + b * p.qs[0] + (long long)tl * p.qs[1] + h * p.qs[2],
+              256, &bars.load);
+    bulk_load(stage_k + row * 256, static_cast<const In*>(p.k) + b * p.ks[0] + (long long)tl * p.ks[1] + h * p.ks[2],
+              256, &bars.load);
+    bulk_load(stage_v + row * 256, static_cast<const In*>(p.v) + b * p.vs[0] + (long long)tl * p.vs[1] + hv * p.vs[2],
+              256, &bars.load);
+  } else if (tid == THREADS - 1 && s0_tiles) {
+    d3b::mbar_arrive_expect_tx(&bars.load, TILE);
+    bulk_load(smem + OFF_S0, s0_tiles + (size_t)hv * TILE, TILE / 2, &bars.load);
+    bulk_load(smem + OFF_S0 + TILE / 2, s0_tiles + (size_t)hv * TILE + TILE / 2, TILE / 2, &bars.load);
+  } else {
+    d3b::mbar_arrive(&bars.load);
+  }
   if (half == 0) {
     bars.gam[row] = valid ? p.g[b * p.gs[0] + (long long)tl * p.gs[1] + hv * p.gs[2]] : 0.f;
     bars.beta[row] = valid ? to_f32(static_cast<const BetaT*>(p.beta)[b * p.bs[0] + (long long)tl * p.bs[1] +
                                                                        hv * p.bs[2]])
                            : 0.f;
   }
-  const In* qrow = static_cast<const In*>(p.q) + b * p.qs[0] + (long long)tl * p.qs[1] + h * p.qs[2] + c0;
-  const In* krow = static_cast<const In*>(p.k) + b * p.ks[0] + (long long)tl * p.ks[1] + h * p.ks[2] + c0;
+  bool ok = d3b::warp_wait(&bars.load, 0, abort_flag, err, kSiteChunkLoad);
   uint4 rq[8], rk[8];
 #pragma unroll
   for (int x = 0; x < 8; ++x) {
-    rq[x] = valid ? reinterpret_cast<const uint4*>(qrow)[x] : make_uint4(0, 0, 0, 0);
-    rk[x] = valid ? reinterpret_cast<const uint4*>(krow)[x] : make_uint4(0, 0, 0, 0);
+    rq[x] = reinterpret_cast<const uint4*>(stage_q + row * 256 + half * 128)[x];
+    rk[x] = reinterpret_cast<const uint4*>(stage_k + row * 256 + half * 128)[x];
   }
   {
     float sq = 0.f, sk = 0.f;
@@ -416,19 +461,6 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
     }
     part[0][half][row] = sq;
     part[1][half][row] = sk;
-  }
-  // S0 row `row` (the K index), columns c0..c0+63, as the MN-major B operand in bf16
-  {
-    const float* srow = p.h0 ? p.h0 + hv * p.h0s[1] + (long long)row * p.h0s[2] + c0 : nullptr;
-    float4 s4[16];
-#pragma unroll
-    for (int x = 0; x < 16; ++x) s4[x] = srow ? reinterpret_cast<const float4*>(srow)[x] : make_float4(0, 0, 0, 0);
-#pragma unroll
-    for (int x = 0; x < 8; ++x)
-      *reinterpret_cast<uint4*>(smem + OFF_S0 + sw_off(row, c0 + x * 8)) =
-          make_uint4(pack2<__nv_bfloat16>(s4[2 * x].x, s4[2 * x].y), pack2<__nv_bfloat16>(s4[2 * x].z, s4[2 * x].w),
-                     pack2<__nv_bfloat16>(s4[2 * x + 1].x, s4[2 * x + 1].y),
-                     pack2<__nv_bfloat16>(s4[2 * x + 1].z, s4[2 * x + 1].w));
   }
   __syncthreads();
   float gam = 0.f;
@@ -461,7 +493,7 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
   const uint32_t s_base = d3b::smem_u32(smem);
 
   // ---- phase 2: K K^T, K S0, Q K^T, Q S0 -------------------------------------
-  if (tid == 0) {
+  if (tid == 0 && ok) {
     constexpr uint32_t id_kk = d3b::make_idesc(1, 1, 1, 0, 0, M, KD);  // both K-major
     constexpr uint32_t id_ks = d3b::make_idesc(1, 1, 1, 0, 1, M, KD);  // B (S0) MN-major
 #pragma unroll
@@ -477,14 +509,13 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
     }
     d3b::mma_commit(&bars.mma1);
   }
-  bool ok = d3b::warp_wait(&bars.mma1, 0, abort_flag, err, kSiteChunkMma1);
+  if (ok) ok = d3b::warp_wait(&bars.mma1, 0, abort_flag, err, kSiteChunkMma1);
   d3b::tc_fence_after();
 
   // ---- phase 3 (row, column half): A, P, R -------------------------------------
   float* Rm = reinterpret_cast<float*>(smem + OFF_R);
   float* Am = reinterpret_cast<float*>(smem + OFF_A);
   const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-  asm volatile("cp.async.wait_group 0;" ::: "memory");  // this thread's v copies
   if (ok) {
     const float beta_i = bars.beta[row];
     uint32_t r[32];
@@ -645,11 +676,16 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
 }  // namespace gdc
 
 template <typename In>
-int launch_chunk(const GdrParams& p, int beta_dtype, cudaStream_t s) {
+int launch_chunk(const GdrParams& p, int beta_dtype, uint8_t* s0_tiles, cudaStream_t s) {
   static int attr_set[64][3] = {{0}};
   const int dev = d3b_host::current_device();
   int* err = d3b_host::device_error_word();
   if (!err) return D3B_ECUDA;
+  if (p.h0) {  // the shared initial state -> one bf16 operand tile per value head
+    gdc::s0_tiles_kernel<<<p.HV, gdc::THREADS, 0, s>>>(p.h0, p.h0s[1], p.h0s[2], s0_tiles);
+    if (const int st = d3b_host::check_launch()) return st;
+  }
+  const uint8_t* tiles = p.h0 ? s0_tiles : nullptr;
   const dim3 grid((unsigned)((p.B + 1) / 2), (unsigned)p.HV);
   auto go = [&](auto kernel, int which) -> int {
     if (dev >= 0 && dev < 64 && !attr_set[dev][which]) {
@@ -657,7 +693,7 @@ int launch_chunk(const GdrParams& p, int beta_dtype, cudaStream_t s) {
         return D3B_ECUDA;
       attr_set[dev][which] = 1;
     }
-    kernel<<<grid, gdc::THREADS, gdc::SMEM_BYTES, s>>>(p, err);
+    kernel<<<grid, gdc::THREADS, gdc::SMEM_BYTES, s>>>(p, tiles, err);
     return d3b_host::check_launch();
   };
   switch (beta_dtype) {
@@ -672,13 +708,17 @@ bool aligned(const void* ptr, int bytes) { return reinterpret_cast<uintptr_t>(pt
 
 }  // namespace
 
+extern "C" size_t d3b_gated_delta_workspace_size(int HV, int K, int V) {
+  return (HV > 0 && K == 128 && V == 128) ? (size_t)HV * gdc::TILE : 0;
+}
+
 extern "C" int d3b_gated_delta_rule(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
                                     const void* v, const int64_t* v_strides, const float* g,
                                     const int64_t* g_strides, const void* beta, int beta_dtype,
                                     const int64_t* beta_strides, const float* h0, const int64_t* h0_strides,
                                     void* o, const int64_t* o_strides, float* ht, int B, int T, int H, int HV,
-                                    int K, int V, int dtype, float scale, int l2norm, int algo,
-                                    d3b_stream_t stream) {
+                                    int K, int V, int dtype, float scale, int l2norm, int algo, void* workspace,
+                                    size_t workspace_bytes, d3b_stream_t stream) {
   if (B < 0 || T < 0 || H <= 0 || HV <= 0 || HV % H != 0 || V <= 0 || V % 32 != 0) return D3B_EINVAL;
   if (!q_strides || !k_strides || !v_strides || !g_strides || !beta_strides || !o_strides) return D3B_EINVAL;
   if (h0 && !h0_strides) return D3B_EINVAL;
@@ -731,10 +771,14 @@ extern "C" int d3b_gated_delta_rule(const void* q, const int64_t* q_strides, con
     rows16 = rows16 && q_strides[i] % 8 == 0 && k_strides[i] % 8 == 0 && v_strides[i] % 8 == 0 &&
              o_strides[i] % 8 == 0;
   if (h0) rows16 = rows16 && h0_strides[1] % 4 == 0 && h0_strides[2] % 4 == 0;
-  const bool chunk_ok = K == 128 && V == 128 && T <= 64 && !ht && (!h0 || h0_strides[0] == 0 || B == 1) && rows16;
+  const bool ws_ok = !h0 || (workspace && workspace_bytes >= d3b_gated_delta_workspace_size(HV, K, V) &&
+                             aligned(workspace, 16));
+  const bool chunk_ok =
+      K == 128 && V == 128 && T <= 64 && !ht && (!h0 || h0_strides[0] == 0 || B == 1) && rows16 && ws_ok;
   if (algo == 2 && !chunk_ok) return D3B_EUNSUPPORTED;
   if (algo == 2 || (algo == 0 && chunk_ok && T > 0))
-    return dtype == D3B_BF16 ? launch_chunk<__nv_bfloat16>(p, beta_dtype, s) : launch_chunk<__half>(p, beta_dtype, s);
+    return dtype == D3B_BF16 ? launch_chunk<__nv_bfloat16>(p, beta_dtype, static_cast<uint8_t*>(workspace), s)
+                             : launch_chunk<__half>(p, beta_dtype, static_cast<uint8_t*>(workspace), s);
   if (K == 128)
     return dtype == D3B_BF16 ? launch_k<128, __nv_bfloat16>(p, beta_dtype, blocks, s)
                              : launch_k<128, __half>(p, beta_dtype, blocks, s);

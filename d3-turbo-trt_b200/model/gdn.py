@@ -23,6 +23,22 @@ import torch
 from .. import _lib
 
 
+_WORKSPACES: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
+    """Per-device scratch for the chunked form's state tiles, grown on demand and reused; the
+    calls that use it are ordered on the stream."""
+    if nbytes == 0:
+        return None
+    key = (device.index or 0, torch.cuda.current_stream(device).cuda_stream)
+    buf = _WORKSPACES.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = buf
+    return buf
+
+
 def _strides3(t: torch.Tensor, what: str) -> object:
     if t.stride(-1) != 1:
         raise RuntimeError(f"{what}: the last dimension must be contiguous")
@@ -83,13 +99,15 @@ def gated_delta_rule(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, g: to
     elif out.shape != (B, T, HV, V) or out.dtype != v.dtype or out.stride(-1) != 1:
         raise RuntimeError("gated_delta_rule: out must be [B,T,HV,V] in v's dtype with a contiguous last dim")
     ht = torch.empty(B, HV, K, V, dtype=torch.float32, device=v.device) if output_final_state else None
+    ws = _workspace(v.device, int(_lib.lib().d3b_gated_delta_workspace_size(HV, K, V))) if algo != "recurrent" else None
     with torch.cuda.device(v.device):
         st = _lib.lib().d3b_gated_delta_rule(
             _lib.ptr(q), _strides3(q, "q"), _lib.ptr(k), _strides3(k, "k"), _lib.ptr(v), _strides3(v, "v"),
             _lib.ptr(g), _lib.i64_array(g.stride()), _lib.ptr(beta), _lib.dtype_code(beta.dtype),
             _lib.i64_array(beta.stride()), _lib.ptr(h0), h0s, _lib.ptr(out), _strides3(out, "out"), _lib.ptr(ht),
             B, T, H, HV, K, V, _lib.dtype_code(v.dtype), float(K ** -0.5 if scale is None else scale),
-            1 if use_qk_l2norm_in_kernel else 0, ALGOS[algo], _lib.stream_of(v))
+            1 if use_qk_l2norm_in_kernel else 0, ALGOS[algo], _lib.ptr(ws), 0 if ws is None else ws.numel(),
+            _lib.stream_of(v))
     _lib.check(st, "d3b_gated_delta_rule")
     return out, ht
 

@@ -210,14 +210,19 @@ D3B_API int d3b_selftest_wait_timeout(int limit_ms, d3b_stream_t stream);
  *   algo: 1 = token recurrence (fp32 throughout, FLA's fused recurrent numerics);
  *   2 = chunked form on the tensor cores (bf16 products, fp32 accumulate and
  *   solve; T <= 64, K = V = 128, h0 NULL or shared by all rows, ht NULL, 16-byte
- *   rows, else D3B_EUNSUPPORTED); 0 = the chunked form where it applies, else 1.
+ *   rows, a workspace of d3b_gated_delta_workspace_size() bytes when h0 is given,
+ *   else D3B_EUNSUPPORTED); 0 = the chunked form where it applies, else 1.
  */
 D3B_API int d3b_gated_delta_rule(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
                                  const void* v, const int64_t* v_strides, const float* g, const int64_t* g_strides,
                                  const void* beta, int beta_dtype, const int64_t* beta_strides, const float* h0,
                                  const int64_t* h0_strides, void* o, const int64_t* o_strides, float* ht, int B,
                                  int T, int H, int HV, int K, int V, int dtype, float scale, int l2norm, int algo,
-                                 d3b_stream_t stream);
+                                 void* workspace, size_t workspace_bytes, d3b_stream_t stream);
+
+/* Device workspace the chunked form needs with an initial state: HV bf16 copies of
+ * the state, 32 KiB each (0 where the chunked form does not apply). */
+D3B_API size_t d3b_gated_delta_workspace_size(int HV, int K, int V);
 
 /*
  * State snapshots (the per-layer K/V and GDN states one state pass leaves

@@ -128,7 +128,7 @@ def test_gated_delta_rejects_bad_arguments():
     def call(B=2, T=3, H=1, HV=2, K=64, V=64, dtype=_lib.BF16, beta_dtype=_lib.BF16, ptr=p, strides=st, algo=0):
         return lib.d3b_gated_delta_rule(ptr, strides, ptr, strides, ptr, strides, ptr, strides, ptr, beta_dtype,
                                         strides, None, None, ptr, strides, None, B, T, H, HV, K, V, dtype, 0.125,
-                                        1, algo, None)
+                                        1, algo, None, 0, None)
 
     assert call(K=96) == _lib.EUNSUPPORTED
     assert call(V=48) == _lib.EINVAL
@@ -141,6 +141,8 @@ def test_gated_delta_rejects_bad_arguments():
     assert call(algo=3) == _lib.EINVAL
     assert call(algo=2) == _lib.EUNSUPPORTED  # the chunked form needs K = V = 128
     assert call(algo=2, K=128, V=128, T=65) == _lib.EUNSUPPORTED  # and blocks of <= 64 tokens
+    assert lib.d3b_gated_delta_workspace_size(48, 128, 128) == 48 * 32768
+    assert lib.d3b_gated_delta_workspace_size(48, 64, 64) == 0
 
 
 def test_wait_selftest_rejects_bad_limit():
