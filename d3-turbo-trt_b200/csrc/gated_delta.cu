@@ -310,6 +310,7 @@ constexpr int A_STRIDE = 68;        // fp32 row stride of A
 constexpr int OFF_R = 0;            // aliases the K/Q/S0 tiles once their products are done
 constexpr int OFF_A = 5 * TILE;
 constexpr int SMEM_BYTES = OFF_A + M * A_STRIDE * 4 + 1024;
+constexpr int V_STAGE = 272;        // staged v row stride (bytes): 128 rows fit the A region
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int COL_KK = 0, COL_KS = 128, COL_QK = 256, COL_QS = 384, COL_PV = 0;
 
@@ -401,9 +402,11 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
   }
   // ---- phase 1: q, k, v rows and the head's S0 tile arrive by bulk copies on one
   // mbarrier (one arrival per thread, each with the bytes it copies); g -> gamma, beta
-  uint8_t* stage_q = smem + OFF_P;  // raw rows, [128][256 B] each; free until phase 3
-  uint8_t* stage_k = smem + OFF_A;
-  uint8_t* stage_v = smem + OFF_V;
+  // raw rows: q and k at 256 B per row (read back with a row-rotated granule order, so
+  // the 8 rows a quarter-warp reads hit 8 different bank groups), v at 272 B per row
+  uint8_t* stage_q = smem + OFF_P;  // free until the P tile is written
+  uint8_t* stage_k = smem + OFF_V;  // free until V' is written
+  uint8_t* stage_v = smem + OFF_A;  // free until A is written (after R is formed)
   if (!s0_tiles) {  // no initial state: a zero S0 tile
 #pragma unroll
     for (int x = 0; x < TILE / 16 / THREADS; ++x)
@@ -414,7 +417,7 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
     for (int x = 0; x < 16; ++x) {
       reinterpret_cast<uint4*>(stage_q + row * 256)[x] = make_uint4(0, 0, 0, 0);
       reinterpret_cast<uint4*>(stage_k + row * 256)[x] = make_uint4(0, 0, 0, 0);
-      reinterpret_cast<uint4*>(stage_v + row * 256)[x] = make_uint4(0, 0, 0, 0);
+      reinterpret_cast<uint4*>(stage_v + row * V_STAGE)[x] = make_uint4(0, 0, 0, 0);
     }
   }
   __syncthreads();  // barrier init visible
@@ -424,8 +427,8 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
               256, &bars.load);
     bulk_load(stage_k + row * 256, static_cast<const In*>(p.k) + b * p.ks[0] + (long long)tl * p.ks[1] + h * p.ks[2],
               256, &bars.load);
-    bulk_load(stage_v + row * 256, static_cast<const In*>(p.v) + b * p.vs[0] + (long long)tl * p.vs[1] + hv * p.vs[2],
-              256, &bars.load);
+    bulk_load(stage_v + row * V_STAGE,
+              static_cast<const In*>(p.v) + b * p.vs[0] + (long long)tl * p.vs[1] + hv * p.vs[2], 256, &bars.load);
   } else if (tid == THREADS - 1 && s0_tiles) {
     d3b::mbar_arrive_expect_tx(&bars.load, TILE);
     bulk_load(smem + OFF_S0, s0_tiles + (size_t)hv * TILE, TILE / 2, &bars.load);
@@ -440,11 +443,12 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
                            : 0.f;
   }
   bool ok = d3b::warp_wait(&bars.load, 0, abort_flag, err, kSiteChunkLoad);
-  uint4 rq[8], rk[8];
+  uint4 rq[8], rk[8];  // rq[x] holds columns c0 + gx(x) * 8 .. + 7
+  auto gx = [&](int x) { return (x + row) & 7; };
 #pragma unroll
   for (int x = 0; x < 8; ++x) {
-    rq[x] = reinterpret_cast<const uint4*>(stage_q + row * 256 + half * 128)[x];
-    rk[x] = reinterpret_cast<const uint4*>(stage_k + row * 256 + half * 128)[x];
+    rq[x] = reinterpret_cast<const uint4*>(stage_q + row * 256 + half * 128)[gx(x)];
+    rk[x] = reinterpret_cast<const uint4*>(stage_k + row * 256 + half * 128)[gx(x)];
   }
   {
     float sq = 0.f, sk = 0.f;
@@ -474,10 +478,10 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
       float fq[8], fk[8];
       unpack8<In>(rq[x], fq);
       unpack8<In>(rk[x], fk);
-      *reinterpret_cast<uint4*>(smem + OFF_QN + sw_off(row, c0 + x * 8)) =
+      *reinterpret_cast<uint4*>(smem + OFF_QN + sw_off(row, c0 + gx(x) * 8)) =
           make_uint4(pack2<__nv_bfloat16>(fq[0] * iq, fq[1] * iq), pack2<__nv_bfloat16>(fq[2] * iq, fq[3] * iq),
                      pack2<__nv_bfloat16>(fq[4] * iq, fq[5] * iq), pack2<__nv_bfloat16>(fq[6] * iq, fq[7] * iq));
-      *reinterpret_cast<uint4*>(smem + OFF_KN + sw_off(row, c0 + x * 8)) =
+      *reinterpret_cast<uint4*>(smem + OFF_KN + sw_off(row, c0 + gx(x) * 8)) =
           make_uint4(pack2<__nv_bfloat16>(fk[0] * ik, fk[1] * ik), pack2<__nv_bfloat16>(fk[2] * ik, fk[3] * ik),
                      pack2<__nv_bfloat16>(fk[4] * ik, fk[5] * ik), pack2<__nv_bfloat16>(fk[6] * ik, fk[7] * ik));
     }
@@ -518,6 +522,34 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
   const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
   if (ok) {
     const float beta_i = bars.beta[row];
+    const float eg = __expf(gam);
+    uint32_t r[32];
+#pragma unroll 1
+    for (int q2 = 0; q2 < 2; ++q2) {
+      const int j0 = c0 + q2 * 32;
+      d3b::tmem_ld32(lane_addr + COL_KS + j0, r);
+      d3b::tmem_wait_ld();
+#pragma unroll
+      for (int x = 0; x < 32; x += 8) {
+        float fv[8];
+        unpack8<In>(*reinterpret_cast<const uint4*>(stage_v + row * V_STAGE + (j0 + x) * 2), fv);
+        float4 r0, r1;
+        r0.x = beta_i * (fv[0] - eg * __uint_as_float(r[x + 0]));
+        r0.y = beta_i * (fv[1] - eg * __uint_as_float(r[x + 1]));
+        r0.z = beta_i * (fv[2] - eg * __uint_as_float(r[x + 2]));
+        r0.w = beta_i * (fv[3] - eg * __uint_as_float(r[x + 3]));
+        r1.x = beta_i * (fv[4] - eg * __uint_as_float(r[x + 4]));
+        r1.y = beta_i * (fv[5] - eg * __uint_as_float(r[x + 5]));
+        r1.z = beta_i * (fv[6] - eg * __uint_as_float(r[x + 6]));
+        r1.w = beta_i * (fv[7] - eg * __uint_as_float(r[x + 7]));
+        *reinterpret_cast<float4*>(Rm + row * R_STRIDE + j0 + x) = r0;
+        *reinterpret_cast<float4*>(Rm + row * R_STRIDE + j0 + x + 4) = r1;
+      }
+    }
+  }
+  __syncthreads();  // R is formed: the staged v rows (A region) are consumed
+  if (ok) {
+    const float beta_i = bars.beta[row];
     uint32_t r[32];
     {  // A: 32 of the own block's 64 columns of K K^T
       const int jl0 = half * 32;
@@ -556,36 +588,8 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
       }
     }
   }
-  __syncthreads();  // the K/Q/S0 tiles are free (their products completed): R overwrites them
-  if (ok) {
-    const float beta_i = bars.beta[row];
-    const float eg = __expf(gam);
-    uint32_t r[32];
-#pragma unroll 1
-    for (int q2 = 0; q2 < 2; ++q2) {
-      const int j0 = c0 + q2 * 32;
-      d3b::tmem_ld32(lane_addr + COL_KS + j0, r);
-      d3b::tmem_wait_ld();
-#pragma unroll
-      for (int x = 0; x < 32; x += 8) {
-        float fv[8];
-        unpack8<In>(*reinterpret_cast<const uint4*>(smem + OFF_V + row * 256 + (j0 + x) * 2), fv);
-        float4 r0, r1;
-        r0.x = beta_i * (fv[0] - eg * __uint_as_float(r[x + 0]));
-        r0.y = beta_i * (fv[1] - eg * __uint_as_float(r[x + 1]));
-        r0.z = beta_i * (fv[2] - eg * __uint_as_float(r[x + 2]));
-        r0.w = beta_i * (fv[3] - eg * __uint_as_float(r[x + 3]));
-        r1.x = beta_i * (fv[4] - eg * __uint_as_float(r[x + 4]));
-        r1.y = beta_i * (fv[5] - eg * __uint_as_float(r[x + 5]));
-        r1.z = beta_i * (fv[6] - eg * __uint_as_float(r[x + 6]));
-        r1.w = beta_i * (fv[7] - eg * __uint_as_float(r[x + 7]));
-        *reinterpret_cast<float4*>(Rm + row * R_STRIDE + j0 + x) = r0;
-        *reinterpret_cast<float4*>(Rm + row * R_STRIDE + j0 + x + 4) = r1;
-      }
-    }
-  }
   d3b::tc_fence_before();
-  __syncthreads();  // R, A complete; the staged v rows are consumed (V' overwrites them)
+  __syncthreads();  // R, A, P complete; the staged k rows are consumed (V' overwrites them)
 
   // ---- phase 4 (thread = state column c of block bk): V' = (I + A)^-1 R --------
   if (ok) {
