@@ -294,8 +294,9 @@ int launch_k(const GdrParams& p, int beta_dtype, long long blocks, cudaStream_t 
 // products K K^T, K S0, Q K^T, Q S0 run on tcgen05 into TMEM (bf16 operands,
 // fp32 accumulate: 512 columns), the epilogue (two threads per row) forms A, R and
 // the decayed P = lower(Q K^T) as bf16, the solve runs with one thread per (state
-// column, block) in fp32 registers, then P V' runs on tcgen05 into the freed
-// columns 0..127. v rows travel to shared memory by cp.async during the first phase.
+// column, block) in fp32 registers (column-oriented, A stored transposed), then
+// P V' runs on tcgen05 into the freed columns 0..127. q, k, v rows and the state's
+// bf16 image arrive by bulk copies during the first phase.
 // ---------------------------------------------------------------------------
 namespace gdc {
 
@@ -555,21 +556,24 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
       const int jl0 = half * 32;
       d3b::tmem_ld32(lane_addr + COL_KK + blk * 64 + jl0, r);
       d3b::tmem_wait_ld();
+      // stored transposed, Am[(blk * 64 + j) * A_STRIDE + i] = A[i][j]: the solve reads columns
 #pragma unroll
-      for (int x = 0; x < 32; x += 4) {
-        float4 av;
-        float* a = reinterpret_cast<float*>(&av);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int jl = jl0 + x + e;
-          a[e] = jl < tl ? beta_i * __uint_as_float(r[x + e]) * __expf(gam - bars.gam[blk * 64 + jl]) : 0.f;
-        }
-        *reinterpret_cast<float4*>(Am + row * A_STRIDE + jl0 + x) = av;
+      for (int x = 0; x < 32; ++x) {
+        const int jl = jl0 + x;
+        Am[(blk * 64 + jl) * A_STRIDE + tl] =
+            jl < tl ? beta_i * __uint_as_float(r[x]) * __expf(gam - bars.gam[blk * 64 + jl]) : 0.f;
       }
     }
-    // P: the decayed lower triangle (diagonal included) of Q K^T, zero off the own block
+    // P: the decayed lower triangle (diagonal included) of Q K^T, zero off the own block.
+    // A warp's 32 rows lie in one block, so a column half off that block is all zeros
+    // (warp-uniform: no TMEM read there).
+    if (half != blk) {
+#pragma unroll
+      for (int x = 0; x < 64; x += 8)
+        *reinterpret_cast<uint4*>(smem + OFF_P + sw_off(row, c0 + x)) = make_uint4(0, 0, 0, 0);
+    }
 #pragma unroll 1
-    for (int q2 = 0; q2 < 2; ++q2) {
+    for (int q2 = 0; q2 < 2 && half == blk; ++q2) {
       const int j0 = c0 + q2 * 32;
       d3b::tmem_ld32(lane_addr + COL_QK + j0, r);
       d3b::tmem_wait_ld();
@@ -579,8 +583,7 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int j = j0 + x + e;
-          const bool keep = (j >> 6) == blk && (j & 63) <= tl;
-          f[e] = keep ? __uint_as_float(r[x + e]) * __expf(gam - bars.gam[j]) : 0.f;
+          f[e] = (j & 63) <= tl ? __uint_as_float(r[x + e]) * __expf(gam - bars.gam[j]) : 0.f;
         }
         *reinterpret_cast<uint4*>(smem + OFF_P + sw_off(row, j0 + x)) =
             make_uint4(pack2<__nv_bfloat16>(f[0], f[1]), pack2<__nv_bfloat16>(f[2], f[3]),
@@ -594,22 +597,25 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
   // ---- phase 4 (thread = state column c of block bk): V' = (I + A)^-1 R --------
   if (ok) {
     const int c = tid & (M - 1), bk = tid >> 7;
+    // column-oriented forward substitution: once x[j] is final it updates every later
+    // row at once, so the dependent chain is one FMA per row and the rest overlaps
     float x[64];
 #pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      const float* arow = Am + (bk * 64 + i) * A_STRIDE;
-      float acc0 = Rm[(bk * 64 + i) * R_STRIDE + c], acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+    for (int i = 0; i < 64; ++i) x[i] = Rm[(bk * 64 + i) * R_STRIDE + c];
 #pragma unroll
-      for (int j = 0; j + 4 <= i; j += 4) {
-        const float4 a4 = *reinterpret_cast<const float4*>(arow + j);
-        acc0 = fmaf(-a4.x, x[j], acc0);
-        acc1 = fmaf(-a4.y, x[j + 1], acc1);
-        acc2 = fmaf(-a4.z, x[j + 2], acc2);
-        acc3 = fmaf(-a4.w, x[j + 3], acc3);
+    for (int j = 0; j < 63; ++j) {
+      const float xj = x[j];
+      const float* col = Am + (bk * 64 + j) * A_STRIDE;  // A[i][j], i = 0..63
+#pragma unroll
+      for (int i = j + 1; i < ((j + 4) & ~3) && i < 64; ++i) x[i] = fmaf(-col[i], xj, x[i]);
+#pragma unroll
+      for (int i = (j + 4) & ~3; i < 64; i += 4) {
+        const float4 a4 = *reinterpret_cast<const float4*>(col + i);
+        x[i] = fmaf(-a4.x, xj, x[i]);
+        x[i + 1] = fmaf(-a4.y, xj, x[i + 1]);
+        x[i + 2] = fmaf(-a4.z, xj, x[i + 2]);
+        x[i + 3] = fmaf(-a4.w, xj, x[i + 3]);
       }
-#pragma unroll
-      for (int j = i & ~3; j < i; ++j) acc0 = fmaf(-arow[j], x[j], acc0);
-      x[i] = (acc0 + acc1) + (acc2 + acc3);
     }
 #pragma unroll
     for (int i = 0; i < 64; ++i)
