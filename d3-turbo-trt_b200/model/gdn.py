@@ -122,6 +122,17 @@ def recurrent_gated_delta_rule(q, k, v, *, g, beta, initial_state, output_final_
 
 def chunk_gated_delta_rule(q, k, v, *, g, beta, initial_state, output_final_state, use_qk_l2norm_in_kernel=True):
     """Drop-in for d3trt/model/ops.py:287-324 (FLA chunk_gated_delta_rule): the chunked form on the tensor
-    cores where it applies (question blocks), else the token recurrence."""
+    cores where it applies (question blocks), else the token recurrence. There is no inter-chunk form yet:
+    for the 4096-token state pass the recurrence is slower than FLA's chunked kernel (3.0 vs 0.65 ms per
+    layer on B200), so keep FLA for that call."""
+    return gated_delta_rule(q, k, v, g=g, beta=beta, initial_state=initial_state,
+                            output_final_state=output_final_state, use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel)
+
+
+def question_gated_delta_rule(q, k, v, *, g, beta, initial_state, output_final_state,
+                              use_qk_l2norm_in_kernel=True):
+    """For the question pass, with ``recurrent_gated_delta_rule``'s arguments (the call core.py:360-372
+    makes for blocks of <= 256 tokens): the chunked form on the tensor cores where it applies, else the
+    token recurrence."""
     return gated_delta_rule(q, k, v, g=g, beta=beta, initial_state=initial_state,
                             output_final_state=output_final_state, use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel)
