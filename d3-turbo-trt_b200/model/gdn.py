@@ -2,11 +2,12 @@
 ``ops.recurrent_gated_delta_rule`` and ``ops.chunk_gated_delta_rule``
 (d3trt/model/ops.py:287-360), which D3Core calls per GDN layer (core.py:348-372).
 
-Both names run ``d3b_gated_delta_rule`` (``csrc/gated_delta.cu``): ``recurrent_...`` the
+All names run ``d3b_gated_delta_rule`` (``csrc/gated_delta.cu``): ``recurrent_...`` the
 token-recurrent form with an fp32 state (the math of FLA's fused recurrent kernel, the
-reference's path for question blocks), ``chunk_...`` the chunked (WY) form on the tensor
-cores for blocks of <= 64 tokens sharing one initial state, falling back to the
-recurrence elsewhere. Differences from the reference's call, all optional for the caller:
+reference's path for question blocks); ``chunk_...`` and ``question_...`` the chunked (WY)
+form on the tensor cores for blocks of <= 64 tokens sharing one initial state, falling back
+to the recurrence elsewhere (for the 4096-token state pass that is slower than FLA's chunked
+kernel). Differences from the reference's call, all optional for the caller:
 
 * q/k may keep H < HV heads (value head hv reads q/k head hv // (HV // H)), so the
   ``repeat_interleave`` of core.py:345-347 can be dropped;
