@@ -174,3 +174,22 @@ def test_chunk_form_matches_fla_chunk():
     o, _ = gdn.gated_delta_rule(q.to(DEV), k.to(DEV), v.to(DEV), g=gl.to(DEV), beta=beta.to(DEV),
                                 initial_state=init, algo="chunk")
     assert float((o.float() - ref.float()).abs().max()) <= 2e-2
+
+
+def test_chunk_form_strong_decay_and_question_entry():
+    """Decays as strong as the model's (g down to -20 per token): no overflow, no NaN; and
+    question_gated_delta_rule (the question-pass entry) takes the chunked form."""
+    B, T, H, HV, K, V = 3, 48, 2, 4, 128, 128
+    q, k, v, _, beta, h0 = _inputs(B, T, H, HV, K, V, 30)
+    gl = -torch.rand(B, T, HV, generator=torch.Generator().manual_seed(31)) * 20.0
+    args = (q.to(DEV), k.to(DEV), v.to(DEV))
+    init = h0.to(DEV).expand(B, -1, -1, -1)
+    o, _ = gdn.question_gated_delta_rule(*args, g=gl.to(DEV), beta=beta.to(DEV), initial_state=init,
+                                         output_final_state=False)
+    assert torch.isfinite(o.float()).all()
+    oc, _ = gdn.gated_delta_rule(*args, g=gl.to(DEV), beta=beta.to(DEV), initial_state=init, algo="chunk")
+    assert torch.equal(o, oc)
+    ro, _ = oracle_gdr(q.float().numpy(), k.float().numpy(), v.float().numpy(), gl.numpy(), beta.float().numpy(),
+                       h0.numpy())
+    _close_chunk(o, ro)
+    assert _lib.device_error() == 0
