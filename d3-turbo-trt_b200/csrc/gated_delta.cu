@@ -24,6 +24,8 @@
 // multiply per token, and the output uses o = S'^T q + (k.q) v' (S' the decayed
 // state before the update), so each state element costs three FMAs per token,
 // issued as packed fp32x2 FMAs (two rows per instruction).
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace {
@@ -290,7 +292,8 @@ int launch_k(const GdrParams& p, int beta_dtype, long long blocks, cudaStream_t 
 //   R  = beta_i (v_i - e^gamma_i S0^T k_i)        (rows i)
 //   V' = (I + A)^-1 R                             (forward substitution)
 //   O  = e^gamma_i S0^T q_i + lower-incl( (q_i . k_j) e^(gamma_i - gamma_j) ) V'
-// One CTA = two blocks (M = 128 rows) and one value head; 256 threads. The four
+// One work item = two blocks (M = 128 rows) and one value head; a persistent CTA of
+// 256 threads per SM loops over work items (TMEM and barriers set up once). The four
 // products K K^T, K S0, Q K^T, Q S0 run on tcgen05 into TMEM (bf16 operands,
 // fp32 accumulate: 512 columns), the epilogue (two threads per row) forms A, R and
 // the decayed P = lower(Q K^T) as bf16, the solve runs with one thread per (state
@@ -386,12 +389,10 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5;
   const int row = tid & (M - 1), half = tid >> 7;  // row phases: one row, 64 of its 128 columns
-  const int hv = blockIdx.y, h = hv / (p.HV / p.H);
   const int blk = row >> 6, tl = row & 63;  // the row's token tl of block blk
-  const int b = blockIdx.x * 2 + blk;
-  const bool valid = b < p.B && tl < p.T;
   volatile int* abort_flag = &bars.abort_flag;
   const int c0 = half * 64;
+  const int npairs = (p.B + 1) / 2, n_items = npairs * p.HV;
 
   if (tid == 0) {
     d3b::mbar_init(&bars.load, THREADS);
@@ -401,6 +402,21 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
     bars.abort_flag = 0;
     d3b::fence_barrier_init();
   }
+  // persistent: TMEM and the barriers are set up once; each iteration is one work item
+  // (two blocks x one value head) and flips the barriers' phase
+  if (warp == 0) d3b::tmem_alloc(&bars.tmem_slot, TMEM_COLS);
+  d3b::tc_fence_before();
+  __syncthreads();
+  d3b::tc_fence_after();
+  const uint32_t tmem = bars.tmem_slot;
+  const uint32_t s_base = d3b::smem_u32(smem);
+  bool alive = true;
+#pragma unroll 1
+  for (int item = blockIdx.x, it = 0; item < n_items && alive; item += gridDim.x, ++it) {
+  const uint32_t ph = (uint32_t)it & 1u;
+  const int hv = item / npairs, h = hv / (p.HV / p.H);
+  const int b = (item % npairs) * 2 + blk;
+  const bool valid = b < p.B && tl < p.T;
   // ---- phase 1: q, k, v rows and the head's S0 tile arrive by bulk copies on one
   // mbarrier (one arrival per thread, each with the bytes it copies); g -> gamma, beta
   // raw rows: q and k at 256 B per row (read back with a row-rotated granule order, so
@@ -421,7 +437,8 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
       reinterpret_cast<uint4*>(stage_v + row * V_STAGE)[x] = make_uint4(0, 0, 0, 0);
     }
   }
-  __syncthreads();  // barrier init visible
+  __syncthreads();  // barrier init visible; the previous item's shared-memory users are done
+  d3b::fence_proxy_async_smem();  // generic writes of the previous item before this item's bulk copies
   if (half == 0 && valid) {
     d3b::mbar_arrive_expect_tx(&bars.load, 3 * 256);
     bulk_load(stage_q + row * 256, static_cast<const In*>(p.q) + b * p.qs[0] + (long long)tl * p.qs[1] + h * p.qs[2],
@@ -443,7 +460,7 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
                                                                        hv * p.bs[2]])
                            : 0.f;
   }
-  bool ok = d3b::warp_wait(&bars.load, 0, abort_flag, err, kSiteChunkLoad);
+  bool ok = d3b::warp_wait(&bars.load, ph, abort_flag, err, kSiteChunkLoad);
   uint4 rq[8], rk[8];  // rq[x] holds columns c0 + gx(x) * 8 .. + 7
   auto gx = [&](int x) { return (x + row) & 7; };
 #pragma unroll
@@ -490,12 +507,9 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
   __syncthreads();  // every thread has read the raw g values
   if (half == 0) bars.gam[row] = gam;
   d3b::fence_proxy_async_smem();
-  if (warp == 0) d3b::tmem_alloc(&bars.tmem_slot, TMEM_COLS);
   d3b::tc_fence_before();
   __syncthreads();
   d3b::tc_fence_after();
-  const uint32_t tmem = bars.tmem_slot;
-  const uint32_t s_base = d3b::smem_u32(smem);
 
   // ---- phase 2: K K^T, K S0, Q K^T, Q S0 -------------------------------------
   if (tid == 0 && ok) {
@@ -514,7 +528,7 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
     }
     d3b::mma_commit(&bars.mma1);
   }
-  if (ok) ok = d3b::warp_wait(&bars.mma1, 0, abort_flag, err, kSiteChunkMma1);
+  if (ok) ok = d3b::warp_wait(&bars.mma1, ph, abort_flag, err, kSiteChunkMma1);
   d3b::tc_fence_after();
 
   // ---- phase 3 (row, column half): A, P, R -------------------------------------
@@ -638,7 +652,7 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
     }
     d3b::mma_commit(&bars.mma2);
   }
-  if (ok) ok = d3b::warp_wait(&bars.mma2, 0, abort_flag, err, kSiteChunkMma2);
+  if (ok) ok = d3b::warp_wait(&bars.mma2, ph, abort_flag, err, kSiteChunkMma2);
   d3b::tc_fence_after();
 
   // ---- phase 6 (row, column half): O = e^gamma (Q S0) + P V' ------------------
@@ -663,6 +677,13 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
         }
       }
     }
+  }
+
+  // every thread's TMEM reads and shared-memory uses of this item are done before the
+  // next item's copies and products; a failed wait anywhere ends the loop for the CTA
+  d3b::tc_fence_before();
+  alive = __syncthreads_and(ok) != 0;
+  d3b::tc_fence_after();
   }
 
   // ---- teardown: every issued MMA has completed before TMEM is freed ---------
@@ -696,7 +717,8 @@ int launch_chunk(const GdrParams& p, int beta_dtype, uint8_t* s0_tiles, cudaStre
     if (const int st = d3b_host::check_launch()) return st;
   }
   const uint8_t* tiles = p.h0 ? s0_tiles : nullptr;
-  const dim3 grid((unsigned)((p.B + 1) / 2), (unsigned)p.HV);
+  const int n_items = ((p.B + 1) / 2) * p.HV;
+  const dim3 grid((unsigned)std::min(n_items, d3b_host::num_sms(dev)));  // persistent, one CTA per SM
   auto go = [&](auto kernel, int which) -> int {
     if (dev >= 0 && dev < 64 && !attr_set[dev][which]) {
       if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gdc::SMEM_BYTES) != cudaSuccess)
