@@ -315,6 +315,7 @@ constexpr int OFF_R = 0;            // aliases the K/Q/S0 tiles once their produ
 constexpr int OFF_A = 5 * TILE;
 constexpr int SMEM_BYTES = OFF_A + M * A_STRIDE * 4 + 1024;
 constexpr int V_STAGE = 272;        // staged v row stride (bytes): 128 rows fit the A region
+constexpr int O_STAGE = 272;        // staged output row stride (bytes)
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int COL_KK = 0, COL_KS = 128, COL_QK = 256, COL_QS = 384, COL_PV = 0;
 
@@ -656,9 +657,11 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
   d3b::tc_fence_after();
 
   // ---- phase 6 (row, column half): O = e^gamma (Q S0) + P V' ------------------
-  if (ok) {  // warp-uniform: every lane loads (tcgen05.ld is warp-collective), valid rows store
+  // Rows are gathered in shared memory (the dead K/Q/R space, 272 B per row so a warp's
+  // rows hit different banks) and leave with one 256-byte bulk copy each.
+  uint8_t* ostage = smem + OFF_KN;
+  if (ok) {  // warp-uniform: every lane loads (tcgen05.ld is warp-collective)
     const float eg = __expf(gam);
-    In* orow = static_cast<In*>(p.o) + b * p.os[0] + (long long)tl * p.os[1] + hv * p.os[2];
     uint32_t rs[32], rp[32];
 #pragma unroll 1
     for (int q2 = 0; q2 < 2; ++q2) {
@@ -666,17 +669,25 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
       d3b::tmem_ld32(lane_addr + COL_QS + j0, rs);
       d3b::tmem_ld32(lane_addr + COL_PV + j0, rp);
       d3b::tmem_wait_ld();
-      if (valid) {
 #pragma unroll
-        for (int x = 0; x < 32; x += 8) {
-          float f[8];
+      for (int x = 0; x < 32; x += 8) {
+        float f[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] = fmaf(eg, __uint_as_float(rs[x + e]), __uint_as_float(rp[x + e]));
-          reinterpret_cast<uint4*>(orow)[(j0 + x) / 8] = make_uint4(pack2<In>(f[0], f[1]), pack2<In>(f[2], f[3]),
-                                                                    pack2<In>(f[4], f[5]), pack2<In>(f[6], f[7]));
-        }
+        for (int e = 0; e < 8; ++e) f[e] = fmaf(eg, __uint_as_float(rs[x + e]), __uint_as_float(rp[x + e]));
+        *reinterpret_cast<uint4*>(ostage + row * O_STAGE + (j0 + x) * 2) =
+            make_uint4(pack2<In>(f[0], f[1]), pack2<In>(f[2], f[3]), pack2<In>(f[4], f[5]), pack2<In>(f[6], f[7]));
       }
     }
+  }
+  d3b::fence_proxy_async_smem();
+  __syncthreads();
+  if (ok && half == 0 && valid) {
+    In* orow = static_cast<In*>(p.o) + b * p.os[0] + (long long)tl * p.os[1] + hv * p.os[2];
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], 256;" ::"l"(orow),
+                 "r"(d3b::smem_u32(ostage + row * O_STAGE))
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // the staging rows may be reused
   }
 
   // every thread's TMEM reads and shared-memory uses of this item are done before the
@@ -686,7 +697,8 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
   d3b::tc_fence_after();
   }
 
-  // ---- teardown: every issued MMA has completed before TMEM is freed ---------
+  // ---- teardown: every issued MMA and output copy has completed ---------------
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   if (tid == 0) {
     d3b::mma_commit(&bars.drain);
     const uint32_t addr = d3b::smem_u32(&bars.drain);
