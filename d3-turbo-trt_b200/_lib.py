@@ -145,7 +145,12 @@ def require_cuda(t: torch.Tensor, what: str) -> None:
 
 def device_error(device: torch.device | int | None = None, reset: bool = True) -> int:
     """Device error word after synchronising the current stream (0 = none)."""
-    dev = torch.device("cuda", torch.cuda.current_device() if device is None else torch.device(device).index or 0)
+    if device is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    else:
+        dev = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        if dev.index is None:  # plain "cuda": the current device, as torch resolves it
+            dev = torch.device("cuda", torch.cuda.current_device())
     with torch.cuda.device(dev):
         s = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
         return int(lib().d3b_device_error(s, 1 if reset else 0))

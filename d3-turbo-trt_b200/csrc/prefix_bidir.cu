@@ -60,7 +60,8 @@ enum {
   kSiteSFull = 2006,
   kSitePFree = 2007,
   kSiteFinal = 2008,
-  kSiteDrain = 2009
+  kSiteDrain = 2009,
+  kSiteBadLength = 2010
 };
 
 template <int D, int BN>
@@ -106,6 +107,19 @@ struct Params {
   float scale_log2;
   int* err;
 };
+
+// Real tokens of question block b. The table lives in device memory, so the
+// host cannot check it: a value outside [0, L] is clamped (every access stays
+// inside the caller's [B, *, L, D] tensors) and reported through the device
+// error word (site kSiteBadLength), which voids the launch's results.
+__device__ __forceinline__ int block_length(const Params& p, int b) {
+  const int n = p.lengths[b];
+  if (n < 0 || n > p.L) {
+    d3b::record_device_error(p.err, kSiteBadLength);
+    return n < 0 ? 0 : p.L;
+  }
+  return n;
+}
 
 // Item i of the K/V stream -> (is_v, kv tile j) for n tiles:
 // K0, K1, V0, K2, V1, ..., K_{n-1}, V_{n-2}, V_{n-1}.
@@ -222,7 +236,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int G = p.G, T = p.T;
-  const int len_b = p.lengths[b];
+  const int len_b = block_length(p, b);
   const int rows_used = G * T;
   const int tok0 = tile * T;
 
@@ -617,7 +631,7 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
   const int tile = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int G = p.G, T = p.T;
   const int rows_used = G * T;
-  const int len_b = p.lengths[b];
+  const int len_b = block_length(p, b);
   const int tok0 = tile * T;
   if (tok0 >= len_b) {  // no real token in this tile: zero-fill and leave
     if (warp < 4) zero_tile_rows<D>(p, b, g, tok0, warp, lane);

@@ -32,6 +32,9 @@ from .. import _lib
 
 HEAD_DIMS = (32, 64, 128, 256)
 KERNEL_NAME = "sm100a"
+# Device error word set by the kernel when a device-resident lengths entry lies
+# outside [0, L] (the entry is clamped; read it with _lib.device_error()).
+SITE_BAD_LENGTH = 2010
 
 _LENGTHS: "OrderedDict[tuple, torch.Tensor]" = OrderedDict()
 _LENGTHS_MAX = 16
@@ -134,6 +137,11 @@ def prefix_bidir_attention(
     Inputs follow the model's natural layout: q/k_q/v_q are [B, H, L, D],
     k_state/v_state are [H_kv, S, D]. Returns [B, H, L, D]. ``out`` may be a
     preallocated [B, H, L, D] tensor (any strides, D contiguous).
+
+    ``lengths`` given as Python ints are checked here (``RuntimeError`` outside
+    [0, L]). A CUDA int32 tensor is passed to the kernel as it is, without a
+    device sync; the kernel clamps entries outside [0, L] and sets the device
+    error word to ``SITE_BAD_LENGTH``, which ``_lib.device_error()`` returns.
     """
     _check(q, k_q, v_q)
     if k_state.dtype != q.dtype or v_state.dtype != q.dtype:
@@ -154,11 +162,11 @@ def prefix_bidir_attention(
     else:
         lengths = [int(n) for n in lengths]
         n_rows = len(lengths)
-        if sum(lengths) == 0:
+        if lengths and (max(lengths) > width or min(lengths) < 0):
+            raise RuntimeError(f"lengths must lie in [0, {width}]")
+        if sum(lengths) == 0 and n_rows == rows:
             out.zero_()
             return out
-        if max(lengths) > width or min(lengths) < 0:
-            raise RuntimeError(f"lengths must lie in [0, {width}]")
     if n_rows != rows:
         raise RuntimeError(f"{n_rows} lengths for {rows} question blocks")
     if rows == 0 or width == 0:

@@ -32,7 +32,8 @@ def _workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
     calls that use it are ordered on the stream."""
     if nbytes == 0:
         return None
-    key = (device.index or 0, torch.cuda.current_stream(device).cuda_stream)
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    key = (index, torch.cuda.current_stream(index).cuda_stream)
     buf = _WORKSPACES.get(key)
     if buf is None or buf.numel() < nbytes:
         buf = torch.empty(nbytes, dtype=torch.uint8, device=device)

@@ -63,7 +63,7 @@ def test_ragged_golden(case):
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_cfg3a_shape_against_oracle(dtype):
     """BASELINE config 3a shapes: 4096-token state + 16 blocks x 64, H32/Hkv4/D128;
-    the oracle checks three blocks (one ragged)."""
+    the oracle checks every block (two ragged)."""
     g = torch.Generator().manual_seed(11)
     B, H, Hkv, L, D, S = 16, 32, 4, 64, 128, 4096
     q = _rand((B, L, H, D), g, dtype).permute(0, 2, 1, 3)  # model layout: [B, L, H, D] memory
@@ -76,10 +76,9 @@ def test_cfg3a_shape_against_oracle(dtype):
     lens[9] = 1
     out = pb.prefix_bidir_attention(q.to(DEV), ks.to(DEV), vs.to(DEV), kq.to(DEV), vq.to(DEV), lens, scale=D**-0.5)
     got = out.float().cpu()
-    for b in (0, 5, 9):
-        ref = oattn.questions(q[b : b + 1], ks, vs, kq[b : b + 1], vq[b : b + 1], [lens[b]], D**-0.5,
-                              dtype=torch.float32)
-        assert float((got[b : b + 1] - ref).abs().max()) <= TOL
+    ref = oattn.questions(q, ks, vs, kq, vq, lens, D**-0.5, dtype=torch.float32)
+    err = (got - ref).abs().amax(dim=(1, 2, 3))
+    assert float(err.max()) <= TOL, err
     assert torch.all(got[5, :, 37:] == 0) and torch.all(got[9, :, 1:] == 0)
 
 
@@ -137,3 +136,77 @@ def test_preallocated_strided_output_and_tensor_lengths():
     pb.prefix_bidir_attention(q, ks, vs, kq, vq, lens, scale=0.125, out=out)
     ref = oattn.questions(q.cpu(), ks.cpu(), vs.cpu(), kq.cpu(), vq.cpu(), [16, 3, 9], 0.125, dtype=torch.float32)
     assert float((out.float().cpu() - ref).abs().max()) <= TOL
+
+
+def _long_state_case(seed, B, L, S=16384, H=32, Hkv=4, D=128):
+    g = torch.Generator().manual_seed(seed)
+    q = _rand((B, L, H, D), g).permute(0, 2, 1, 3)
+    ks = _rand((S, Hkv, D), g).permute(1, 0, 2)
+    vs = _rand((S, Hkv, D), g).permute(1, 0, 2)
+    kq = _rand((B, L, Hkv, D), g).permute(0, 2, 1, 3)
+    vq = _rand((B, L, Hkv, D), g).permute(0, 2, 1, 3)
+    return q, ks, vs, kq, vq
+
+
+@pytest.mark.parametrize("name,B,L", [("cfg3b", 255, 48), ("cfg5", 255, 64)])
+def test_long_state_against_oracle(name, B, L):
+    """BASELINE configs 3b and 5: a 16384-token state and 255 question blocks
+    (48 or 64 tokens), H32/Hkv4/D128. Ten blocks are checked against the oracle:
+    the first, the last, three ragged ones and five spread over the batch."""
+    q, ks, vs, kq, vq = _long_state_case(21 if name == "cfg3b" else 22, B, L)
+    lens = [L] * B
+    lens[3], lens[130], lens[B - 2] = L - 1, 1, L // 2 + 3
+    out = pb.prefix_bidir_attention(q.to(DEV), ks.to(DEV), vs.to(DEV), kq.to(DEV), vq.to(DEV), lens, scale=128**-0.5)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    for b in (0, 3, 41, 97, 130, 166, 201, 229, B - 2, B - 1):
+        ref = oattn.questions(q[b : b + 1], ks, vs, kq[b : b + 1], vq[b : b + 1], [lens[b]], 128**-0.5,
+                              dtype=torch.float32)
+        got = out[b : b + 1].float().cpu()
+        assert float((got - ref).abs().max()) <= TOL, b
+        assert torch.all(got[0, :, lens[b]:] == 0)
+
+
+def test_head_dim_256_at_4k_state():
+    """The model's own attention shape (24 query heads, 4 KV heads, head_dim 256:
+    a GQA group of 6, which does not divide the 128-row tile) over a 4096-token
+    state, question pass and state pass, against the oracle."""
+    g = torch.Generator().manual_seed(23)
+    B, H, Hkv, L, D, S = 6, 24, 4, 48, 256, 4096
+    q = _rand((B, L, H, D), g).permute(0, 2, 1, 3)
+    ks = _rand((S, Hkv, D), g).permute(1, 0, 2)
+    vs = _rand((S, Hkv, D), g).permute(1, 0, 2)
+    kq = _rand((B, L, Hkv, D), g).permute(0, 2, 1, 3)
+    vq = _rand((B, L, Hkv, D), g).permute(0, 2, 1, 3)
+    lens = [48, 13, 48, 1, 47, 48]
+    out = pb.prefix_bidir_attention(q.to(DEV), ks.to(DEV), vs.to(DEV), kq.to(DEV), vq.to(DEV), lens, scale=D**-0.5)
+    ref = oattn.questions(q, ks, vs, kq, vq, lens, D**-0.5, dtype=torch.float32)
+    assert float((out.float().cpu() - ref).abs().max()) <= TOL
+    # state pass over the same 4096 tokens (S = 0 in the kernel): rows spread over the state
+    qs = _rand((1, S, H, D), g).permute(0, 2, 1, 3)
+    st = ops.flash_state(qs.to(DEV), ks[None].to(DEV), vs[None].to(DEV), scale=D**-0.5)
+    rows = torch.tensor([0, 1, 127, 128, 2049, 4094, 4095])
+    ref_s = oattn.state(qs[:, :, rows], ks[None], vs[None], D**-0.5, dtype=torch.float32)
+    assert float((st[:, :, rows.to(DEV)].float().cpu() - ref_s).abs().max()) <= TOL
+    assert _lib.device_error() == 0
+
+
+def test_device_lengths_out_of_range_are_reported():
+    """A device lengths table is read by the kernel itself: values outside
+    [0, L] are clamped (no access leaves the tensors) and reported through the
+    device error word, which the caller reads with d3b_device_error."""
+    g = torch.Generator().manual_seed(24)
+    B, H, Hkv, L, D, S = 4, 8, 2, 32, 128, 256
+    q = _rand((B, H, L, D), g).to(DEV)
+    ks, vs = _rand((Hkv, S, D), g).to(DEV), _rand((Hkv, S, D), g).to(DEV)
+    kq, vq = _rand((B, Hkv, L, D), g).to(DEV), _rand((B, Hkv, L, D), g).to(DEV)
+    assert _lib.device_error() == 0
+    good = torch.tensor([32, 5, 0, 17], dtype=torch.int32, device=DEV)
+    ref = pb.prefix_bidir_attention(q, ks, vs, kq, vq, good, scale=0.1)
+    assert _lib.device_error() == 0
+    bad = torch.tensor([1000, 5, -3, 17], dtype=torch.int32, device=DEV)
+    out = pb.prefix_bidir_attention(q, ks, vs, kq, vq, bad, scale=0.1)
+    assert _lib.device_error() == pb.SITE_BAD_LENGTH
+    assert _lib.device_error() == 0  # read-and-clear
+    # clamped to [0, L]: identical to the lengths 32 and 0
+    assert torch.equal(out, ref)

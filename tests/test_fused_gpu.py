@@ -113,3 +113,35 @@ def test_unsupported_shapes_raise():
         fused.add_rmsnorm(y, None, torch.ones(100), 1e-6)
     with pytest.raises(RuntimeError):
         fused.add_rmsnorm(x.float(), None, torch.ones(6152), 1e-6)
+
+
+def test_fused_producers_against_model_module_fixture():
+    """The fused kernels on the inputs of tests/golden/norm_quant.npz (recorded
+    from transformers' Qwen3_5RMSNorm, the eager gate and the reference's
+    quantize_rows): rows within one bf16 ulp of the modules, codes and scales
+    identical wherever the rows are identical."""
+    from conftest import bf16_from_bits, load_golden
+
+    g = load_golden("norm_quant.npz")
+    res, delta = bf16_from_bits(g["residual"]).to(DEV), bf16_from_bits(g["delta"]).to(DEV)
+    w1 = torch.from_numpy(1.0 + g["weight"])
+    for mode in ("fp8", "int8"):
+        hidden, q, s = fused.add_rmsnorm_quant(res, delta, w1, float(g["eps"]), mode)
+        _, normed = fused.add_rmsnorm(res, delta, w1, float(g["eps"]))
+        assert torch.equal(hidden.cpu(), bf16_from_bits(g["hidden"]))
+        want = bf16_from_bits(g["normed"])
+        ulps = (normed.cpu().view(torch.int16).int() - want.view(torch.int16).int()).abs()
+        assert int(ulps.max()) <= 1
+        same = (normed.cpu() == want).all(dim=1).numpy()
+        assert same.mean() > 0.5
+        assert np.array_equal(s.cpu().numpy().reshape(-1)[same], g[f"normed_s_{mode}"].reshape(-1)[same])
+        assert np.array_equal(_codes(q)[same], g[f"normed_q_{mode}"].view(np.uint8)[same])
+        attn, gate = bf16_from_bits(g["attn"]).to(DEV), bf16_from_bits(g["gate"]).to(DEV)
+        qg, sg = fused.sigmoid_gate_quant(attn, gate, mode)
+        gated = fused.sigmoid_gate(attn, gate).reshape(16, 256)
+        want = bf16_from_bits(g["gated"])
+        ulps = (gated.cpu().view(torch.int16).int() - want.view(torch.int16).int()).abs()
+        assert int(ulps.max()) <= 1
+        same = (gated.cpu() == want).all(dim=1).numpy()
+        assert np.array_equal(sg.cpu().numpy().reshape(-1)[same], g[f"gated_s_{mode}"].reshape(-1)[same])
+        assert np.array_equal(_codes(qg)[same], g[f"gated_q_{mode}"].view(np.uint8)[same])

@@ -1,12 +1,15 @@
-"""CPU checks of the fused-producer oracle (oracle/norm_quant.py) against an
-independent torch formulation of the eager model ops: Qwen3_5RMSNorm after a
-bf16 residual add (modeling_qwen3_5.py:711-725) and attn * sigmoid(gate)."""
+"""CPU checks of the fused-producer oracle (oracle/norm_quant.py): against an
+independent torch formulation of the eager model ops (Qwen3_5RMSNorm after a
+bf16 residual add, modeling_qwen3_5.py:711-725, and attn * sigmoid(gate)), and
+against the fixture recorded from the modules themselves and the reference's
+quantize_rows (tests/golden/norm_quant.npz)."""
 
 from __future__ import annotations
 
 import numpy as np
 import torch
 
+from conftest import load_golden
 from oracle import norm_quant as onq
 from oracle import quant as oq
 
@@ -53,3 +56,31 @@ def test_sigmoid_gate_oracle_matches_eager_formula():
     want = (a * torch.sigmoid(gt)).reshape(10, 256).float().numpy()
     d = _ulp_diff_bf16(got, want)
     assert d.max() <= 1 and (d == 0).mean() > 0.99  # exp implementations may differ in the last fp32 bit
+
+
+def _bf16(bits: np.ndarray) -> np.ndarray:
+    return (np.ascontiguousarray(bits).astype(np.uint32) << 16).view(np.float32)
+
+
+def test_oracle_pinned_to_model_modules():
+    """tests/golden/norm_quant.npz was recorded from transformers' Qwen3_5RMSNorm
+    after a bf16 residual add, the eager ``out * sigmoid(gate)`` and the
+    reference's own quantize_rows (tests/golden/make_norm_golden.py)."""
+    g = load_golden("norm_quant.npz")
+    res, delta = _bf16(g["residual"]), _bf16(g["delta"])
+    hidden, normed = onq.add_rmsnorm(res, delta, 1.0 + g["weight"], float(g["eps"]))
+    assert np.array_equal(hidden, _bf16(g["hidden"]))
+    d = _ulp_diff_bf16(normed, _bf16(g["normed"]))
+    # the module's mean is an fp32 sum in its own order; the oracle's is exact
+    assert d.max() <= 1 and (d == 0).mean() > 0.99
+    gated = onq.sigmoid_gate(_bf16(g["attn"]), _bf16(g["gate"]))
+    d = _ulp_diff_bf16(gated, _bf16(g["gated"]))
+    assert d.max() <= 1 and (d == 0).mean() > 0.99
+    # codes: identical wherever the rows themselves are identical
+    for mode in ("fp8", "int8"):
+        for name, rows in (("normed", normed), ("gated", gated)):
+            q, s = onq.quantize_rows(rows, mode)
+            same = np.all(rows == _bf16(g[name]), axis=1)
+            assert same.mean() > 0.5
+            assert np.array_equal(s[same], g[f"{name}_s_{mode}"][same])
+            assert np.array_equal(q.view(np.uint8)[same], g[f"{name}_q_{mode}"].view(np.uint8)[same])

@@ -196,6 +196,9 @@ def test_cfg2_full_size(mode):
         qa_np, qw_np = qa_np.view(np.int8), qw_np.view(np.int8)
         acc = quant.scaled_mm(qa, layer.weight, None, None, out_dtype=torch.int32)
         assert np.array_equal(acc[rows.to(DEV)].cpu().numpy(), oq.int_gemm(qa_np, qw_np))
+        # the whole [4096, 13824] int32 accumulator, bit for bit, against torch._int_mm
+        # (exact integer arithmetic, the reference's own INT8 call: quant.py:190-197)
+        assert torch.equal(acc, torch._int_mm(qa, layer.weight.t()))
     y32 = quant.scaled_mm(qa, layer.weight, sa, layer.weight_scale, out_dtype=torch.float32)
     ref = oq.w8a8_linear(qa_np, sa[rows.to(DEV)].cpu().numpy(), qw_np, layer.weight_scale.cpu().numpy(), mode)
     got = y32[rows.to(DEV)].cpu().numpy()
