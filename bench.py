@@ -388,7 +388,9 @@ def main():
     extra = {}
     if not args.no_extra:
         extra = secondary(dev, stream, flush, peaks, quant, pb, d3b)
-        extra["cfg5_strong_scaling"] = cfg5_strong(dev, stream, flush, peaks, pb, d3dist, rank, world)
+    # config 5 at every N: the request split over the ranks (strong) and 64 independent requests
+    cfg5 = cfg5_strong(dev, stream, flush, peaks, pb, d3dist, rank, world)
+    cfg5_dp = dp_requests(dev, stream, flush, pb, rank, world)
     if world > 1:
         dist.barrier()
 
@@ -420,6 +422,8 @@ def main():
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
             "state_kv_broadcast_ms": bcast_ms,
+            "cfg5_strong_scaling": cfg5,
+            "cfg5_dp_requests": cfg5_dp,
             "extra": extra,
         }
         print(json.dumps(line), flush=True)
@@ -428,55 +432,152 @@ def main():
         dist.destroy_process_group()
 
 
-def cfg5_strong(dev, stream, flush, peaks, pb, d3dist, rank, world):
-    """Config 5: one request, 255 question blocks of 64 over a 16384-token
-    state, split over the ranks (contiguous, length-sorted shards; sizes differ by <= 1).
-    Rank 0 builds the state K/V and broadcasts it (32 MiB, timed on its own); each rank
-    then runs its shard; the pass time is the max over ranks (strong scaling)."""
+def cfg5_strong(dev, stream, flush, peaks, pb, d3dist, rank, world, layers=4):
+    """Config 5, one request split over the ranks: 255 question blocks of 64 tokens over a
+    16384-token state, H32/Hkv4/D128, through `layers` full-attention layers (the reference
+    runs the state once, then the question blocks, layer by layer: d3trt/model/core.py:146-181).
+
+    Rank 0 runs every layer's state pass (dense attention over the 16384 state tokens) and
+    posts that layer's K/V broadcast (one 32 MiB buffer) right behind it, so layer l crosses
+    NVLink while layer l+1's state pass runs. Every rank then runs its contiguous,
+    length-sorted shard of the blocks through the layers, each layer once its K/V has landed
+    (rank 0 holds them already). Device-timed from a common start (barrier), max over ranks:
+    the state pass on rank 0, the broadcast still in flight when it ends, and the question
+    phase after it. blocks/s = 255 / (question phase), the phase counted from the end of
+    the state pass to the last rank's last question pass (so an exposed broadcast counts)."""
     import torch.distributed as dist
 
     cfg = CFG5
-    S, Hkv, D, L = cfg["S"], cfg["Hkv"], cfg["D"], cfg["L"]
-    g = torch.Generator().manual_seed(55)
-    ks = torch.empty(S, Hkv, D, dtype=torch.bfloat16, device=dev)
-    vs = torch.empty_like(ks)
+    S, H, Hkv, D, L, nb = cfg["S"], cfg["H"], cfg["Hkv"], cfg["D"], cfg["L"], cfg["B"]
+    ex = d3dist.StateKVExchange(layers, S, Hkv, D, dtype=torch.bfloat16, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(55)
     if rank == 0:
-        ks.copy_(torch.randn(S, Hkv, D, generator=g).to(torch.bfloat16))
-        vs.copy_(torch.randn(S, Hkv, D, generator=g).to(torch.bfloat16))
-    bcast_ms = None
+        ex.buffers.normal_(generator=gen)
+        q_state = torch.randn(1, S, H, D, generator=gen, device=dev, dtype=torch.bfloat16).permute(0, 2, 1, 3)
+        st_out = torch.empty(1, H, S, D, dtype=torch.bfloat16, device=dev)
+    else:
+        ex.buffers.zero_()
+    lengths = [L] * nb
+    order = d3dist.length_order(lengths)
+    lo, hi = d3dist.shard_bounds(nb, world, rank)
+    mine = [order[i] for i in range(lo, hi)]
+    q = torch.randn(len(mine), L, H, D, generator=gen, device=dev, dtype=torch.bfloat16).permute(0, 2, 1, 3)
+    kq = torch.randn(len(mine), L, Hkv, D, generator=gen, device=dev, dtype=torch.bfloat16).permute(0, 2, 1, 3)
+    vq = torch.randn(len(mine), L, Hkv, D, generator=gen, device=dev, dtype=torch.bfloat16).permute(0, 2, 1, 3)
+    out = torch.empty(len(mine), H, L, D, dtype=torch.bfloat16, device=dev)
+    lens = [lengths[i] for i in mine]
+
+    def request():
+        ev = {k: torch.cuda.Event(enable_timing=True) for k in ("start", "state", "last_kv", "end")}
+        flush()
+        if world > 1:
+            dist.barrier()
+        ev["start"].record(stream)
+        for layer in range(layers):
+            if rank == 0:
+                k, v = ex.kv(layer)
+                pb.state_attention(q_state, k[None], v[None], scale=D ** -0.5, out=st_out)
+            ex.post(layer)
+        ev["state"].record(stream)
+        for layer in range(layers):
+            if rank != 0:
+                ex.wait(layer)
+            if layer == layers - 1:
+                ev["last_kv"].record(stream)
+            k, v = ex.kv(layer)
+            pb.prefix_bidir_attention(q, k, v, kq, vq, lens, scale=D ** -0.5, out=out)
+        ev["end"].record(stream)
+        if rank == 0:
+            for layer in range(layers):
+                ex.wait(layer)
+        torch.cuda.synchronize()
+        return {k: ev["start"].elapsed_time(e) for k, e in ev.items() if k != "start"}
+
+    for _ in range(2):
+        request()
+    runs = [request() for _ in range(5)]
+    state_ms = statistics.median(r["state"] for r in runs)  # rank 0's is the one that counts
+    end_ms = statistics.median(r["end"] for r in runs)
+    kv_ms = statistics.median(r["last_kv"] for r in runs)
+    t = torch.tensor([state_ms if rank == 0 else 0.0, end_ms, kv_ms if rank != 0 else 0.0], device=dev)
     if world > 1:
-        d3dist.broadcast_state_kv([(ks, vs)], src=0)  # warm
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    state_ms, end_ms, kv_ms = (float(x) for x in t.tolist())
+    question_ms = end_ms - state_ms
+    bcast_exposed = max(0.0, kv_ms - state_ms) if world > 1 else 0.0
+    # the 32 MiB layer broadcast on its own, for reference (all ranks, same order)
+    bcast_alone = None
+    if world > 1:
+        ex.post(0)
+        ex.wait(0)
         torch.cuda.synchronize()
         dist.barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        d3dist.broadcast_state_kv([(ks, vs)], src=0)
+        ex.post(0)
+        ex.wait(0)
         b.record(stream)
         torch.cuda.synchronize()
-        t = torch.tensor([a.elapsed_time(b)], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        bcast_ms = float(t.item())
-    lengths = [L] * cfg["B"]
-    order = d3dist.length_order(lengths)
-    lo, hi = d3dist.shard_bounds(cfg["B"], world, rank)
-    mine = [order[i] for i in range(lo, hi)]
-    nb = len(mine)
-    q = torch.randn(nb, L, cfg["H"], D, generator=g).to(torch.bfloat16).to(dev).permute(0, 2, 1, 3)
-    kq = torch.randn(nb, L, Hkv, D, generator=g).to(torch.bfloat16).to(dev).permute(0, 2, 1, 3)
-    vq = torch.randn(nb, L, Hkv, D, generator=g).to(torch.bfloat16).to(dev).permute(0, 2, 1, 3)
-    lens = [lengths[i] for i in mine]
-    ksv, vsv = ks.permute(1, 0, 2), vs.permute(1, 0, 2)
-    fn = lambda: pb.prefix_bidir_attention(q, ksv, vsv, kq, vq, lens, scale=D ** -0.5)
-    t_ms = statistics.median(time_steps(fn, 5, 3, stream, flush))
+        bt = torch.tensor([a.elapsed_time(b)], device=dev)
+        dist.all_reduce(bt, op=dist.ReduceOp.MAX)
+        bcast_alone = float(bt.item())
+    fl = attn_flops(**cfg) * layers
+    return {"workload": f"{nb} blocks x {L} tokens over a {S}-token state, H{H}/Hkv{Hkv}/D{D} bf16, "
+                        f"{layers} full-attention layers, blocks split over {world} rank(s)",
+            "value": nb / (question_ms / 1e3), "unit": "question-blocks/s (per request, all layers)",
+            "question_phase_ms": question_ms, "state_pass_ms_rank0": state_ms,
+            "broadcast_exposed_ms": bcast_exposed, "broadcast_32MiB_alone_ms": bcast_alone,
+            "broadcast_gbs_alone": (2 * S * Hkv * D * 2) / bcast_alone / 1e6 if bcast_alone else None,
+            "question_tflops_total": fl / question_ms / 1e9, "blocks_per_rank": len(mine),
+            "timing": "device events from a common barrier, median of 5 requests, max over ranks; "
+                      "L2 flushed before each request", "scaling": "strong"}
+
+
+def dp_requests(dev, stream, flush, pb, rank, world, n_req=64):
+    """Config 5's independent requests spread data-parallel: 64 requests, each one
+    full-attention layer's state pass over 16384 tokens and its 255 x 64-token question
+    pass, ceil/floor(64 / N) per rank, no communication. Device-timed, max over ranks."""
+    import torch.distributed as dist
+
+    cfg = CFG5
+    S, H, Hkv, D, L, nb = cfg["S"], cfg["H"], cfg["Hkv"], cfg["D"], cfg["L"], cfg["B"]
+    lo, hi = (rank * n_req) // world, ((rank + 1) * n_req) // world
+    gen = torch.Generator(device=dev).manual_seed(77 + rank)
+    kv = torch.randn(2, S, Hkv, D, generator=gen, device=dev, dtype=torch.bfloat16)
+    ks, vs = kv[0].permute(1, 0, 2), kv[1].permute(1, 0, 2)
+    q_state = torch.randn(1, S, H, D, generator=gen, device=dev, dtype=torch.bfloat16).permute(0, 2, 1, 3)
+    st_out = torch.empty(1, H, S, D, dtype=torch.bfloat16, device=dev)
+    q = torch.randn(nb, L, H, D, generator=gen, device=dev, dtype=torch.bfloat16).permute(0, 2, 1, 3)
+    kq = torch.randn(nb, L, Hkv, D, generator=gen, device=dev, dtype=torch.bfloat16).permute(0, 2, 1, 3)
+    vq = torch.randn(nb, L, Hkv, D, generator=gen, device=dev, dtype=torch.bfloat16).permute(0, 2, 1, 3)
+    out = torch.empty(nb, H, L, D, dtype=torch.bfloat16, device=dev)
+    lens = [L] * nb
+
+    def one():
+        flush()
+        pb.state_attention(q_state, ks[None], vs[None], scale=D ** -0.5, out=st_out)
+        pb.prefix_bidir_attention(q, ks, vs, kq, vq, lens, scale=D ** -0.5, out=out)
+
+    one()
+    torch.cuda.synchronize()
     if world > 1:
-        t = torch.tensor([t_ms], device=dev)
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(hi - lo):
+        one()
+    b.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b)], device=dev)
+    if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_ms = float(t.item())
-    fl = attn_flops(**cfg)
-    return {"workload": "255 blocks x 64 tokens over a 16384-token state, H32/Hkv4/D128 bf16, split over ranks",
-            "question_pass_ms": t_ms, "blocks_per_s": cfg["B"] / (t_ms / 1e3),
-            "tflops_total": fl / t_ms / 1e9, "state_kv_broadcast_ms": bcast_ms, "state_kv_bytes": 2 * ks.numel() * 2,
-            "timing": "device, max over ranks, L2 flushed before each pass", "scaling": "strong"}
+    ms = float(t.item())
+    return {"workload": f"{n_req} independent requests, each a {S}-token state pass and {nb} x {L}-token "
+                        f"question pass (one full-attention layer, H{H}/Hkv{Hkv}/D{D} bf16), spread over "
+                        f"{world} rank(s), no communication",
+            "value": n_req / (ms / 1e3), "unit": "requests/s", "ms": ms,
+            "requests_per_rank_max": -(-n_req // world), "scaling": "strong",
+            "timing": "device events, max over ranks, L2 flushed before each request"}
 
 
 def secondary(dev, stream, flush, peaks, quant, pb, d3b):

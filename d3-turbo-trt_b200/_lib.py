@@ -59,6 +59,13 @@ SIGNATURES: list[tuple[str, Any, list[Any]]] = [
         _I,
         [_VP, _I64P, _VP, _VP, _I64P, _VP, _VP, _I64P, _VP, _I, _I, _I, _I, _I, _I, _I, _F, _VP, _I64P, _VP],
     ),
+    (
+        "d3b_prefix_bidir_ws",
+        _I,
+        [_VP, _I64P, _VP, _VP, _I64P, _VP, _VP, _I64P, _VP, _I, _I, _I, _I, _I, _I, _I, _F, _VP, _I64P, _VP, _SZ,
+         _VP],
+    ),
+    ("d3b_prefix_bidir_workspace_size", _SZ, [_I, _I, _I, _I, _I, _I]),
     ("d3b_readout_workspace_size", _SZ, [_I, _I]),
     ("d3b_readout", _I, [_VP, _I, _VP, _VP, _F, _VP, _I, _I, _I, _VP, _SZ, _VP]),
     ("d3b_readout_noalloc", _I, [_VP, _I, _VP, _VP, _F, _VP, _I, _I, _I, _VP]),
@@ -143,8 +150,22 @@ def require_cuda(t: torch.Tensor, what: str) -> None:
     lib()
 
 
+_ERROR_RESET_HOOKS: list = []
+
+
+def on_device_error(hook) -> None:
+    """Register ``hook(device_index)``, called when ``device_error`` reads a
+    non-zero word with ``reset``: state that a launch which gave up may have
+    left behind (a workspace's counters) is restored there."""
+    _ERROR_RESET_HOOKS.append(hook)
+
+
 def device_error(device: torch.device | int | None = None, reset: bool = True) -> int:
-    """Device error word after synchronising the current stream (0 = none)."""
+    """Device error word after synchronising the current stream (0 = none).
+
+    The word is sticky: once a device-side wait has given up, later launches
+    stop early and their outputs are undefined until it is read with
+    ``reset``; check it after a pass (or a batch of passes)."""
     if device is None:
         dev = torch.device("cuda", torch.cuda.current_device())
     else:
@@ -153,4 +174,8 @@ def device_error(device: torch.device | int | None = None, reset: bool = True) -
             dev = torch.device("cuda", torch.cuda.current_device())
     with torch.cuda.device(dev):
         s = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
-        return int(lib().d3b_device_error(s, 1 if reset else 0))
+        word = int(lib().d3b_device_error(s, 1 if reset else 0))
+        if word and reset:
+            for hook in _ERROR_RESET_HOOKS:
+                hook(dev.index)
+        return word

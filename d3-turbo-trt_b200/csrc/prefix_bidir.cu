@@ -42,6 +42,13 @@
 // TMEM (512 columns): O [0,D) | S0 | S1 (BN each) | P0 | P1 (BN/2 each).
 #include "common.cuh"
 
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <queue>
+#include <tuple>
+#include <vector>
+
 namespace {
 
 constexpr int BM = 128;
@@ -106,6 +113,15 @@ struct Params {
   int H, Hkv, G, T, S, L;
   float scale_log2;
   int* err;
+  // Launch plan of the D <= 128 kernel (1-D grid). Unit u = (b * Hkv + g) *
+  // tiles + tile has n_full key-tile iterations (state tiles, then
+  // ceil(L / BN) own tiles). CTA u < whole_units runs unit u whole. The last
+  // split_units units run as `pieces` CTAs each: CTA whole_units + k *
+  // split_units + r is piece k of unit whole_units + r, iterations
+  // [0, piece0) for k = 0, then consecutive runs of piece_rest.
+  int tiles, n_full, whole_units, split_units, pieces, piece0, piece_rest;
+  float* part;  // split pieces' partial results, one slot per piece CTA
+  int* count;   // per split unit: iterations accounted for (zero between launches)
 };
 
 // Real tokens of question block b. The table lives in device memory, so the
@@ -584,6 +600,7 @@ struct __align__(8) BarsDual {
   uint64_t drain_qk, drain_pv;
   uint32_t tmem_slot;
   int abort_flag;
+  int last_arrival;  // split unit: this CTA's piece completed the unit
 };
 
 enum {
@@ -615,7 +632,98 @@ __device__ __forceinline__ void scale_cols(uint32_t addr, float f) {
   }
 }
 
+// Partial result of one piece of a split unit (fp32): O as [D/4][128 rows]
+// float4 (a warp's 32 rows form one coalesced 512-byte run), then the row's
+// reference max (log2 units, scale applied) m[128] and row sum l[128].
+template <int D>
+struct PartSlot {
+  static constexpr int FLOATS = BM * D + 2 * BM;
+};
+
+// This CTA's unit and iteration range [a, e) in a launch with split units
+// (1-D grid); slot >= 0 for a piece of a split unit.
+__device__ __forceinline__ void cta_work(const Params& p, int& u, int& a, int& e, int& slot) {
+  const int bid = blockIdx.x;
+  if (bid < p.whole_units) {
+    u = bid;
+    a = 0;
+    e = p.n_full;
+    slot = -1;
+    return;
+  }
+  const int q = bid - p.whole_units, k = q / p.split_units, r = q % p.split_units;
+  u = p.whole_units + r;
+  slot = q;
+  a = k == 0 ? 0 : p.piece0 + (k - 1) * p.piece_rest;
+  e = k == 0 ? p.piece0 : min(p.n_full, a + p.piece_rest);
+}
+
+// Adds this piece's iterations to its unit's count; true for the piece that
+// completes the unit (which then merges every piece and resets the count).
+__device__ __forceinline__ bool count_piece(const Params& p, int r, int add) {
+  __threadfence();  // the CTA's partial rows (ordered before by a CTA barrier) before the count
+  const int before = atomicAdd(&p.count[r], add);
+  const bool last = before + add == p.n_full;
+  if (last) {
+    p.count[r] = 0;  // ready for the next launch
+    __threadfence();
+  }
+  return last;
+}
+
+// Merge the pieces of split unit r for one row half (wg: columns [wg*D/2,
+// (wg+1)*D/2)) and store it: O = sum_k 2^(m_k - m) O_k, l = sum_k 2^(m_k - m) l_k
+// over the pieces with l_k > 0, output O / l (zero for padding rows).
 template <int D, int FP16>
+__device__ void merge_unit(const Params& p, int r, int b, int g, int tok0, int len_b, int wg, int row) {
+  constexpr int OH = D / 2;
+  const int tok = tok0 + row / p.G, h = row % p.G;
+  if (!(row < p.G * p.T && tok < p.L)) return;
+  const bool real = tok < len_b;
+  float mx = -INFINITY;
+  for (int k = 0; k < p.pieces; ++k) {
+    const float* ps = p.part + (int64_t)(k * p.split_units + r) * PartSlot<D>::FLOATS;
+    if (__ldcg(ps + BM * D + BM + row) > 0.f) mx = fmaxf(mx, __ldcg(ps + BM * D + row));
+  }
+  float acc[OH];
+#pragma unroll
+  for (int c = 0; c < OH; ++c) acc[c] = 0.f;
+  float lt = 0.f;
+  for (int k = 0; k < p.pieces; ++k) {
+    const float* ps = p.part + (int64_t)(k * p.split_units + r) * PartSlot<D>::FLOATS;
+    const float ls = __ldcg(ps + BM * D + BM + row);
+    if (!(ls > 0.f)) continue;
+    const float w = d3b::ex2_approx(__ldcg(ps + BM * D + row) - mx);
+    lt += ls * w;
+    const float4* os = reinterpret_cast<const float4*>(ps);
+#pragma unroll
+    for (int c = 0; c < OH; c += 4) {
+      const float4 v = __ldcg(os + (wg * OH + c) / 4 * BM + row);
+      acc[c] += v.x * w;
+      acc[c + 1] += v.y * w;
+      acc[c + 2] += v.z * w;
+      acc[c + 3] += v.w * w;
+    }
+  }
+  const float inv_l = 1.f / lt;
+  uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + (int64_t)b * p.out_sb +
+                                        (int64_t)(g * p.G + h) * p.out_sh + (int64_t)tok * p.out_sl + wg * OH);
+#pragma unroll
+  for (int c = 0; c < OH; c += 8) {
+    uint4 v;
+    v.x = real ? pack2<FP16>(acc[c] * inv_l, acc[c + 1] * inv_l) : 0u;
+    v.y = real ? pack2<FP16>(acc[c + 2] * inv_l, acc[c + 3] * inv_l) : 0u;
+    v.z = real ? pack2<FP16>(acc[c + 4] * inv_l, acc[c + 5] * inv_l) : 0u;
+    v.w = real ? pack2<FP16>(acc[c + 6] * inv_l, acc[c + 7] * inv_l) : 0u;
+    dst[c / 8] = v;
+  }
+}
+
+// SPLIT: the launch has split units (1-D grid, pieces, partial merge). The
+// instantiation without it is one CTA per unit on the (tiles, Hkv, B) grid,
+// with none of the split code in it (measured 2-3 % faster than one kernel
+// carrying both paths).
+template <int D, int FP16, bool SPLIT>
 __global__ void __launch_bounds__(DU_THREADS, 1)
     prefix_bidir_dual_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapKs,
                              const __grid_constant__ CUtensorMap mapVs, const __grid_constant__ CUtensorMap mapKq,
@@ -627,14 +735,24 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
   __shared__ float mref_s[2][BM];   // reference max of the last tile of each group, per row
   __shared__ float lsum_s[2][BM];   // epilogue exchange: running sums and their references
   __shared__ float mlast_s[2][BM];
+  __shared__ int work_s[4];  // unit, end of range, slot, start of range: reloaded where used, not kept in registers
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  int unit, a, e, slot;
+  if constexpr (SPLIT) {
+    cta_work(p, unit, a, e, slot);
+  } else {
+    unit = ((int)blockIdx.z * p.Hkv + (int)blockIdx.y) * p.tiles + (int)blockIdx.x;
+    a = 0;
+    e = p.n_full;
+    slot = -1;
+  }
+  const int tile = unit % p.tiles, g = (unit / p.tiles) % p.Hkv, b = unit / (p.tiles * p.Hkv);
   const int G = p.G, T = p.T;
   const int rows_used = G * T;
   const int len_b = block_length(p, b);
   const int tok0 = tile * T;
-  if (tok0 >= len_b) {  // no real token in this tile: zero-fill and leave
-    if (warp < 4) zero_tile_rows<D>(p, b, g, tok0, warp, lane);
+  if (tok0 >= len_b) {  // no real token in this tile: zero-fill (once per unit) and leave
+    if (warp < 4 && a == 0) zero_tile_rows<D>(p, b, g, tok0, warp, lane);
     return;
   }
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -643,9 +761,31 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
   uint8_t* sV = sK + C::NK * C::SLOT_BYTES;
   volatile int* abort_flag = &bars.abort_flag;
   const int n_s = (p.S + BN - 1) / BN;
-  const int n = n_s + (len_b + BN - 1) / BN;
+  // this CTA's key tiles: kt = a + j for j in [0, n); own tiles past the block's length are skipped
+  const int n = max(0, min(e, n_s + (len_b + BN - 1) / BN) - a);
+  if (SPLIT && n == 0) {
+    // A piece of a split unit with no real key tile: an empty partial (l = 0),
+    // counted in like any other piece.
+    if (threadIdx.x < BM) {
+      float* ps = p.part + (int64_t)slot * PartSlot<D>::FLOATS;
+      ps[BM * D + threadIdx.x] = -INFINITY;
+      ps[BM * D + BM + threadIdx.x] = 0.f;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) bars.last_arrival = count_piece(p, unit - p.whole_units, e - a);
+    __syncthreads();
+    if (bars.last_arrival && threadIdx.x < 2 * BM) {
+      __threadfence();
+      merge_unit<D, FP16>(p, unit - p.whole_units, b, g, tok0, len_b, threadIdx.x / BM, threadIdx.x % BM);
+    }
+    return;
+  }
 
   if (threadIdx.x == 0) {
+    work_s[0] = unit;
+    work_s[1] = e;
+    work_s[2] = slot;
+    work_s[3] = a;
     d3b::mbar_init(&bars.q_full, 1);
     for (int i = 0; i < 8; ++i) {
       d3b::mbar_init(&bars.k_full[i], 1);
@@ -718,14 +858,15 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
         uint64_t* full = &fulls[slot];
         uint8_t* dst = ring + slot * C::SLOT_BYTES;
         d3b::mbar_arrive_expect_tx(full, C::SLOT_BYTES);
-        if (j < n_s) {
+        const int kt = a + j;  // key tile of the unit
+        if (kt < n_s) {
 #pragma unroll
           for (int c = 0; c < C::NCH; ++c)
-            d3b::tma_load_3d(dst + c * C::SLOT_CHUNK, m_state, full, c * C::CH, j * BN, g);
+            d3b::tma_load_3d(dst + c * C::SLOT_CHUNK, m_state, full, c * C::CH, kt * BN, g);
         } else {
 #pragma unroll
           for (int c = 0; c < C::NCH; ++c)
-            d3b::tma_load_4d(dst + c * C::SLOT_CHUNK, m_own, full, c * C::CH, (j - n_s) * BN, g, b);
+            d3b::tma_load_4d(dst + c * C::SLOT_CHUNK, m_own, full, c * C::CH, (kt - n_s) * BN, g, b);
         }
         if (++slot == nslot) { slot = 0; ph ^= 1; }
       }
@@ -828,7 +969,8 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
       d3b::tmem_wait_ld();
       d3b::tc_fence_before();
       d3b::mbar_arrive(&bars.s_free[wg]);
-      const int valid = j < n_s ? p.S - j * BN : len_b - (j - n_s) * BN;
+      const int kt = SPLIT ? reinterpret_cast<volatile int*>(work_s)[3] + j : j;  // key tile of the unit
+      const int valid = kt < n_s ? p.S - kt * BN : len_b - (kt - n_s) * BN;
       if (valid < BN) {
 #pragma unroll
         for (int c = 0; c < BN; ++c)
@@ -891,16 +1033,31 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
       const bool in_tensor = r < rows_used && tok < p.L;
       const bool real = tok < len_b;
       const float inv_l = 1.f / l;
-      // each group normalises and stores half of the D columns
+      // each group normalises and stores half of the D columns (a piece of a
+      // split unit writes its raw half of O, with m and l, to its slot instead)
       uint16_t* dst_row = static_cast<uint16_t*>(p.out) + (int64_t)b * p.out_sb + (int64_t)(g * G + h) * p.out_sh +
                           (int64_t)tok * p.out_sl + wg * C::OH;
+      float* ps = nullptr;
+      if constexpr (SPLIT) {
+        const int slot_e = reinterpret_cast<volatile int*>(work_s)[2];
+        if (slot_e >= 0) ps = p.part + (int64_t)slot_e * PartSlot<D>::FLOATS;
+      }
+      if (ps && wg == 0) {
+        ps[BM * D + r] = m_fin;
+        ps[BM * D + BM + r] = l;
+      }
       if constexpr (C::OH % 32 == 0) {
 #pragma unroll 1
         for (int c = 0; c < C::OH / 32; ++c) {
           uint32_t o[32];
           d3b::tmem_ld32(lane_addr + C::COL_O + wg * C::OH + c * 32, o);
           d3b::tmem_wait_ld();
-          if (in_tensor) {
+          if (ps) {
+            uint4* os = reinterpret_cast<uint4*>(ps);
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+              os[(wg * C::OH + c * 32 + 4 * k) / 4 * BM + r] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+          } else if (in_tensor) {
             uint32_t w[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i)
@@ -915,7 +1072,12 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
         uint32_t o[16];
         d3b::tmem_ld16(lane_addr + C::COL_O + wg * C::OH, o);
         d3b::tmem_wait_ld();
-        if (in_tensor) {
+        if (ps) {
+          uint4* os = reinterpret_cast<uint4*>(ps);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            os[(wg * C::OH + 4 * k) / 4 * BM + r] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+        } else if (in_tensor) {
           uint32_t w[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i)
@@ -926,6 +1088,22 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
         }
       }
     }
+    const volatile int* wv = work_s;
+    if (SPLIT && wv[2] >= 0) {
+      const int unit_e = wv[0], end_e = wv[1];
+      // Piece of a split unit: count it in; the piece that completes the unit
+      // merges every piece's partial. Every softmax thread reaches this point
+      // exactly once (failed waits only skip work above), so the named barrier
+      // over the 256 softmax threads cannot be left waiting.
+      __threadfence();
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (threadIdx.x == 0) bars.last_arrival = *abort_flag ? 0 : (int)count_piece(p, unit_e - p.whole_units, end_e - wv[3]);
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (bars.last_arrival) {
+        __threadfence();
+        merge_unit<D, FP16>(p, unit_e - p.whole_units, b, g, tok0, len_b, wg, r);
+      }
+    }
   }
 
   d3b::tc_fence_before();
@@ -934,20 +1112,26 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
   if (warp == 9) d3b::tmem_dealloc(tmem_base, C::TMEM_COLS);
 }
 
-template <int D, int FP16>
-int launch_dual(const CUtensorMap* maps, const Params& prm, dim3 grid, cudaStream_t stream) {
+template <int D, int FP16, bool SPLIT>
+int launch_dual_as(const CUtensorMap* maps, const Params& prm, dim3 grid, cudaStream_t stream) {
   using C = CfgDual<D>;
   static int attr_set[64] = {0};
   const int dev = d3b_host::current_device();
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(prefix_bidir_dual_kernel<D, FP16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(prefix_bidir_dual_kernel<D, FP16, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::SMEM_BYTES) != cudaSuccess)
       return D3B_ECUDA;
     attr_set[dev] = 1;
   }
-  prefix_bidir_dual_kernel<D, FP16><<<grid, DU_THREADS, C::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2],
-                                                                                maps[3], maps[4], prm);
+  prefix_bidir_dual_kernel<D, FP16, SPLIT><<<grid, DU_THREADS, C::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2],
+                                                                                       maps[3], maps[4], prm);
   return d3b_host::check_launch();
+}
+
+template <int D, int FP16>
+int launch_dual(const CUtensorMap* maps, const Params& prm, dim3 grid, cudaStream_t stream) {
+  return prm.split_units ? launch_dual_as<D, FP16, true>(maps, prm, grid, stream)
+                         : launch_dual_as<D, FP16, false>(maps, prm, grid, stream);
 }
 
 template <int D, int BN, int FP16>
@@ -967,25 +1151,124 @@ int launch(const CUtensorMap* maps, const Params& prm, dim3 grid, cudaStream_t s
 }
 
 template <int FP16>
-int dispatch(int D, const CUtensorMap* maps, const Params& prm, dim3 grid, cudaStream_t s) {
+int dispatch(int D, const CUtensorMap* maps, const Params& prm, dim3 grid, dim3 grid_dual, cudaStream_t s) {
   // D = 256 (O needs 256 TMEM columns): one tile per CTA, one CTA per SM.
   if (D == 256) return launch<256, 64, FP16>(maps, prm, grid, s);
-  // D <= 128: one tile per CTA, one CTA per SM, two MMA-issuing threads.
+  // D <= 128: one unit (or piece of a unit) per CTA, one CTA per SM, two MMA-issuing threads.
   switch (D) {
-    case 32: return launch_dual<32, FP16>(maps, prm, grid, s);
-    case 64: return launch_dual<64, FP16>(maps, prm, grid, s);
-    case 128: return launch_dual<128, FP16>(maps, prm, grid, s);
+    case 32: return launch_dual<32, FP16>(maps, prm, grid_dual, s);
+    case 64: return launch_dual<64, FP16>(maps, prm, grid_dual, s);
+    case 128: return launch_dual<128, FP16>(maps, prm, grid_dual, s);
   }
   return D3B_EUNSUPPORTED;
 }
 
+// ---------------------------------------------------------------------------
+// Launch plan of the D <= 128 kernel. Units take equal time (n key tiles) and
+// one CTA runs per SM, dispatched in block order. With U units on P SMs the
+// first U - U % P units fill whole waves; the last R = U % P units would leave
+// P - R SMs idle for a whole unit, so they may be cut into pieces instead: a
+// first piece of piece0 iterations, then runs of piece_rest. The plan is the
+// one with the shortest makespan of greedy (list) dispatch of the pieces in
+// block order, with a fixed per-CTA cost (start-up, pipeline fill, epilogue,
+// merge) of kCtaCost iterations; it is kept only if it saves >= 3 %.
+// kCtaCost comes from B200 timings of one CTA per unit at D = 128: 33-tile
+// units (config 3a) take 37.9 us per wave, 129-tile units (configs 3b, 5)
+// 121.2 us, i.e. 0.87 us per key tile plus ~9 us per CTA. Cutting is limited
+// to the regime where it measured faster: units of >= kMinSplitTiles key
+// tiles (states of 8k tokens and more) and at most kMaxFullWaves full waves
+// before the tail. A 32-block shard of config 5 (one rank of eight): 0.43 ms
+// against 0.47 ms uncut; config 3a's 33-tile units cut (26 + 7): 88 us
+// against 76 us uncut, so short units stay whole.
+// ---------------------------------------------------------------------------
+constexpr double kCtaCost = 12.0;
+constexpr int kMinSplitTiles = 64;
+constexpr int kMaxFullWaves = 7;
+
+struct TailPlan {
+  int split_units = 0, pieces = 0, piece0 = 0, piece_rest = 0;
+  double makespan = 0.0;
+};
+
+double tail_makespan(int R, int n, int P, int piece0, int rest) {
+  // pieces are dispatched piece 0 of every split unit first, then piece 1, ...
+  std::priority_queue<double, std::vector<double>, std::greater<double>> sm;
+  for (int i = 0; i < P; ++i) sm.push(0.0);
+  double mk = 0.0;
+  for (int a = 0, k = 0; a < n; ++k) {
+    const int len = std::min(n - a, k == 0 ? piece0 : rest);
+    for (int r = 0; r < R; ++r) {
+      double t = sm.top();
+      sm.pop();
+      t += len + kCtaCost;
+      mk = std::max(mk, t);
+      sm.push(t);
+    }
+    a += len;
+  }
+  return mk;
+}
+
+TailPlan plan_tail(int units, int n, int P) {
+  TailPlan best;
+  const int R = P > 0 ? units % P : 0;
+  best.makespan = n + kCtaCost;
+  // 256: the fixed count region of the workspace
+  if (R == 0 || n < kMinSplitTiles || units / P > kMaxFullWaves || R > 256) return best;
+  TailPlan cand;
+  auto consider = [&](int piece0, int rest) {
+    const double mk = tail_makespan(R, n, P, piece0, rest);
+    if (mk < cand.makespan || cand.pieces == 0) {
+      cand.makespan = mk;
+      cand.split_units = R;
+      cand.piece0 = piece0;
+      cand.piece_rest = rest;
+      cand.pieces = 1 + (n - piece0 + rest - 1) / rest;
+    }
+  };
+  for (int t = (n + 1) / 2; t < n; ++t) consider(t, n - t);  // a big and a small piece
+  for (int k = 3; k <= 8 && k <= n; ++k) {                    // k near-equal pieces
+    const int len = (n + k - 1) / k;
+    consider(len, len);
+  }
+  if (cand.pieces > 1 && cand.makespan <= 0.97 * best.makespan) return cand;
+  return best;
+}
+
+// Cached per (units, n, SMs): the plan is host arithmetic, but a call should not redo it.
+TailPlan cached_plan(int units, int n, int P) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int>, TailPlan> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_tuple(units, n, P);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  if (cache.size() > 4096) cache.clear();
+  const TailPlan t = plan_tail(units, n, P);
+  cache.emplace(key, t);
+  return t;
+}
+
+// Workspace layout: the per-unit counts first, in a region of fixed size for
+// every shape (split_units < SMs <= kMaxCounts), so partial slots written for
+// one shape never land where another shape's counts must read zero; then one
+// partial slot per piece.
+constexpr int kMaxCounts = 256;
+constexpr size_t kCountBytes = kMaxCounts * sizeof(int);
+
+size_t plan_bytes(const TailPlan& t, int D, size_t* count_bytes) {
+  if (count_bytes) *count_bytes = kCountBytes;
+  if (!t.split_units) return 0;
+  return kCountBytes + (size_t)t.split_units * t.pieces * (size_t)(BM * D + 2 * BM) * sizeof(float);
+}
+
 }  // namespace
 
-extern "C" int d3b_prefix_bidir(const void* q, const int64_t* q_strides, const void* k_state, const void* v_state,
-                                const int64_t* kv_strides, const void* k_q, const void* v_q,
-                                const int64_t* kq_strides, const int32_t* lengths, int B, int H, int Hkv, int S, int L,
-                                int D, int dtype, float scale, void* out, const int64_t* out_strides,
-                                d3b_stream_t stream) {
+static int prefix_bidir_impl(const void* q, const int64_t* q_strides, const void* k_state, const void* v_state,
+                             const int64_t* kv_strides, const void* k_q, const void* v_q, const int64_t* kq_strides,
+                             const int32_t* lengths, int B, int H, int Hkv, int S, int L, int D, int dtype,
+                             float scale, void* out, const int64_t* out_strides, void* workspace,
+                             size_t workspace_bytes, d3b_stream_t stream) {
   if (B < 0 || H <= 0 || Hkv <= 0 || S < 0 || L < 0) return D3B_EINVAL;
   if (H % Hkv) return D3B_EINVAL;
   if (dtype != D3B_BF16 && dtype != D3B_F16) return D3B_EUNSUPPORTED;
@@ -1056,9 +1339,66 @@ extern "C" int d3b_prefix_bidir(const void* q, const int64_t* q_strides, const v
   prm.err = d3b_host::device_error_word();
   if (!prm.err) return D3B_ECUDA;
 
-  const int tiles = (L + T - 1) / T;
-  if (tiles > 0x7FFFFFFF) return D3B_EINVAL;
-  dim3 grid(tiles, Hkv, B);
+  const int64_t tiles = (L + T - 1) / T;
+  const int64_t units = tiles * Hkv * B;
+  const int64_t n_full = (int64_t)(S + BN - 1) / BN + (L + BN - 1) / BN;
+  if (units > 0x7FFFFFFF || n_full > 0x7FFFFFFF) return D3B_EINVAL;
+  prm.tiles = (int)tiles;
+  prm.n_full = (int)n_full;
+  prm.whole_units = (int)units;
+  prm.split_units = prm.pieces = prm.piece0 = prm.piece_rest = 0;
+  prm.part = nullptr;
+  prm.count = nullptr;
+  int64_t ctas = units;
+  if (D <= 128 && workspace) {
+    const TailPlan t = cached_plan((int)units, (int)n_full, d3b_host::num_sms(d3b_host::current_device()));
+    if (t.split_units) {
+      size_t count_bytes = 0;
+      if (workspace_bytes < plan_bytes(t, D, &count_bytes)) return D3B_ENOSPACE;
+      if (reinterpret_cast<uintptr_t>(workspace) % 256) return D3B_EALIGN;
+      prm.whole_units = (int)units - t.split_units;
+      prm.split_units = t.split_units;
+      prm.pieces = t.pieces;
+      prm.piece0 = t.piece0;
+      prm.piece_rest = t.piece_rest;
+      prm.count = static_cast<int*>(workspace);
+      prm.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + count_bytes);
+      ctas = prm.whole_units + (int64_t)t.split_units * t.pieces;
+    }
+  }
+  if (ctas > 0x7FFFFFFF) return D3B_EINVAL;
+  const dim3 grid((unsigned)tiles, Hkv, B);
+  const dim3 grid_dual = prm.split_units ? dim3((unsigned)ctas) : grid;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  return dtype == D3B_F16 ? dispatch<1>(D, maps, prm, grid, s) : dispatch<0>(D, maps, prm, grid, s);
+  return dtype == D3B_F16 ? dispatch<1>(D, maps, prm, grid, grid_dual, s)
+                          : dispatch<0>(D, maps, prm, grid, grid_dual, s);
+}
+
+extern "C" size_t d3b_prefix_bidir_workspace_size(int B, int H, int Hkv, int S, int L, int D) {
+  if (B <= 0 || H <= 0 || Hkv <= 0 || S < 0 || L <= 0 || H % Hkv || H / Hkv > BM) return 0;
+  if (D != 32 && D != 64 && D != 128) return 0;  // D = 256 runs without one
+  const int T = BM / (H / Hkv);
+  const int64_t units = (int64_t)((L + T - 1) / T) * Hkv * B;
+  const int64_t n_full = (int64_t)(S + 127) / 128 + (L + 127) / 128;
+  if (units > 0x7FFFFFFF || n_full > 0x7FFFFFFF) return 0;
+  const TailPlan t = cached_plan((int)units, (int)n_full, d3b_host::num_sms(d3b_host::current_device()));
+  return t.split_units ? plan_bytes(t, D, nullptr) : 0;
+}
+
+extern "C" int d3b_prefix_bidir(const void* q, const int64_t* q_strides, const void* k_state, const void* v_state,
+                                const int64_t* kv_strides, const void* k_q, const void* v_q,
+                                const int64_t* kq_strides, const int32_t* lengths, int B, int H, int Hkv, int S, int L,
+                                int D, int dtype, float scale, void* out, const int64_t* out_strides,
+                                d3b_stream_t stream) {
+  return prefix_bidir_impl(q, q_strides, k_state, v_state, kv_strides, k_q, v_q, kq_strides, lengths, B, H, Hkv, S, L,
+                           D, dtype, scale, out, out_strides, nullptr, 0, stream);
+}
+
+extern "C" int d3b_prefix_bidir_ws(const void* q, const int64_t* q_strides, const void* k_state, const void* v_state,
+                                   const int64_t* kv_strides, const void* k_q, const void* v_q,
+                                   const int64_t* kq_strides, const int32_t* lengths, int B, int H, int Hkv, int S,
+                                   int L, int D, int dtype, float scale, void* out, const int64_t* out_strides,
+                                   void* workspace, size_t workspace_bytes, d3b_stream_t stream) {
+  return prefix_bidir_impl(q, q_strides, k_state, v_state, kv_strides, k_q, v_q, kq_strides, lengths, B, H, Hkv, S, L,
+                           D, dtype, scale, out, out_strides, workspace, workspace_bytes, stream);
 }

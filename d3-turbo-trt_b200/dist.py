@@ -40,6 +40,49 @@ def length_order(lengths: Sequence[int]) -> list[int]:
     return sorted(range(len(lengths)), key=lambda i: (-int(lengths[i]), i))
 
 
+class StateKVExchange:
+    """The state K/V of one request's full-attention layers, moved from ``src``
+    to every rank one layer at a time (d3trt/model/core.py:150-154 produces
+    them layer by layer in the state pass).
+
+    Each layer's keys and values share one contiguous ``[2, S, Hkv, D]`` buffer
+    (token-major, the layout the state pass writes and the question pass reads
+    through strided views), so a layer crosses NVLink in a single broadcast.
+    ``post(layer)`` enqueues that broadcast behind the work already queued on
+    the current stream (on ``src``: the state pass that produced the layer)
+    and returns at once: the next layer's state pass runs while NCCL moves this
+    one. ``wait(layer)`` makes the current stream wait for the layer before a
+    question pass reads it. Every rank posts every layer, in the same order.
+    """
+
+    def __init__(self, layers: int, tokens: int, kv_heads: int, head_dim: int, *, dtype: torch.dtype,
+                 device: torch.device, src: int = 0, group=None):
+        self.buffers = torch.empty((layers, 2, tokens, kv_heads, head_dim), dtype=dtype, device=device)
+        self.src, self.group = src, group
+        self._works: list = [None] * layers
+
+    def kv(self, layer: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """(keys, values) of a layer as ``[Hkv, S, D]`` views (token-major strides)."""
+        buf = self.buffers[layer]
+        return buf[0].permute(1, 0, 2), buf[1].permute(1, 0, 2)
+
+    def post(self, layer: int) -> None:
+        if self._works[layer] is not None:
+            raise RuntimeError(f"layer {layer} is already posted")
+        if dist.get_world_size(self.group) > 1:
+            self._works[layer] = dist.broadcast(self.buffers[layer], src=self.src, group=self.group, async_op=True)
+        else:
+            self._works[layer] = True
+
+    def wait(self, layer: int) -> None:
+        work = self._works[layer]
+        if work is None:
+            raise RuntimeError(f"layer {layer} was never posted")
+        if work is not True:
+            work.wait()
+        self._works[layer] = None
+
+
 def broadcast_state_kv(entries: Sequence[tuple[torch.Tensor, torch.Tensor]], *, src: int = 0, group=None) -> None:
     """Broadcast every (keys, values) pair in place from ``src`` to all ranks.
 

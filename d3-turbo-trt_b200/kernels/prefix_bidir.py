@@ -39,6 +39,33 @@ SITE_BAD_LENGTH = 2010
 _LENGTHS: "OrderedDict[tuple, torch.Tensor]" = OrderedDict()
 _LENGTHS_MAX = 16
 
+# Workspaces of d3b_prefix_bidir_ws, one per (device, stream): zero-filled when
+# made; every launch leaves them zeroed again and calls on one stream are
+# ordered, so they are reused as they are.
+_WORKSPACES: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
+    if nbytes == 0:
+        return None
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    key = (index, torch.cuda.current_stream(index).cuda_stream)
+    buf = _WORKSPACES.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(nbytes, dtype=torch.uint8, device=torch.device("cuda", index))
+        _WORKSPACES[key] = buf
+    return buf
+
+
+def _rezero_workspaces(index: int) -> None:
+    # a launch that gave up may have left a unit's count behind
+    for (dev, _), buf in _WORKSPACES.items():
+        if dev == index:
+            buf.zero_()
+
+
+_lib.on_device_error(_rezero_workspaces)
+
 
 def kernel_available() -> bool:
     """True when libd3b200 is built and a CUDA device is present."""
@@ -113,12 +140,14 @@ def _launch(
         raise RuntimeError("k_state and v_state must share strides")
     if k_q.stride() != v_q.stride():
         raise RuntimeError("k_q and v_q must share strides")
-    status = _lib.lib().d3b_prefix_bidir(
+    lib = _lib.lib()
+    ws = _workspace(q.device, int(lib.d3b_prefix_bidir_workspace_size(rows, heads, kv_heads, state, width, dim)))
+    status = lib.d3b_prefix_bidir_ws(
         _lib.ptr(q), st_q, _lib.ptr(k_state), _lib.ptr(v_state), st_kv, _lib.ptr(k_q), _lib.ptr(v_q), st_kq,
         _lib.ptr(lens), rows, heads, kv_heads, state, width, dim, _lib.dtype_code(q.dtype), float(scale),
-        _lib.ptr(out), st_out, _lib.stream_of(q),
+        _lib.ptr(out), st_out, _lib.ptr(ws), 0 if ws is None else ws.numel(), _lib.stream_of(q),
     )
-    _lib.check(status, "d3b_prefix_bidir")
+    _lib.check(status, "d3b_prefix_bidir_ws")
 
 
 def prefix_bidir_attention(
@@ -179,11 +208,13 @@ def prefix_bidir_attention(
     return out
 
 
-def state_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: float) -> torch.Tensor:
+def state_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale: float,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
     """Dense bidirectional attention of the state block over itself, [B, H, S, D].
 
     Drop-in for ``ops.flash_state`` / ``ops.sdpa_state`` (ops.py:107-124, :174-193):
     q [B, H, S, D], k/v [B, H_kv, S, D], GQA native, no transposes or copies.
+    ``out`` may be a preallocated [B, H, S, D] tensor (any strides, D contiguous).
     """
     _check(q, k, v)
     rows, heads, tokens, dim = q.shape
@@ -191,7 +222,10 @@ def state_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, scale:
         raise RuntimeError("heads must be divisible by kv heads")
     if tuple(k.shape) != (rows, k.shape[1], tokens, dim) or tuple(v.shape) != tuple(k.shape):
         raise RuntimeError("k/v must be [B, H_kv, S, D] matching q")
-    out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    if out is None:
+        out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    elif tuple(out.shape) != tuple(q.shape) or out.dtype != q.dtype or out.stride(-1) != 1:
+        raise RuntimeError("out must be [B, H, S, D] like q with a contiguous last dimension")
     if rows == 0 or tokens == 0:
         return out
     lens = block_offsets([tokens] * rows, q.device)

@@ -9,7 +9,11 @@
  * stride, alignment, unsupported dtype) are reported before any launch and
  * never reach the GPU. A device-side wait that runs past its wall-clock limit
  * records a site code that d3b_device_error() returns after the stream is
- * synchronised.
+ * synchronised. The word is sticky: while it is set, every later launch's
+ * waits stop early and that launch's outputs are undefined (entry points
+ * still return D3B_OK, since the launch itself was valid). Callers check
+ * d3b_device_error() after a pass (or a batch of passes) and discard the
+ * results it covers when it is non-zero; reading it with reset != 0 clears it.
  *
  * Dtype codes (x_dtype, dtype, h_dtype, out_kind):
  *   D3B_F32 = 0, D3B_F16 = 1, D3B_BF16 = 2, D3B_I32 = 3
@@ -141,11 +145,43 @@ D3B_API int d3b_w8a8_gemm(const void* qa, const void* qw, const float* sa, const
  *   out      [B, H, L, D]   strides out_strides = {b, h, l}
  * dtype: D3B_F16 or D3B_BF16 for all of q/k/v/out. D in {32, 64, 128, 256};
  * H % Hkv == 0 and H/Hkv <= 128. Strides must be multiples of 8 elements.
+ * The kernel reads `lengths` itself: an entry outside [0, L] is clamped and
+ * sets the device error word (site 2010, see d3b_device_error).
+ * Work unit: one (block, kv head, 128-row Q tile); one CTA per unit.
  */
 D3B_API int d3b_prefix_bidir(const void* q, const int64_t* q_strides, const void* k_state, const void* v_state,
                      const int64_t* kv_strides, const void* k_q, const void* v_q, const int64_t* kq_strides,
                      const int32_t* lengths, int B, int H, int Hkv, int S, int L, int D, int dtype, float scale,
                      void* out, const int64_t* out_strides, d3b_stream_t stream);
+
+/*
+ * Bytes of workspace d3b_prefix_bidir_ws uses for this shape on the current
+ * device; 0 when the shape gains nothing from one (units fill whole waves of
+ * the SMs, or D == 256).
+ */
+D3B_API size_t d3b_prefix_bidir_workspace_size(int B, int H, int Hkv, int S, int L, int D);
+
+/*
+ * d3b_prefix_bidir with a workspace: same arguments, results within rounding
+ * of it, same reference function (d3trt/kernels/prefix_bidir.py:187-260).
+ * One CTA runs per SM. When the units do not fill whole waves of the SMs, the
+ * units of the last partial wave are cut into pieces along their key tiles
+ * (sized by a host-side model of the dispatch), so that wave keeps every SM
+ * busy; the piece that finishes a unit last merges the pieces' partial
+ * results (O, row max, row sum) through the workspace.
+ *   workspace  256-byte aligned, >= d3b_prefix_bidir_workspace_size(...)
+ *              bytes, ZERO-FILLED before its first use; every launch leaves
+ *              it zeroed again. After a device-side error (d3b_device_error
+ *              non-zero) zero it again before reuse. Launches that share a
+ *              workspace must be ordered (one stream, or events).
+ *              NULL: runs as d3b_prefix_bidir.
+ * Returns D3B_ENOSPACE if workspace_bytes is too small.
+ */
+D3B_API int d3b_prefix_bidir_ws(const void* q, const int64_t* q_strides, const void* k_state, const void* v_state,
+                        const int64_t* kv_strides, const void* k_q, const void* v_q, const int64_t* kq_strides,
+                        const int32_t* lengths, int B, int H, int Hkv, int S, int L, int D, int dtype, float scale,
+                        void* out, const int64_t* out_strides, void* workspace, size_t workspace_bytes,
+                        d3b_stream_t stream);
 
 /*
  * 255-way (any n_opt <= 1024) fp32 readout softmax at the selected positions.

@@ -61,6 +61,21 @@ def _worker(rank: int, world: int, port: int, scenario: str, q) -> None:
         d3dist.broadcast_state_kv([(kb, vb)], src=0)
         assert torch.equal(kb, ks) and torch.equal(vb, vs)
 
+        # per-layer exchange: every layer posted as it is produced, waited before use
+        ex = d3dist.StateKVExchange(3, 128, 4, 32, dtype=torch.float32, device=torch.device("cpu"))
+        for layer in range(3):
+            if rank == 0:
+                ex.buffers[layer].copy_(torch.full_like(ex.buffers[layer], float(layer + 1)))
+                ex.buffers[layer, 0, 5, 2, 7] = -1.0
+            else:
+                ex.buffers[layer].zero_()
+            ex.post(layer)
+        for layer in range(3):
+            ex.wait(layer)
+            k, v = ex.kv(layer)
+            assert k.shape == (4, 128, 32) and float(k[2, 5, 7]) == -1.0
+            assert torch.all(v == layer + 1)
+
         def run_blocks(ids):
             if scenario == "fail" and rank == 1:
                 raise RuntimeError("planted failure on rank 1")
