@@ -291,7 +291,8 @@ def main():
         saved_stdout = os.dup(1)
         os.dup2(2, 1)
         try:
-            dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev,
+                                    pg_options=d3dist.nccl_options())
             dist.barrier()
             torch.cuda.synchronize()
         finally:

@@ -22,6 +22,19 @@ import torch
 import torch.distributed as dist
 
 
+def nccl_options():
+    """Options for the NCCL process group: collectives on high-priority streams.
+
+    The attention kernels fill every SM with one CTA each, so a broadcast
+    posted behind a state pass (StateKVExchange.post) waits for SMs; on a
+    high-priority stream its CTAs take the next SM that frees up, ahead of the
+    attention kernel's pending CTAs, and the layer moves while the next state
+    pass runs."""
+    opts = dist.ProcessGroupNCCL.Options()
+    opts.is_high_priority_stream = True
+    return opts
+
+
 def shard_bounds(n_blocks: int, world_size: int, rank: int) -> tuple[int, int]:
     """Contiguous split of n_blocks into world_size shards of ceil/floor sizes.
 
@@ -69,7 +82,7 @@ class StateKVExchange:
     def post(self, layer: int) -> None:
         if self._works[layer] is not None:
             raise RuntimeError(f"layer {layer} is already posted")
-        if dist.get_world_size(self.group) > 1:
+        if dist.is_available() and dist.is_initialized() and dist.get_world_size(self.group) > 1:
             self._works[layer] = dist.broadcast(self.buffers[layer], src=self.src, group=self.group, async_op=True)
         else:
             self._works[layer] = True

@@ -36,6 +36,19 @@ def test_shard_bounds_cover_every_block_once():
         d3dist.shard_bounds(10, 2, 2)
 
 
+def test_exchange_without_a_process_group_is_local():
+    ex = d3dist.StateKVExchange(2, 16, 2, 8, dtype=torch.float32, device=torch.device("cpu"))
+    ex.buffers.fill_(3.0)
+    for layer in range(2):
+        ex.post(layer)
+    for layer in range(2):
+        ex.wait(layer)
+        k, v = ex.kv(layer)
+        assert k.shape == (2, 16, 8) and torch.all(v == 3.0)
+    with pytest.raises(RuntimeError):
+        ex.wait(0)  # each post is waited once
+
+
 def test_length_order_is_stable_longest_first():
     assert d3dist.length_order([3, 48, 48, 1, 20]) == [1, 2, 4, 0, 3]
 

@@ -45,9 +45,11 @@ def _worker(rank: int, world: int, port: int, q_out) -> None:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
         torch.cuda.set_device(rank)
         dev = torch.device("cuda", rank)
-        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
         from d3_turbo_trt_b200 import _lib
         from d3_turbo_trt_b200 import dist as d3dist
+
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev,
+                                pg_options=d3dist.nccl_options())
         from d3_turbo_trt_b200.kernels import prefix_bidir as pb
 
         q, kq, vq, kv, lengths = _inputs()
