@@ -58,6 +58,17 @@ METRIC = "question-blocks/s at 4k state"
 L2_FLUSH_BYTES = 256 << 20
 
 
+def headline_config(world: int) -> dict:
+    """The `config` of the headline line, the same for both arms (ours and the reference's)."""
+    cfg = CFG3A
+    return {"workload": "cfg3a question pass: 16 blocks x 64 tokens over a 4096-token state, "
+                        "H32/Hkv4/D128 bf16, one layer, per rank",
+            "question_blocks_per_rank": cfg["B"], "state_tokens": cfg["S"], "block_tokens": cfg["L"],
+            "parallelism": f"dp{world} (question-block sharding, state KV broadcast once)",
+            "l2": "flushed before every timed step (256 MiB write) on the GPU; inputs far larger than the "
+                  "CPU caches on the host"}
+
+
 def attn_flops(B, H, L, D, S, **_):
     """4*H*D*sum_b Lq*(S+Lq) (matmul FLOPs of QK^T and PV)."""
     return 4.0 * H * D * B * L * (S + L)
@@ -202,16 +213,22 @@ def time_steps(fn, steps, warmup, stream, flush, host_bound=False):
     return [a.elapsed_time(b) for a, b in times]
 
 
+def _fp32(inp):
+    return {k: v.float() for k, v in inp.items()}
+
+
 def cpu_baseline_questions(cfg, target_s=10.0):
-    """The oracle's fp32 question pass on all host threads; blocks/s over a bounded sample."""
+    """The reference's CPU question pass (ops.sdpa_questions' call pattern: one torch SDPA per
+    block over state + own keys, fp32, oracle.attention.questions_sdpa) on all host threads;
+    blocks/s over a bounded sample."""
     from oracle import attention as oattn
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     one = dict(cfg, B=1)
-    inp = make_question_inputs(one, 99, None)
-    fn = lambda: oattn.questions(inp["q"], inp["ks"], inp["vs"], inp["kq"], inp["vq"], [one["L"]], one["D"] ** -0.5,
-                                 dtype=torch.float32)
+    inp = _fp32(make_question_inputs(one, 99, None))
+    fn = lambda: oattn.questions_sdpa(inp["q"], inp["ks"], inp["vs"], inp["kq"], inp["vq"], [one["L"]],
+                                      one["D"] ** -0.5)
     fn()  # warm-up
     n, t0 = 0, time.perf_counter()
     while True:
@@ -222,7 +239,8 @@ def cpu_baseline_questions(cfg, target_s=10.0):
             break
     return {"value": n / el, "unit": "question-blocks/s", "cores": threads, "kind": "port",
             "sample": f"{n} question blocks of config 3a ({one['L']} tokens vs a {one['S']}-token state, "
-                      f"H{one['H']}/Hkv{one['Hkv']}/D{one['D']}), oracle fp32 torch CPU, {el:.1f} s"}
+                      f"H{one['H']}/Hkv{one['Hkv']}/D{one['D']}), torch SDPA per block in fp32 (the reference's "
+                      f"sdpa_questions pattern), {el:.1f} s"}
 
 
 def run_reference(args):
@@ -234,11 +252,11 @@ def run_reference(args):
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    sample = 2  # question blocks per step: keeps K steps within a few minutes on the host
+    sample = CFG3A["B"]  # every step is the whole config-3a pass (16 blocks), as on the GPU
     one = dict(CFG3A, B=sample)
-    inp = make_question_inputs(one, 7, None)
-    fn = lambda: oattn.questions(inp["q"], inp["ks"], inp["vs"], inp["kq"], inp["vq"], [one["L"]] * sample,
-                                 one["D"] ** -0.5, dtype=torch.float32)
+    inp = _fp32(make_question_inputs(one, 7, None))
+    fn = lambda: oattn.questions_sdpa(inp["q"], inp["ks"], inp["vs"], inp["kq"], inp["vq"], [one["L"]] * sample,
+                                      one["D"] ** -0.5)
     for _ in range(args.warmup):
         fn()
     t0 = time.perf_counter()
@@ -250,10 +268,11 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "question-blocks/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "cfg3a question pass (4096-token state + 16 x 64-token blocks, H32/Hkv4/D128)",
-                   "sample_blocks_per_step": sample, "l2": "n/a (CPU)"},
+        "config": headline_config(args.gpus),
         "cpu_baseline": {"value": value, "unit": "question-blocks/s", "cores": threads, "kind": "port",
-                         "sample": f"{sample} blocks per step, oracle restatement of ops.sdpa_questions, fp32 torch CPU"},
+                         "sample": f"the whole config-3a pass ({sample} blocks) per step: one torch SDPA per block "
+                                   "over state + own keys in fp32, the call pattern of the reference's "
+                                   "ops.sdpa_questions (d3trt/model/ops.py:127-171), all host threads"},
         "e2e": {"value": value, "unit": "question-blocks/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -406,11 +425,7 @@ def main():
             "metric": METRIC, "value": value, "unit": "question-blocks/s", "n_gpus": world, "steps": args.steps,
             "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) q/k/v)",
-            "config": {"workload": "cfg3a question pass: 16 blocks x 64 tokens over a 4096-token state, "
-                                   "H32/Hkv4/D128 bf16, one layer, per rank",
-                       "question_blocks_per_rank": cfg["B"], "state_tokens": cfg["S"], "block_tokens": cfg["L"],
-                       "parallelism": f"dp{world} (question-block sharding, state KV broadcast once)",
-                       "l2": "flushed before every timed step (256 MiB write)"},
+            "config": headline_config(world),
             "roofline": {"bound": "tensor", "achieved": achieved_tflops, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved_tflops / peak, "traffic": traffic,
                          "kernel": "prefix_bidir_dual_kernel<128,bf16>",

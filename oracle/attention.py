@@ -56,6 +56,34 @@ def questions(
     return out
 
 
+def questions_sdpa(
+    q: torch.Tensor,
+    k_state: torch.Tensor,
+    v_state: torch.Tensor,
+    k_q: torch.Tensor,
+    v_q: torch.Tensor,
+    lengths: Sequence[int],
+    scale: float,
+) -> torch.Tensor:
+    """The question pass as the reference's CPU path computes it (ops.sdpa_questions,
+    d3trt/model/ops.py:127-171): per block, one torch scaled_dot_product_attention call
+    over cat(state keys, own keys[:length]) with native GQA, in the inputs' dtype. The
+    timed reference arm and CPU baseline run this, so they use the same torch CPU kernel
+    as the reference; padding rows are zero."""
+    import torch.nn.functional as F
+
+    out = q.new_zeros(q.shape)
+    for b in range(q.shape[0]):
+        n = int(lengths[b])
+        if n == 0:
+            continue
+        keys = torch.cat([k_state, k_q[b, :, :n]], dim=1)
+        vals = torch.cat([v_state, v_q[b, :, :n]], dim=1)
+        out[b, :, :n] = F.scaled_dot_product_attention(q[b, :, :n][None], keys[None], vals[None], scale=scale,
+                                                      enable_gqa=True)[0]
+    return out
+
+
 def state(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, dtype: torch.dtype = torch.float64):
     """[B,H,S,D] dense bidirectional GQA attention over [B,H_kv,S,D] (ops.py:107-124)."""
     rows, heads, tokens, dim = q.shape

@@ -152,6 +152,10 @@ def test_attention_ragged(case):
     out = oattn.questions(t["q"], t["ks"], t["vs"], t["kq"], t["vq"], g[f"{case}_lens"].tolist(),
                           float(g[f"{case}_scale"]))
     np.testing.assert_allclose(out.numpy(), g[f"{case}_out"], atol=2e-6, rtol=0)
+    # the reference's own call pattern (timed by bench.py's reference arm) gives the golden too
+    out = oattn.questions_sdpa(t["q"], t["ks"], t["vs"], t["kq"], t["vq"], g[f"{case}_lens"].tolist(),
+                               float(g[f"{case}_scale"]))
+    np.testing.assert_allclose(out.numpy(), g[f"{case}_out"], atol=2e-6, rtol=0)
 
 
 # --- readout ---
