@@ -95,7 +95,13 @@ def apply(cache, call, error_type):
 def observe(cache):
     stats = cache.stats()
     return {k: stats[k] for k in ("entries", "bytes", "capacity_bytes", "hits", "misses", "hit_rate",
-                                  "evictions", "rejected")} | {"order": list(cache._entries)}
+                                  "evictions", "rejected")} | {"order": _lru_order(cache)}
+
+
+def _lru_order(cache):
+    """Keys least recently used first: the reference keeps them in an ordered dict; this
+    library's cache reports them with lru_keys()."""
+    return list(cache.lru_keys()) if hasattr(cache, "lru_keys") else list(cache._entries)
 
 
 def main() -> None:

@@ -172,7 +172,7 @@ def test_cache_with_arena_replays_reference_trace(name):
             got = gen.apply(cache, step["call"], dcache.StateCacheError)
             assert got == step["result"], f"step {i} {step['call']}"
             assert gen.observe(cache) == step["after"], f"step {i} {step['call']}"
-        packed = [e for e in cache._entries.values() if isinstance(e.snapshot, PackedSnapshot)]
+        packed = [e for e in cache.entries() if isinstance(e.snapshot, PackedSnapshot)]
         assert cache.count == 0 or packed
         assert arena.stats()["used_bytes"] >= sum(e.nbytes for e in packed)
     finally:
