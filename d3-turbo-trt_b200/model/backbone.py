@@ -18,16 +18,21 @@ library:
 * attention: ``state_attention`` for the state pass, ``prefix_bidir_attention``
   for the question pass, then ``out * sigmoid(gate)`` fused with o_proj's
   quantisation (``fused.sigmoid_gate_quant``);
+* the GDN layers' causal convolution + SiLU: ``conv.causal_conv1d_silu`` on the
+  in_proj output as the GEMM writes it (token-major; reads the snapshot's tail in
+  place of the reference's concatenation), its q/k/v handed on as strided views;
 * the GDN scan of the question pass: ``gdn.question_gated_delta_rule`` (one
   shared initial state, no per-row copy or head repeat); of the state pass:
   the library's recurrence, or FLA's chunked kernel when the caller selects it
   (``gdn_state="fla"``: the reference's own GPU path for that call);
+* SiLU(gate) * up fused with down_proj's quantisation (``fused.silu_mul_quant``) and
+  the GDN output's gated RMSNorm fused with out_proj's (``fused.gated_rmsnorm_quant``);
 * the 255-way readout: ``readout.probabilities_tensor``.
 
-The rest stays on the reference's own formulas in torch (config 4 keeps the GDN
-layers' convolution on the existing path): the causal depthwise convolution
-(ops.py:266-285), q/k RMSNorm, rotary embedding (transformers'
-``apply_rotary_pos_emb``), the gated RMSNorm of the GDN output, SiLU(gate) * up.
+The rest stays on the reference's own formulas in torch: q/k RMSNorm and the
+rotary embedding (transformers' ``apply_rotary_pos_emb``) of the 16 attention
+layers, and the GDN gates g and beta. ``causal_conv1d``, ``gated_rms_norm`` below
+are the reference's torch forms, kept as the checks of the kernels.
 Weights are taken by the model's own parameter names (``layers.{i}.self_attn.
 q_proj.weight``, ...), so a checkpoint or a transformers model's ``state_dict``
 loads as it is.
@@ -43,6 +48,7 @@ import torch.nn.functional as F
 
 from ..kernels import prefix_bidir as pb
 from . import fused, gdn
+from .conv import causal_conv1d_silu
 from .quant import QuantLinear, quantizable, quantize_rows
 from .readout import probabilities_tensor
 from .snapshot import AttentionEntry, DeltaEntry
@@ -195,11 +201,12 @@ class D3Backbone:
                 L["A_log"], L["dt_bias"], L["norm"] = w(a + "A_log"), w(a + "dt_bias"), w(a + "norm.weight")
             else:
                 raise ValueError(f"unknown layer type {kind!r}")
-            fed = ("q_proj", "k_proj", "v_proj", "in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a", "gate_up")
+            fed = ("q_proj", "k_proj", "v_proj", "o_proj", "in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a",
+                   "out_proj", "gate_up", "down")
             for n in fed:
                 if n in L and not L[n].quant:
-                    raise ValueError(f"layer {i} {n}: every projection of the normed rows must be quantizable "
-                                     "(in and out features divisible by 16)")
+                    raise ValueError(f"layer {i} {n}: every projection reads fused-producer codes and must be "
+                                     "quantizable (in and out features divisible by 16)")
             self.layers.append(L)
 
     # ------------------------------------------------------------------
@@ -254,10 +261,9 @@ class D3Backbone:
         else:
             mixed, entry = self._delta(L, q, s, rows, T, entry)
         h2, q2, s2 = fused.add_rmsnorm_quant(res, mixed.view(rows, T, H), L["post_w1"], c.rms_norm_eps, self.mode)
-        gu = L["gate_up"].from_codes(q2, s2, None).view(rows * T, 2, -1)
-        act = F.silu(gu[:, 0]) * gu[:, 1]  # silu(gate_proj(x)) * up_proj(x), bf16
-        qa, sa = quantize_rows(act, self.mode)
-        down = L["down"].from_codes(qa, sa, act).view(rows, T, H)
+        gu = L["gate_up"].from_codes(q2, s2, None)  # [M, 2I]: gate, then up
+        qa, sa = fused.silu_mul_quant(gu, self.mode)  # silu(gate_proj(x)) * up_proj(x), quantised for down_proj
+        down = L["down"].from_codes(qa, sa, None).view(rows, T, H)
         return h2, down, entry
 
     def _attention(self, L, q, s, rows, T, rope, entry, lengths, lens_d):
@@ -287,25 +293,24 @@ class D3Backbone:
         c = self.config
         window = c.linear_conv_kernel_dim - 1
         HV, HK, Dk, Dv = c.linear_num_value_heads, c.linear_num_key_heads, c.linear_key_head_dim, c.linear_value_head_dim
-        mixed = L["in_proj_qkv"].from_codes(q, s, None).view(rows, T, -1).transpose(1, 2)
+        mixed = L["in_proj_qkv"].from_codes(q, s, None).view(rows, T, -1)  # token-major [rows, T, conv_dim]
         z = L["in_proj_z"].from_codes(q, s, None).view(rows, T, HV, Dv)
         b = L["in_proj_b"].from_codes(q, s, None).view(rows, T, HV)
         a = L["in_proj_a"].from_codes(q, s, None).view(rows, T, HV)
         if entry is None:
-            conv = causal_conv1d(mixed, L["conv"])
-            tail = mixed[:, :, -window:]
+            conv = causal_conv1d_silu(mixed, L["conv"])
+            tail = mixed[:, -window:, :].transpose(1, 2)  # [1, conv_dim, window], as core.py:321
             if tail.shape[-1] < window:
                 tail = F.pad(tail, (window - tail.shape[-1], 0))
             initial = None
         else:
             tail, initial = entry.tail, entry.recurrent
-            joined = torch.cat([tail.expand(rows, -1, -1), mixed], dim=-1)
-            conv = causal_conv1d(joined, L["conv"])[:, :, window:]
+            conv = causal_conv1d_silu(mixed, L["conv"], tail)  # reads the tail in place: no cat
             initial = initial.expand(rows, -1, -1, -1)
-        query, key, value = torch.split(conv.transpose(1, 2), [c.key_dim, c.key_dim, c.value_dim], dim=-1)
-        query = query.reshape(rows, T, HK, Dk)
-        key = key.reshape(rows, T, HK, Dk)
-        value = value.reshape(rows, T, HV, Dv)
+        kd = c.key_dim
+        query = conv[..., :kd].view(rows, T, HK, Dk)  # strided views: the scan reads them in place
+        key = conv[..., kd:2 * kd].view(rows, T, HK, Dk)
+        value = conv[..., 2 * kd:].view(rows, T, HV, Dv)
         beta = b.sigmoid()
         g = -L["A_log"].float().exp() * F.softplus(a.float() + L["dt_bias"])
         if entry is None:
@@ -314,15 +319,17 @@ class D3Backbone:
         else:
             core, _ = gdn.question_gated_delta_rule(query, key, value, g=g, beta=beta, initial_state=initial,
                                                     output_final_state=False, use_qk_l2norm_in_kernel=True)
-        out = gated_rms_norm(core.reshape(-1, Dv), z.reshape(-1, Dv), L["norm"], c.rms_norm_eps)
-        return L["out_proj"](out.reshape(rows * T, -1)), entry
+        qo, so = fused.gated_rmsnorm_quant(core.reshape(rows * T, -1), z.reshape(rows * T, -1), L["norm"],
+                                           c.rms_norm_eps, Dv, self.mode)  # Qwen3_5RMSNormGated, then out_proj's codes
+        return L["out_proj"].from_codes(qo, so, None), entry
 
     def _state_scan(self, query, key, value, g, beta):
         if self.gdn_state == "fla":
             from fla.ops.gated_delta_rule import chunk_gated_delta_rule
 
             rep = value.shape[2] // query.shape[2]
-            return chunk_gated_delta_rule(query.repeat_interleave(rep, 2), key.repeat_interleave(rep, 2), value,
+            return chunk_gated_delta_rule(query.repeat_interleave(rep, 2), key.repeat_interleave(rep, 2),
+                                          value.contiguous(),
                                           g=g, beta=beta, initial_state=None, output_final_state=True,
                                           use_qk_l2norm_in_kernel=True)
         return gdn.gated_delta_rule(query, key, value, g=g, beta=beta, initial_state=None, output_final_state=True,

@@ -135,3 +135,71 @@ def sigmoid_gate_quant(attn_out: torch.Tensor, gate: torch.Tensor, mode: str):
     """(q [B*T, H*D], scale [B*T, 1]): the gated rows quantised per row in ``mode`` for o_proj."""
     _, q, scale = _gate(attn_out, gate, _mode_code(mode))
     return q, scale[:, None]
+
+
+def _out_buffers(M, K, mode_code, dev):
+    out = torch.empty((M, K), dtype=torch.bfloat16, device=dev) if mode_code == _lib.MODE_NONE else None
+    q = scale = None
+    if mode_code != _lib.MODE_NONE:
+        q = torch.empty((M, K), dtype=_FP8 if mode_code == _lib.MODE_FP8 else torch.int8, device=dev)
+        scale = torch.empty((M,), dtype=torch.float32, device=dev)
+    return out, q, scale
+
+
+def _silu_mul(gate_up: torch.Tensor, mode_code: int):
+    _check_bf16(gate_up, "silu_mul")
+    rows = _rows(gate_up, "gate_up")
+    M, two_i = rows.shape
+    if two_i % 2:
+        raise RuntimeError("gate_up rows must hold gate and up halves")
+    out, q, scale = _out_buffers(M, two_i // 2, mode_code, rows.device)
+    if M:
+        st = _lib.lib().d3b_silu_mul_quant(_lib.ptr(rows), rows.stride(0), _lib.ptr(out), _lib.ptr(q), _lib.ptr(scale),
+                                          M, two_i // 2, mode_code, _lib.stream_of(rows))
+        _lib.check(st, "d3b_silu_mul_quant")
+    return out, q, scale
+
+
+def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
+    """bf16(bf16(silu(gate)) * up) [M, I] from the fused gate/up projection's rows [M, 2I]
+    (the Qwen3.5 MLP's act_fn(gate_proj(x)) * up_proj(x))."""
+    out, _, _ = _silu_mul(gate_up, _lib.MODE_NONE)
+    return out
+
+
+def silu_mul_quant(gate_up: torch.Tensor, mode: str):
+    """(q [M, I], scale [M, 1]): the MLP activation quantised per row for down_proj."""
+    _, q, scale = _silu_mul(gate_up, _mode_code(mode))
+    return q, scale[:, None]
+
+
+def _gated_norm(x: torch.Tensor, z: torch.Tensor, weight: torch.Tensor, eps: float, head_dim: int, mode_code: int):
+    _check_bf16(x, "gated_rmsnorm")
+    _check_bf16(z, "gated_rmsnorm")
+    xr, zr = _rows(x, "x"), _rows(z, "z")
+    if xr.shape != zr.shape:
+        raise RuntimeError(f"x {tuple(xr.shape)} and z {tuple(zr.shape)} differ")
+    M, K = xr.shape
+    w = weight.to(device=xr.device, dtype=torch.bfloat16).contiguous()
+    if w.numel() != head_dim:
+        raise RuntimeError(f"weight has {w.numel()} values for head_dim {head_dim}")
+    out, q, scale = _out_buffers(M, K, mode_code, xr.device)
+    if M:
+        st = _lib.lib().d3b_gated_rmsnorm_quant(_lib.ptr(xr), xr.stride(0), _lib.ptr(zr), zr.stride(0), _lib.ptr(w),
+                                               float(eps), head_dim, _lib.ptr(out), _lib.ptr(q), _lib.ptr(scale), M, K,
+                                               mode_code, _lib.stream_of(xr))
+        _lib.check(st, "d3b_gated_rmsnorm_quant")
+    return out, q, scale
+
+
+def gated_rmsnorm(x: torch.Tensor, z: torch.Tensor, weight: torch.Tensor, eps: float, head_dim: int) -> torch.Tensor:
+    """Qwen3_5RMSNormGated over heads of ``head_dim`` on token rows x, z [..., K] -> [M, K] bf16."""
+    out, _, _ = _gated_norm(x, z, weight, eps, head_dim, _lib.MODE_NONE)
+    return out
+
+
+def gated_rmsnorm_quant(x: torch.Tensor, z: torch.Tensor, weight: torch.Tensor, eps: float, head_dim: int,
+                        mode: str):
+    """(q [M, K], scale [M, 1]): the gated norm's token rows quantised for out_proj."""
+    _, q, scale = _gated_norm(x, z, weight, eps, head_dim, _mode_code(mode))
+    return q, scale[:, None]

@@ -184,6 +184,50 @@ D3B_API int d3b_prefix_bidir_ws(const void* q, const int64_t* q_strides, const v
                         d3b_stream_t stream);
 
 /*
+ * Causal depthwise convolution + SiLU of the GDN layers over token-major rows.
+ * Replaces d3trt/model/ops.py:266-285 (causal_conv1d: F.conv1d with groups=C
+ * and padding W-1, cut to L, then SiLU) as called at d3trt/model/core.py:311-330,
+ * including the question pass's torch.cat of the snapshot tail.
+ *   x      [rows, T, C] bf16, channels contiguous, strides {row, token} in
+ *          elements (multiples of 8, token stride >= C)
+ *   tail   NULL (state pass: zeros before the first token) or the last W-1
+ *          inputs [rows or 1, C, W-1] bf16 with strides {row (0 = shared), c, k}
+ *   weight [C, W] bf16 contiguous (conv1d.weight squeezed)
+ *   out    [rows, T, C] bf16 contiguous
+ *   out[r,t,c] = bf16(silu(bf16(sum_j weight[c,j] * in(r, t-(W-1)+j, c))))
+ * C % 8 == 0, 2 <= W <= 8, 16-byte aligned x and out.
+ */
+D3B_API int d3b_causal_conv1d_silu(const void* x, const int64_t* x_strides, const void* tail,
+                                   const int64_t* tail_strides, const void* weight, void* out, int rows, int T,
+                                   int C, int W, d3b_stream_t stream);
+
+/*
+ * SiLU(gate) * up fused with the per-row quantisation of down_proj's input.
+ * Replaces the MLP's act_fn(gate_proj(x)) * up_proj(x) (transformers Qwen3_5MLP,
+ * d3trt/model/trtllm_stack.py:118-120) followed by d3trt/model/quant.py:92-100.
+ *   gate_up [M, 2I] bf16 rows of ld elements: gate in [0, I), up in [I, 2I)
+ *   act = bf16(bf16(silu(gate)) * up); act_out [M, I] bf16 contiguous, optional
+ *   (required with D3B_MODE_NONE); q [M, I] codes + scale [M] of act
+ * I % 8 == 0, I <= 24576.
+ */
+D3B_API int d3b_silu_mul_quant(const void* gate_up, int64_t ld, void* act_out, void* q, float* scale, int64_t M,
+                               int64_t I, int mode, d3b_stream_t stream);
+
+/*
+ * Gated RMSNorm of the GDN output fused with out_proj's per-row quantisation.
+ * Replaces Qwen3_5RMSNormGated (called at d3trt/model/core.py:400-401) followed
+ * by d3trt/model/quant.py:92-100 on the token rows it produces.
+ *   x, z [M, K] bf16 token rows (K = heads * head_dim) of ldx / ldz elements
+ *   per head: out = bf16(bf16(weight * bf16(x * rsqrt(mean(x^2) + eps))) * silu(z))
+ *   weight [head_dim] bf16; out [M, K] bf16 contiguous, optional (required with
+ *   D3B_MODE_NONE); q [M, K] codes + scale [M] of out
+ * head_dim in {64, 128, 256}, K % head_dim == 0, K <= 6144.
+ */
+D3B_API int d3b_gated_rmsnorm_quant(const void* x, int64_t ldx, const void* z, int64_t ldz, const void* weight,
+                                    float eps, int head_dim, void* out, void* q, float* scale, int64_t M, int64_t K,
+                                    int mode, d3b_stream_t stream);
+
+/*
  * 255-way (any n_opt <= 1024) fp32 readout softmax at the selected positions.
  * Replaces the probabilities body of d3trt/model/trtllm_stack.py:451-468
  * (= hf_stack.py:67-84): logits = f32(hidden) @ readout^T; logits[b, j] = -inf

@@ -1,0 +1,97 @@
+"""GPU parity of the GDN causal convolution + SiLU kernel (d3b_causal_conv1d_silu)
+against the reference's torch form (d3trt/model/ops.py:266-285: F.conv1d over the
+channel-major [B, C, L] input, cut to L, then SiLU), for the state pass (no tail)
+and the question pass (the snapshot's tail concatenated in front, shared by all
+rows or one per row). The kernel sums in fp32 in kernel order, so its bf16 results
+may differ from the library convolution's by one bf16 ulp where the fp32 sums
+round differently; they must agree within that and be identical almost
+everywhere."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from d3_turbo_trt_b200 import _lib
+from d3_turbo_trt_b200.model.backbone import causal_conv1d
+from d3_turbo_trt_b200.model.conv import causal_conv1d_silu
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _ulps(a, b):
+    return (a.view(torch.int16).int() - b.view(torch.int16).int()).abs()
+
+
+def _check(got, want):
+    d = _ulps(got, want)
+    assert int(d.max()) <= 1 and float((d == 0).float().mean()) > 0.995
+
+
+@pytest.mark.parametrize("B,T,C,W", [(1, 4096, 2048, 4), (1, 37, 520, 3), (3, 1, 64, 4), (2, 70, 1032, 5)])
+def test_state_pass_against_torch(B, T, C, W):
+    g = torch.Generator().manual_seed(B * 1000 + T)
+    x = torch.randn(B, T, C, generator=g).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(C, W, generator=g) * 0.5).to(torch.bfloat16).to(DEV)
+    got = causal_conv1d_silu(x, w)
+    want = causal_conv1d(x.transpose(1, 2), w).transpose(1, 2)
+    _check(got, want)
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("shared", [True, False])
+def test_question_pass_with_tail(shared):
+    g = torch.Generator().manual_seed(5)
+    B, T, C, W = 17, 48, 1536, 4
+    state = torch.randn(1 if shared else B, 200, C, generator=g).to(torch.bfloat16).to(DEV)
+    x = torch.randn(B, T, C, generator=g).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(C, W, generator=g) * 0.5).to(torch.bfloat16).to(DEV)
+    tail = state[:, -(W - 1):, :].transpose(1, 2)  # [1 or B, C, W-1] strided view, as the backbone keeps it
+    got = causal_conv1d_silu(x, w, tail)
+    joined = torch.cat([tail.expand(B, -1, -1), x.transpose(1, 2)], dim=-1)
+    want = causal_conv1d(joined, w)[:, :, W - 1:].transpose(1, 2)
+    _check(got, want)
+    # the input read through row and token strides (a slice of a wider buffer)
+    wide = torch.randn(B, T, C + 64, generator=g).to(torch.bfloat16).to(DEV)
+    got2 = causal_conv1d_silu(wide[..., :C], w, tail)
+    joined2 = torch.cat([tail.expand(B, -1, -1), wide[..., :C].transpose(1, 2)], dim=-1)
+    _check(got2, causal_conv1d(joined2, w)[:, :, W - 1:].transpose(1, 2))
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("M,I", [(300, 2048), (77, 17408), (5, 512)])
+def test_silu_mul_quant_against_torch(M, I):
+    """SiLU(gate) * up (the MLP, bf16 as torch computes it) and its per-row codes."""
+    from d3_turbo_trt_b200.model import fused, quant
+
+    g = torch.Generator().manual_seed(M)
+    gu = (torch.randn(M, 2 * I, generator=g) * 3).to(torch.bfloat16).to(DEV)
+    want = torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]
+    act = fused.silu_mul(gu)
+    _check(act, want)
+    for mode in ("fp8", "int8"):
+        q, s = fused.silu_mul_quant(gu, mode)
+        rq, rs = quant.quantize_rows(act, mode)  # the codes of the kernel's own rows, bit for bit
+        assert torch.equal(q.view(torch.uint8), rq.view(torch.uint8)) and torch.equal(s, rs)
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("M,H,D", [(300, 16, 128), (41, 48, 128), (9, 8, 64), (7, 4, 256)])
+def test_gated_rmsnorm_quant_against_torch(M, H, D):
+    """Qwen3_5RMSNormGated per head on token rows, and the rows' codes for out_proj."""
+    from d3_turbo_trt_b200.model import fused, quant
+    from d3_turbo_trt_b200.model.backbone import gated_rms_norm
+
+    g = torch.Generator().manual_seed(M + H)
+    x = (torch.randn(M, H * D, generator=g) * 0.3).to(torch.bfloat16).to(DEV)
+    z = torch.randn(M, H * D, generator=g).to(torch.bfloat16).to(DEV)
+    w = (1 + torch.randn(D, generator=g) * 0.1).to(torch.bfloat16).to(DEV)
+    want = gated_rms_norm(x.reshape(-1, D), z.reshape(-1, D), w, 1e-6).reshape(M, H * D)
+    out = fused.gated_rmsnorm(x, z, w, 1e-6, D)
+    _check(out, want)
+    for mode in ("fp8", "int8"):
+        q, s = fused.gated_rmsnorm_quant(x, z, w, 1e-6, D, mode)
+        rq, rs = quant.quantize_rows(out, mode)
+        assert torch.equal(q.view(torch.uint8), rq.view(torch.uint8)) and torch.equal(s, rs)
+    assert _lib.device_error() == 0
