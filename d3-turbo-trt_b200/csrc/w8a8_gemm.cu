@@ -234,6 +234,209 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 1) d3b::tmem_dealloc(tmem_base, TMEM_COLS);
 }
 
+// ===========================================================================
+// CTA-pair form (cluster of 2, tcgen05 cta_group::2) for M >= 512: the pair owns
+// a 256 x 256 output tile. Each CTA TMA-loads its own 128 rows of A and its own
+// 128 rows of B per stage (no multicast), both completing on rank 0's "full"
+// barrier, which rank 0 alone arms with the pair's bytes; rank 0's MMA thread issues M=256 N=256 K=32 instructions that read A
+// and B from both CTAs' shared memory and accumulate 128 rows x 256 columns into
+// each CTA's TMEM. Compared with one CTA per SM (M=128, N=256), each SM writes
+// and feeds the tensor core 32 KB of operands per 4 instructions instead of
+// 48 KB, so shared-memory bandwidth no longer caps the MMA rate, and 6 stages
+// fit. Commits go to both CTAs' barriers (tcgen05.commit multicast); each CTA's
+// epilogue hands the accumulator back to rank 0 with a remote arrive.
+// ===========================================================================
+constexpr int P_BM = 128, P_BN = 256, P_STAGES = 6;
+constexpr int P_A_BYTES = P_BM * BK;                     // 16 KB: this CTA's 128 rows of A
+constexpr int P_B_BYTES = (P_BN / 2) * BK;               // 16 KB: this CTA's 128 rows of B
+constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024;
+
+enum { kSitePairProducer = 1101, kSitePairMma, kSitePairMmaAcc, kSitePairEpi, kSitePairDrain };
+
+struct __align__(8) PairBarriers {
+  uint64_t full[P_STAGES];   // rank 0: both CTAs' loads of the stage (rank 0 arms it with all bytes)
+  uint64_t empty[P_STAGES];  // each CTA: the pair's MMAs of the stage are done
+  uint64_t tfull[2];         // each CTA: accumulator ready
+  uint64_t tempty[2];        // rank 0: both CTAs' epilogues done with the accumulator (256 arrivals)
+  uint64_t drain;
+  uint32_t tmem_slot;
+  int abort_flag;
+};
+
+template <int MODE>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    w8a8_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
+                          const float* __restrict__ sa, const float* __restrict__ sw, void* __restrict__ out,
+                          int64_t ldo, int M, int N, int K, int out_kind, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ PairBarriers bars;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + P_STAGES * P_A_BYTES;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = d3b::cluster_ctarank();
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  const int num_m = (M + 2 * P_BM - 1) / (2 * P_BM), num_n = (N + P_BN - 1) / P_BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + BK - 1) / BK;
+  volatile int* abort_flag = &bars.abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      d3b::mbar_init(&bars.full[s], 1);
+      d3b::mbar_init(&bars.empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      d3b::mbar_init(&bars.tfull[a], 1);
+      d3b::mbar_init(&bars.tempty[a], 256);
+    }
+    d3b::mbar_init(&bars.drain, 1);
+    bars.abort_flag = 0;
+    d3b::fence_barrier_init();
+    d3b::tma_prefetch_desc(&mapA);
+    d3b::tma_prefetch_desc(&mapB);
+  }
+  if (warp == 1) d3b::tmem_alloc_pair(&bars.tmem_slot, TMEM_COLS);
+  d3b::tc_fence_before();
+  d3b::cluster_sync();  // both CTAs' barriers initialised before any remote arrive or commit
+  d3b::tc_fence_after();
+  const uint32_t tmem_base = bars.tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (each CTA: its halves of A and B) ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = pair; t < num_tiles && !*abort_flag; t += pairs) {
+        const int m0 = (t % num_m) * 2 * P_BM + (int)rank * P_BM, n0 = (t / num_m) * P_BN + (int)rank * (P_BN / 2);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!d3b::mbar_wait(&bars.empty[stage], phase ^ 1, abort_flag, err, kSitePairProducer)) break;
+          // rank 0 arms the stage with both CTAs' bytes; rank 1's loads only complete
+          // bytes on it (they may land before the arming: the phase still waits for
+          // rank 0's arrival)
+          if (rank == 0) d3b::mbar_arrive_expect_tx(&bars.full[stage], 2 * P_STAGE_BYTES);
+          const uint32_t leader_full = d3b::cluster_addr(&bars.full[stage], 0);
+          d3b::tma_load_2d_pair(sA + stage * P_A_BYTES, &mapA, leader_full, kb * BK, m0);
+          d3b::tma_load_2d_pair(sB + stage * P_B_BYTES, &mapB, leader_full, kb * BK, n0);
+          if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (rank 0 only) ----------------
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = MODE == D3B_MODE_FP8 ? d3b::make_idesc(1, 0, 0, 0, 0, 2 * P_BM, P_BN)
+                                                       : d3b::make_idesc(2, 1, 1, 0, 0, 2 * P_BM, P_BN);
+      const uint32_t a_base = d3b::smem_u32(sA), b_base = d3b::smem_u32(sB);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int t = pair; t < num_tiles && !*abort_flag; t += pairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!d3b::mbar_wait(&bars.tempty[acc], acc_phase ^ 1, abort_flag, err, kSitePairMmaAcc)) break;
+        d3b::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * P_BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!d3b::mbar_wait(&bars.full[stage], phase, abort_flag, err, kSitePairMma)) break;
+          d3b::tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < BK / 32; ++k) {
+            const uint64_t ad = d3b::make_smem_desc(a_base + stage * P_A_BYTES + k * 32, 16, 1024, d3b::kLayoutSW128);
+            const uint64_t bd = d3b::make_smem_desc(b_base + stage * P_B_BYTES + k * 32, 16, 1024, d3b::kLayoutSW128);
+            const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+            if (MODE == D3B_MODE_FP8)
+              d3b::mma_f8f6f4_pair(d_tmem, ad, bd, idesc, accum);
+            else
+              d3b::mma_i8_pair(d_tmem, ad, bd, idesc, accum);
+          }
+          d3b::mma_commit_pair(&bars.empty[stage], 0x3);
+          if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
+        }
+        d3b::mma_commit_pair(&bars.tfull[acc], 0x3);
+      }
+      d3b::mma_commit_pair(&bars.drain, 0x1);
+      const uint32_t addr = d3b::smem_u32(&bars.drain);
+      const uint64_t t0 = d3b::globaltimer_ns();
+      while (!d3b::mbar_try_wait(addr, 0)) {
+        if (d3b::globaltimer_ns() - t0 > D3B_WAIT_LIMIT_NS) {
+          d3b::record_device_error(err, kSitePairDrain);
+          break;
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5 of each CTA: its 128 rows) ----------------
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    const bool is_int = MODE == D3B_MODE_INT8;
+    int local = 0;
+    for (int t = pair; t < num_tiles && !*abort_flag; t += pairs, ++local) {
+      const int m0 = (t % num_m) * 2 * P_BM + (int)rank * P_BM, n0 = (t / num_m) * P_BN;
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!d3b::warp_wait(&bars.tfull[acc], acc_phase, abort_flag, err, kSitePairEpi)) break;
+      d3b::tc_fence_after();
+      const int row = m0 + row_in_tile;
+      const float sa_row = (out_kind != D3B_I32 && row < M) ? __ldg(sa + row) : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < P_BN / 32; ++c) {
+        uint32_t r[32];
+        d3b::tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * P_BN + c * 32, r);
+        d3b::tmem_wait_ld();
+        if (c == P_BN / 32 - 1) {
+          d3b::tc_fence_before();
+          d3b::mbar_arrive_cluster(d3b::cluster_addr(&bars.tempty[acc], 0));  // to rank 0
+        }
+        store_chunk(out, ldo, out_kind, row, M, n0 + c * 32, N, r, sa_row, sw, is_int);
+      }
+    }
+  }
+
+  __syncwarp();  // lanes that skipped a role loop rejoin before the aligned cluster barrier
+  d3b::tc_fence_before();
+  d3b::cluster_sync();  // rank 0's MMAs (which write both TMEMs) are drained before either CTA frees TMEM
+  d3b::tc_fence_after();
+  if (warp == 1) d3b::tmem_dealloc_pair(tmem_base, TMEM_COLS);
+}
+
+template <int MODE>
+int launch_pair(const CUtensorMap& mA, const CUtensorMap& mB, const float* sa, const float* sw, void* y, int64_t ldy,
+                int M, int N, int K, int out_kind, cudaStream_t stream) {
+  static int attr_set[64] = {0};
+  const int dev = d3b_host::current_device();
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(w8a8_gemm_pair_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             P_SMEM_BYTES) != cudaSuccess)
+      return D3B_ECUDA;
+    attr_set[dev] = 1;
+  }
+  int* err = d3b_host::device_error_word();
+  if (!err) return D3B_ECUDA;
+  const int tiles = ((M + 2 * P_BM - 1) / (2 * P_BM)) * ((N + P_BN - 1) / P_BN);
+  // Pairs that fit at once (SM pairs of a GPC with one free SM stay idle), queried once per device.
+  static int max_pairs_of[64] = {0};
+  int max_pairs = (dev >= 0 && dev < 64) ? max_pairs_of[dev] : 0;
+  if (max_pairs <= 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 256);
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = P_SMEM_BYTES;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, w8a8_gemm_pair_kernel<MODE>, &cfg) != cudaSuccess || clusters <= 0) {
+      cudaGetLastError();
+      clusters = d3b_host::num_sms(dev) / 2;
+    }
+    max_pairs = clusters;
+    if (dev >= 0 && dev < 64) max_pairs_of[dev] = clusters;
+  }
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  w8a8_gemm_pair_kernel<MODE><<<2 * pairs, NUM_THREADS, P_SMEM_BYTES, stream>>>(mA, mB, sa, sw, y, ldy, M, N, K,
+                                                                               out_kind, err);
+  return d3b_host::check_launch();
+}
+
 template <int MODE>
 int launch(const CUtensorMap& mA, const CUtensorMap& mB, const float* sa, const float* sw, void* y, int64_t ldy,
            int M, int N, int K, int out_kind, cudaStream_t stream) {
@@ -274,13 +477,19 @@ extern "C" int d3b_w8a8_gemm(const void* qa, const void* qw, const float* sa, co
   CUtensorMap mA, mB;
   const uint64_t dA[2] = {(uint64_t)K, (uint64_t)M}, dB[2] = {(uint64_t)K, (uint64_t)N};
   const uint64_t st[1] = {(uint64_t)K};
-  const uint32_t boxA[2] = {BK, BM}, boxB[2] = {BK, BN};
+  const bool pair = M >= 512;  // CTA pairs: 256 x 256 tiles, each CTA loads 128 rows of B
+  const uint32_t boxA[2] = {BK, BM}, boxB[2] = {BK, pair ? (uint32_t)(P_BN / 2) : (uint32_t)BN};
   int rc = d3b_host::encode_tiled(&mA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, qa, dA, st, boxA,
                                   CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = d3b_host::encode_tiled(&mB, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, qw, dB, st, boxB, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (pair) {
+    if (mode == D3B_MODE_FP8)
+      return launch_pair<D3B_MODE_FP8>(mA, mB, sa, sw, y, ldy, (int)M, (int)N, (int)K, out_kind, s);
+    return launch_pair<D3B_MODE_INT8>(mA, mB, sa, sw, y, ldy, (int)M, (int)N, (int)K, out_kind, s);
+  }
   if (mode == D3B_MODE_FP8) return launch<D3B_MODE_FP8>(mA, mB, sa, sw, y, ldy, (int)M, (int)N, (int)K, out_kind, s);
   return launch<D3B_MODE_INT8>(mA, mB, sa, sw, y, ldy, (int)M, (int)N, (int)K, out_kind, s);
 }

@@ -112,8 +112,23 @@ def test_int8_accumulators_bit_exact(shape):
     assert np.array_equal(acc.cpu().numpy(), oq.int_gemm(qa, qw))
 
 
+@pytest.mark.parametrize("shape", [(512, 256, 128), (600, 272, 320), (777, 1040, 4096), (1030, 528, 17408)])
+def test_int8_pair_tiles_bit_exact(shape):
+    """M >= 512 runs on CTA pairs (256 x 256 tiles): ragged M leaves the second CTA's
+    rows past the end, ragged N the second half of B."""
+    m, n, k = shape
+    qa, _ = _rand_codes(m, k, "int8", 11)
+    qw, _ = _rand_codes(n, k, "int8", 12)
+    a, w = _to_dev_codes(qa, "int8"), _to_dev_codes(qw, "int8")
+    acc = quant.scaled_mm(a, w, None, None, out_dtype=torch.int32)
+    if m * n * k <= 600 * 272 * 320:
+        assert np.array_equal(acc.cpu().numpy(), oq.int_gemm(qa, qw))
+    assert torch.equal(acc, torch._int_mm(a, w.t()))
+    assert _lib.device_error() == 0
+
+
 @pytest.mark.parametrize("mode", ["fp8", "int8"])
-@pytest.mark.parametrize("shape", [(300, 272, 320), (77, 13824 // 8, 5120)])
+@pytest.mark.parametrize("shape", [(300, 272, 320), (77, 13824 // 8, 5120), (600, 272, 320), (1030, 528, 1024)])
 def test_w8a8_fp32_and_bf16_outputs(mode, shape):
     m, n, k = shape
     qa, sa = _rand_codes(m, k, mode, 3)
@@ -132,8 +147,11 @@ def test_w8a8_fp32_and_bf16_outputs(mode, shape):
     if mode == "int8":
         assert np.array_equal(y16, ref16)
     else:
+        # the bf16 store is the kernel's own fp32 result rounded once; against the
+        # reference: the fp32 tolerance above plus the two roundings (<= 2 ulp)
+        assert np.array_equal(y16, oq.bf16_round(y32))
         ulp = np.abs(oq.bf16_round(ref * (1 + 2.0**-7)) - ref16) + 1e-30
-        assert np.all(np.abs(y16 - ref16) <= ulp)
+        assert np.all(np.abs(y16 - ref16) <= 2 * ulp + 1e-5 * max(1.0, np.abs(ref).max()))
 
 
 @pytest.mark.parametrize("mode", ["fp8", "int8"])
