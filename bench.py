@@ -707,6 +707,36 @@ def cfg4_e2e(dev, stream, flush, peaks):
             "timing": "device events, median of 2 requests after one warm-up, L2 flushed before each"}
 
 
+FP8_SPEC_TFLOPS = 4500.0  # B200 dense e4m3 / int8, nominal
+
+
+def model_gemms(dev, stream, flush):
+    """The config-4 backbone's W8A8 projections at the question pass's 255 x 48 = 12240
+    rows, e4m3 codes with per-row and per-channel scales, bf16 out: this library's kernel
+    against torch._scaled_mm (a CUTLASS sm100 kernel) on the same operands."""
+    from d3_turbo_trt_b200.model import quant
+
+    g = torch.Generator(device=dev).manual_seed(12)
+    M, out = 12240, {}
+    for name, N, K in (("mlp_gate_or_up", 17408, 5120), ("mlp_down", 5120, 17408), ("attn_q_gate", 8192, 5120),
+                       ("attn_k_or_v", 512, 5120), ("gdn_in_proj_qkv", 10240, 5120), ("gdn_out_proj", 5120, 6144)):
+        a = (torch.randn(M, K, generator=g, device=dev) * 0.5).to(torch.float8_e4m3fn)
+        w = (torch.randn(N, K, generator=g, device=dev) * 0.5).to(torch.float8_e4m3fn)
+        sa = torch.rand(M, generator=g, device=dev) + 0.5
+        sw = torch.rand(N, generator=g, device=dev) + 0.5
+        ours = statistics.median(time_steps(lambda: quant.scaled_mm(a, w, sa, sw, out_dtype=torch.bfloat16),
+                                            10, 3, stream, flush))
+        wt = w.t()
+        lib = statistics.median(time_steps(lambda: torch._scaled_mm(a, wt, scale_a=sa[:, None], scale_b=sw[None, :],
+                                                                    out_dtype=torch.bfloat16), 10, 3, stream, flush))
+        fl = 2.0 * M * N * K
+        out[name] = {"M": M, "N": N, "K": K, "ms": ours, "tflops": fl / ours / 1e9,
+                     "frac_spec_4500": fl / ours / 1e9 / FP8_SPEC_TFLOPS, "torch_scaled_mm_ms": lib,
+                     "speedup_vs_torch": lib / ours}
+        del a, w, wt
+    return out
+
+
 def secondary(dev, stream, flush, peaks, quant, pb, d3b):
     """State pass, config 3b, W8A8 GEMM (config 2), act quant and readout."""
     res = {}
@@ -750,6 +780,7 @@ def secondary(dev, stream, flush, peaks, quant, pb, d3b):
         qbytes = M * K * 2 + M * K + M * 4
         res[f"w8a8_{mode}_cfg2"] = {
             "gemm_ms": tg, "gemm_tflops": gemm_flops / tg / 1e9, "frac_dense_peak": gemm_flops / tg / 1e9 / fp8_peak,
+            "frac_spec_4500": gemm_flops / tg / 1e9 / FP8_SPEC_TFLOPS,
             "act_quant_ms": tq, "act_quant_gbs": qbytes / tq / 1e6, "act_quant_frac_hbm": qbytes / tq / 1e6 / peaks["hbm_gbs"],
             "quant_linear_ms": tl}
         if mode == "fp8":
@@ -763,6 +794,7 @@ def secondary(dev, stream, flush, peaks, quant, pb, d3b):
         del layer, qa, sa
     res["fp8_int8_peak_tflops"] = fp8_peak
     del x, w
+    res["w8a8_fp8_model_shapes"] = model_gemms(dev, stream, flush)
     # launch-bound regime: back-to-back config-1-sized question passes, eager wrapper calls
     # against replays of a captured CUDA graph (events around the whole loop: host gaps count)
     from d3_turbo_trt_b200.kernels.graphs import QuestionPassGraph
