@@ -650,6 +650,7 @@ def cfg4_e2e(dev, stream, flush, peaks):
     on this library's chunked form. Timed on the device: state pass, question pass, readout;
     end to end: token ids from pinned host memory and probabilities back to it."""
     from d3_turbo_trt_b200.model.backbone import BackboneConfig, D3Backbone
+    from d3_turbo_trt_b200.model.batching import QuestionBatcher
 
     cfg = BackboneConfig()
     vocab, S, nb, L, n_opt = 151_936, 4096, 255, 48, 255
@@ -664,7 +665,9 @@ def cfg4_e2e(dev, stream, flush, peaks):
     build_s = time.perf_counter() - t0
     g = torch.Generator().manual_seed(44)
     state_ids = torch.randint(0, vocab, (1, S), generator=g).pin_memory()
-    q_ids = torch.randint(0, vocab, (nb, L), generator=g).pin_memory()
+    q_ids = torch.randint(0, vocab, (nb, L), generator=g)
+    pieces = q_ids.tolist()  # the request's question pieces as the backend holds them (token lists)
+    batcher = QuestionBatcher(dev, pad_id=0, stream=stream)
     lengths = [L] * nb
     readout = (torch.randn(n_opt, cfg.hidden_size, generator=g) * 0.02).to(dev)
     counts = torch.full((nb,), n_opt, dtype=torch.int32, device=dev)
@@ -675,7 +678,7 @@ def cfg4_e2e(dev, stream, flush, peaks):
         flush()
         ev[0].record(stream)
         s_ids = state_ids.to(dev, non_blocking=True)
-        qi = q_ids.to(dev, non_blocking=True)
+        qi, _ = batcher.build(pieces)  # padded ids + lengths: one pinned buffer, one copy
         ev[1].record(stream)
         snap = bb.state(s_ids)
         ev[2].record(stream)
@@ -702,7 +705,7 @@ def cfg4_e2e(dev, stream, flush, peaks):
             "value": nb / (t_end / 1e3), "unit": "question-blocks/s (end to end, one request)",
             "e2e_ms": t_end, "h2d_ms": t_in, "state_pass_ms": t_state - t_in, "question_pass_ms": t_q - t_state,
             "readout_and_copy_ms": t_end - t_q, "linear_params": dense, "gemm_tflop": gemm_flops / 1e12,
-            "h2d_bytes": (state_ids.numel() + q_ids.numel()) * 8, "d2h_bytes": host_probs.numel() * 4,
+            "h2d_bytes": (state_ids.numel() + q_ids.numel()) * 8 + nb * 4, "d2h_bytes": host_probs.numel() * 4,
             "gdn_state_scan": gdn_state, "build_s": build_s,
             "timing": "device events, median of 2 requests after one warm-up, L2 flushed before each"}
 
