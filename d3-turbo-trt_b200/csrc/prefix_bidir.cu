@@ -588,6 +588,7 @@ struct CfgDual {
 
 struct __align__(8) BarsDual {
   uint64_t q_full;
+  uint64_t q_empty;  // the unit's QK^T MMAs have completed: Q may be reloaded
   uint64_t k_full[8], k_empty[8];  // K ring
   uint64_t v_full[8], v_empty[8];  // V ring
   uint64_t s_full[2];   // QK(j) committed into S[j%2]
@@ -596,7 +597,8 @@ struct __align__(8) BarsDual {
   uint64_t p_free[2];   // PV(j) committed: P[j%2] is free and O holds PV(0..j)
   uint64_t mdone[2];    // reference max of tile j published (by group j%2)
   uint64_t xsum[4];     // per-group sums exchanged for the epilogue (per warp pair)
-  uint64_t o_final;
+  uint64_t o_final;     // the unit's last PV committed: O is complete
+  uint64_t o_free;      // the epilogue has read O: the next unit's first PV may overwrite it
   uint64_t drain_qk, drain_pv;
   uint32_t tmem_slot;
   int abort_flag;
@@ -719,10 +721,49 @@ __device__ void merge_unit(const Params& p, int r, int b, int g, int tok0, int l
   }
 }
 
-// SPLIT: the launch has split units (1-D grid, pieces, partial merge). The
-// instantiation without it is one CTA per unit on the (tiles, Hkv, B) grid,
-// with none of the split code in it (measured 2-3 % faster than one kernel
-// carrying both paths).
+// One work item of the D <= 128 kernel: a unit (block b, kv head g, Q tile at
+// token tok0) and its key-tile range [a, a + n); n == 0 when the tile holds no
+// real token (its rows are zero-filled) or, in a split launch, when the piece
+// has no real key tile.
+struct Work {
+  int unit, b, g, tok0, len_b, a, n;
+};
+
+// Item i of this CTA. Without SPLIT the launch is persistent: CTA c takes units
+// c, c + gridDim.x, ... (all of a launch's units have the same number of key
+// tiles up to the blocks' lengths, so a static round robin balances them).
+// With SPLIT each CTA has one item, the unit or piece of cta_work.
+template <bool SPLIT>
+__device__ __forceinline__ bool work_item(const Params& p, int i, int n_s, Work& w) {
+  int e;
+  if constexpr (SPLIT) {
+    if (i > 0) return false;
+    int slot;
+    cta_work(p, w.unit, w.a, e, slot);
+  } else {
+    w.unit = (int)blockIdx.x + i * (int)gridDim.x;
+    if (w.unit >= p.whole_units) return false;
+    w.a = 0;
+    e = p.n_full;
+  }
+  const int tile = w.unit % p.tiles;
+  w.g = (w.unit / p.tiles) % p.Hkv;
+  w.b = w.unit / (p.tiles * p.Hkv);
+  w.len_b = block_length(p, w.b);
+  w.tok0 = tile * p.T;
+  w.n = w.tok0 >= w.len_b ? 0 : max(0, min(e, n_s + (w.len_b + 127) / 128) - w.a);
+  return true;
+}
+
+// SPLIT: the launch has split units (1-D grid, one unit or piece per CTA,
+// partial merge). Without it the kernel is persistent: min(units, SMs) CTAs,
+// each looping over its units with TMEM, the barriers and the rings set up
+// once. Every ring, S/P buffer and barrier phase counts on across units (tile
+// jg of the CTA's sequence, non-empty unit ie), so the next unit's Q and first
+// K/V tiles load, and its first QK^T runs, while the softmax warps finish the
+// previous unit's epilogue. Q is single-buffered: its load waits for the last
+// QK^T of the previous unit (q_empty); O is reused: the first PV of a unit
+// waits until the epilogue has read the previous unit's O (o_free).
 template <int D, int FP16, bool SPLIT>
 __global__ void __launch_bounds__(DU_THREADS, 1)
     prefix_bidir_dual_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapKs,
@@ -730,63 +771,61 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
                              const __grid_constant__ CUtensorMap mapVq, const Params p) {
   using C = CfgDual<D>;
   constexpr int BN = C::BN;
+  static_assert(BN == 128, "work_item counts own tiles of 128 keys");
   extern __shared__ uint8_t smem_raw[];
   __shared__ BarsDual bars;
   __shared__ float mref_s[2][BM];   // reference max of the last tile of each group, per row
   __shared__ float lsum_s[2][BM];   // epilogue exchange: running sums and their references
   __shared__ float mlast_s[2][BM];
-  __shared__ int work_s[4];  // unit, end of range, slot, start of range: reloaded where used, not kept in registers
+  __shared__ int work_s[4];  // split launch: unit, end of range, slot, start of range (reloaded where used)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int unit, a, e, slot;
-  if constexpr (SPLIT) {
-    cta_work(p, unit, a, e, slot);
-  } else {
-    unit = ((int)blockIdx.z * p.Hkv + (int)blockIdx.y) * p.tiles + (int)blockIdx.x;
-    a = 0;
-    e = p.n_full;
-    slot = -1;
-  }
-  const int tile = unit % p.tiles, g = (unit / p.tiles) % p.Hkv, b = unit / (p.tiles * p.Hkv);
   const int G = p.G, T = p.T;
   const int rows_used = G * T;
-  const int len_b = block_length(p, b);
-  const int tok0 = tile * T;
-  if (tok0 >= len_b) {  // no real token in this tile: zero-fill (once per unit) and leave
-    if (warp < 4 && a == 0) zero_tile_rows<D>(p, b, g, tok0, warp, lane);
-    return;
+  const int n_s = (p.S + BN - 1) / BN;
+  if constexpr (SPLIT) {
+    int unit, a, e, slot;
+    cta_work(p, unit, a, e, slot);
+    const int tile = unit % p.tiles, g = (unit / p.tiles) % p.Hkv, b = unit / (p.tiles * p.Hkv);
+    const int len_b = block_length(p, b);
+    const int tok0 = tile * T;
+    if (tok0 >= len_b) {  // no real token in this tile: zero-fill (once per unit) and leave
+      if (warp < 4 && a == 0) zero_tile_rows<D>(p, b, g, tok0, warp, lane);
+      return;
+    }
+    const int n = max(0, min(e, n_s + (len_b + BN - 1) / BN) - a);
+    if (n == 0) {
+      // A piece of a split unit with no real key tile: an empty partial (l = 0),
+      // counted in like any other piece.
+      if (threadIdx.x < BM) {
+        float* ps = p.part + (int64_t)slot * PartSlot<D>::FLOATS;
+        ps[BM * D + threadIdx.x] = -INFINITY;
+        ps[BM * D + BM + threadIdx.x] = 0.f;
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) bars.last_arrival = count_piece(p, unit - p.whole_units, e - a);
+      __syncthreads();
+      if (bars.last_arrival && threadIdx.x < 2 * BM) {
+        __threadfence();
+        merge_unit<D, FP16>(p, unit - p.whole_units, b, g, tok0, len_b, threadIdx.x / BM, threadIdx.x % BM);
+      }
+      return;
+    }
+    if (threadIdx.x == 0) {
+      work_s[0] = unit;
+      work_s[1] = e;
+      work_s[2] = slot;
+      work_s[3] = a;
+    }
   }
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sK = smem + C::Q_BYTES;
   uint8_t* sV = sK + C::NK * C::SLOT_BYTES;
   volatile int* abort_flag = &bars.abort_flag;
-  const int n_s = (p.S + BN - 1) / BN;
-  // this CTA's key tiles: kt = a + j for j in [0, n); own tiles past the block's length are skipped
-  const int n = max(0, min(e, n_s + (len_b + BN - 1) / BN) - a);
-  if (SPLIT && n == 0) {
-    // A piece of a split unit with no real key tile: an empty partial (l = 0),
-    // counted in like any other piece.
-    if (threadIdx.x < BM) {
-      float* ps = p.part + (int64_t)slot * PartSlot<D>::FLOATS;
-      ps[BM * D + threadIdx.x] = -INFINITY;
-      ps[BM * D + BM + threadIdx.x] = 0.f;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) bars.last_arrival = count_piece(p, unit - p.whole_units, e - a);
-    __syncthreads();
-    if (bars.last_arrival && threadIdx.x < 2 * BM) {
-      __threadfence();
-      merge_unit<D, FP16>(p, unit - p.whole_units, b, g, tok0, len_b, threadIdx.x / BM, threadIdx.x % BM);
-    }
-    return;
-  }
 
   if (threadIdx.x == 0) {
-    work_s[0] = unit;
-    work_s[1] = e;
-    work_s[2] = slot;
-    work_s[3] = a;
     d3b::mbar_init(&bars.q_full, 1);
+    d3b::mbar_init(&bars.q_empty, 1);
     for (int i = 0; i < 8; ++i) {
       d3b::mbar_init(&bars.k_full[i], 1);
       d3b::mbar_init(&bars.k_empty[i], 1);
@@ -802,12 +841,13 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
     }
     for (int q = 0; q < 4; ++q) d3b::mbar_init(&bars.xsum[q], 64);
     d3b::mbar_init(&bars.o_final, 1);
+    d3b::mbar_init(&bars.o_free, 256);
     d3b::mbar_init(&bars.drain_qk, 1);
     d3b::mbar_init(&bars.drain_pv, 1);
     bars.abort_flag = 0;
     d3b::fence_barrier_init();
   }
-  if (rows_used < BM) {
+  if (rows_used < BM) {  // rows no Q box covers stay zero for every unit
     const int per_chunk = (BM - rows_used) * C::ROWB / 16;
     for (int i = threadIdx.x; i < C::NCH * per_chunk; i += DU_THREADS) {
       const int c = i / per_chunk, o = i % per_chunk;
@@ -829,7 +869,7 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
     // a whole 128-key row of S in registers.
     asm volatile("setmaxnreg.dec.sync.aligned.u32 48;" ::: "memory");
    if (warp == 8 || warp == 11) {
-    // ================= TMA producers: warp 8 Q and K_0, K_1, ..., warp 11 V_0, V_1, ... =================
+    // ================= TMA producers: warp 8 Q and K tiles, warp 11 V tiles =================
     // (one producer per ring, so K tiles never wait behind a full V ring)
     if (lane == 0) {
       const bool is_v = warp == 11;
@@ -840,10 +880,6 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
         d3b::tma_prefetch_desc(&mapQ);
         d3b::tma_prefetch_desc(&mapKq);
         if (n_s) d3b::tma_prefetch_desc(&mapKs);
-        d3b::mbar_arrive_expect_tx(&bars.q_full, C::NCH * rows_used * C::ROWB);
-#pragma unroll
-        for (int c = 0; c < C::NCH; ++c)
-          d3b::tma_load_4d(sQ + c * C::Q_CHUNK, &mapQ, &bars.q_full, c * C::CH, g * G, tok0, b);
       }
       const int nslot = is_v ? C::NV : C::NK;
       uint64_t* fulls = is_v ? bars.v_full : bars.k_full;
@@ -851,24 +887,39 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
       uint8_t* ring = is_v ? sV : sK;
       const CUtensorMap* m_state = is_v ? &mapVs : &mapKs;
       const CUtensorMap* m_own = is_v ? &mapVq : &mapKq;
-      int slot = 0;
+      int slot = 0, ie = 0;
       uint32_t ph = 0;
-      for (int j = 0; j < n; ++j) {
-        if (!d3b::mbar_wait(&empties[slot], ph ^ 1, abort_flag, p.err, kSiteDuSlotEmpty)) break;
-        uint64_t* full = &fulls[slot];
-        uint8_t* dst = ring + slot * C::SLOT_BYTES;
-        d3b::mbar_arrive_expect_tx(full, C::SLOT_BYTES);
-        const int kt = a + j;  // key tile of the unit
-        if (kt < n_s) {
+      bool ok = true;
+      Work w;
+      for (int i = 0; ok && work_item<SPLIT>(p, i, n_s, w); ++i) {
+        if (w.n == 0) continue;
+        if (!is_v) {
+          // Q of this unit: the previous unit's QK^T MMAs have all completed
+          if (ie > 0 && !(ok = d3b::mbar_wait(&bars.q_empty, (uint32_t)(ie - 1) & 1, abort_flag, p.err, kSiteDuQ)))
+            break;
+          d3b::mbar_arrive_expect_tx(&bars.q_full, C::NCH * rows_used * C::ROWB);
 #pragma unroll
           for (int c = 0; c < C::NCH; ++c)
-            d3b::tma_load_3d(dst + c * C::SLOT_CHUNK, m_state, full, c * C::CH, kt * BN, g);
-        } else {
-#pragma unroll
-          for (int c = 0; c < C::NCH; ++c)
-            d3b::tma_load_4d(dst + c * C::SLOT_CHUNK, m_own, full, c * C::CH, (kt - n_s) * BN, g, b);
+            d3b::tma_load_4d(sQ + c * C::Q_CHUNK, &mapQ, &bars.q_full, c * C::CH, w.g * G, w.tok0, w.b);
         }
-        if (++slot == nslot) { slot = 0; ph ^= 1; }
+        for (int j = 0; j < w.n; ++j) {
+          if (!(ok = d3b::mbar_wait(&empties[slot], ph ^ 1, abort_flag, p.err, kSiteDuSlotEmpty))) break;
+          uint64_t* full = &fulls[slot];
+          uint8_t* dst = ring + slot * C::SLOT_BYTES;
+          d3b::mbar_arrive_expect_tx(full, C::SLOT_BYTES);
+          const int kt = w.a + j;  // key tile of the unit
+          if (kt < n_s) {
+#pragma unroll
+            for (int c = 0; c < C::NCH; ++c)
+              d3b::tma_load_3d(dst + c * C::SLOT_CHUNK, m_state, full, c * C::CH, kt * BN, w.g);
+          } else {
+#pragma unroll
+            for (int c = 0; c < C::NCH; ++c)
+              d3b::tma_load_4d(dst + c * C::SLOT_CHUNK, m_own, full, c * C::CH, (kt - n_s) * BN, w.g, w.b);
+          }
+          if (++slot == nslot) { slot = 0; ph ^= 1; }
+        }
+        ++ie;
       }
     }
   } else if (warp == 9) {
@@ -877,25 +928,35 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
       constexpr uint32_t idesc_qk = d3b::make_idesc(1, fmt, fmt, 0, 0, BM, BN);
       const uint64_t dq0 = d3b::make_smem_desc(d3b::smem_u32(sQ), 16, C::SBO, C::LAYOUT);
       const uint64_t dk0 = d3b::make_smem_desc(d3b::smem_u32(sK), 16, C::SBO, C::LAYOUT);
-      bool ok = d3b::mbar_wait(&bars.q_full, 0, abort_flag, p.err, kSiteDuQ);
-      for (int j = 0; j < n && ok; ++j) {
-        const int sb = j & 1;
-        const uint32_t u = (uint32_t)(j >> 1);
-        // S[sb] was last read by the softmax of tile j-2
-        if (!(ok = d3b::mbar_wait(&bars.s_free[sb], (u & 1) ^ 1, abort_flag, p.err, kSiteDuSFree))) break;
-        const int slot = j % C::NK;
-        if (!(ok = d3b::mbar_wait(&bars.k_full[slot], (uint32_t)(j / C::NK) & 1, abort_flag, p.err, kSiteDuSlotK)))
-          break;
-        d3b::tc_fence_after();
-        const uint64_t dk = dk0 + (uint64_t)((slot * C::SLOT_BYTES) >> 4);
+      bool ok = true;
+      int jg = 0, ie = 0;
+      Work w;
+      for (int i = 0; ok && work_item<SPLIT>(p, i, n_s, w); ++i) {
+        if (w.n == 0) continue;
+        if (!(ok = d3b::mbar_wait(&bars.q_full, (uint32_t)ie & 1, abort_flag, p.err, kSiteDuQ))) break;
+        for (int j = 0; j < w.n; ++j, ++jg) {
+          const int sb = jg & 1;
+          const uint32_t u = (uint32_t)(jg >> 1);
+          // S[sb] was last read by the softmax of tile jg-2
+          if (!(ok = d3b::mbar_wait(&bars.s_free[sb], (u & 1) ^ 1, abort_flag, p.err, kSiteDuSFree))) break;
+          const int slot = jg % C::NK;
+          if (!(ok = d3b::mbar_wait(&bars.k_full[slot], (uint32_t)(jg / C::NK) & 1, abort_flag, p.err,
+                                    kSiteDuSlotK)))
+            break;
+          d3b::tc_fence_after();
+          const uint64_t dk = dk0 + (uint64_t)((slot * C::SLOT_BYTES) >> 4);
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const int c = (k * 16) / C::CH, off = ((k * 16) % C::CH) * 2;
-          d3b::mma_f16_ss(tmem_base + C::COL_S + sb * BN, dq0 + (uint64_t)((c * C::Q_CHUNK + off) >> 4),
-                          dk + (uint64_t)((c * C::SLOT_CHUNK + off) >> 4), idesc_qk, k > 0 ? 1u : 0u);
+          for (int k = 0; k < D / 16; ++k) {
+            const int c = (k * 16) / C::CH, off = ((k * 16) % C::CH) * 2;
+            d3b::mma_f16_ss(tmem_base + C::COL_S + sb * BN, dq0 + (uint64_t)((c * C::Q_CHUNK + off) >> 4),
+                            dk + (uint64_t)((c * C::SLOT_CHUNK + off) >> 4), idesc_qk, k > 0 ? 1u : 0u);
+          }
+          d3b::mma_commit(&bars.s_full[sb]);
+          d3b::mma_commit(&bars.k_empty[slot]);
         }
-        d3b::mma_commit(&bars.s_full[sb]);
-        d3b::mma_commit(&bars.k_empty[slot]);
+        if (!ok) break;
+        d3b::mma_commit(&bars.q_empty);  // the unit's QK^T MMAs have read Q
+        ++ie;
       }
       d3b::mma_commit(&bars.drain_qk);
       const uint32_t addr = d3b::smem_u32(&bars.drain_qk);
@@ -913,23 +974,35 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
       constexpr uint32_t idesc_pv = d3b::make_idesc(1, fmt, fmt, 0, 1, BM, D);
       const uint64_t dv0 = d3b::make_smem_desc(d3b::smem_u32(sV), C::SLOT_CHUNK, C::SBO, C::LAYOUT);
       bool ok = true;
-      for (int j = 0; j < n && ok; ++j) {
-        const int sb = j & 1;
-        const uint32_t u = (uint32_t)(j >> 1);
-        if (!(ok = d3b::mbar_wait(&bars.p_full[sb], u & 1, abort_flag, p.err, kSiteDuPFull))) break;
-        const int slot = j % C::NV;
-        if (!(ok = d3b::mbar_wait(&bars.v_full[slot], (uint32_t)(j / C::NV) & 1, abort_flag, p.err, kSiteDuSlotV)))
-          break;
-        d3b::tc_fence_after();
-        const uint64_t dv = dv0 + (uint64_t)((slot * C::SLOT_BYTES) >> 4);
+      int jg = 0, ie = 0;
+      Work w;
+      for (int i = 0; ok && work_item<SPLIT>(p, i, n_s, w); ++i) {
+        if (w.n == 0) continue;
+        for (int j = 0; j < w.n; ++j, ++jg) {
+          const int sb = jg & 1;
+          const uint32_t u = (uint32_t)(jg >> 1);
+          if (!(ok = d3b::mbar_wait(&bars.p_full[sb], u & 1, abort_flag, p.err, kSiteDuPFull))) break;
+          // O of the previous unit has been read by the epilogue before this unit's first PV overwrites it
+          if (j == 0 && ie > 0 &&
+              !(ok = d3b::mbar_wait(&bars.o_free, (uint32_t)(ie - 1) & 1, abort_flag, p.err, kSiteDuFinal)))
+            break;
+          const int slot = jg % C::NV;
+          if (!(ok = d3b::mbar_wait(&bars.v_full[slot], (uint32_t)(jg / C::NV) & 1, abort_flag, p.err,
+                                    kSiteDuSlotV)))
+            break;
+          d3b::tc_fence_after();
+          const uint64_t dv = dv0 + (uint64_t)((slot * C::SLOT_BYTES) >> 4);
 #pragma unroll
-        for (int k = 0; k < BN / 16; ++k)
-          d3b::mma_f16_ts(tmem_base + C::COL_O, tmem_base + C::COL_P + sb * (BN / 2) + k * 8,
-                          dv + (uint64_t)((k * 16 * C::ROWB) >> 4), idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
-        d3b::mma_commit(&bars.p_free[sb]);
-        d3b::mma_commit(&bars.v_empty[slot]);
+          for (int k = 0; k < BN / 16; ++k)
+            d3b::mma_f16_ts(tmem_base + C::COL_O, tmem_base + C::COL_P + sb * (BN / 2) + k * 8,
+                            dv + (uint64_t)((k * 16 * C::ROWB) >> 4), idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+          d3b::mma_commit(&bars.p_free[sb]);
+          d3b::mma_commit(&bars.v_empty[slot]);
+        }
+        if (!ok) break;
+        d3b::mma_commit(&bars.o_final);  // O holds the unit's PV(0..n-1)
+        ++ie;
       }
-      if (ok) d3b::mma_commit(&bars.o_final);
       d3b::mma_commit(&bars.drain_pv);
       const uint32_t addr = d3b::smem_u32(&bars.drain_pv);
       const uint64_t t0 = d3b::globaltimer_ns();
@@ -944,99 +1017,110 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory");
     // ================= softmax + epilogue (warps 0-7) =================
-    // Group wg (warps 4wg .. 4wg+3, one thread per row) takes the key tiles
-    // j = wg, wg+2, ... with S[wg] and P[wg]. Both groups scale P by the same
-    // per-row reference max, decided tile by tile in order: tile j reads the
-    // reference of tile j-1 (from the other group, through shared memory),
-    // raises it only if its own max exceeds it by more than 2^8, and publishes
-    // its own. Each group keeps its own running sum l (with the reference of
-    // its last tile); the two are combined in the epilogue.
+    // Group wg (warps 4wg .. 4wg+3, one thread per row) takes the key tiles of
+    // odd or even position jg in the CTA's tile sequence, with S[wg] and P[wg].
+    // Within a unit both groups scale P by the same per-row reference max,
+    // decided tile by tile in order: tile jg reads the reference of tile jg-1
+    // (from the other group, through shared memory), raises it only if its own
+    // max exceeds it by more than 2^8, and publishes its own; the first tile of
+    // a unit ignores the value it reads (the wait keeps the groups in step).
+    // Each group keeps its own running sum l (with the reference of its last
+    // tile); the two are combined in the epilogue.
     const int wg = warp >> 2, quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
     const uint32_t col_s = C::COL_S + wg * BN, col_p = C::COL_P + wg * (BN / 2);
     const float sl2 = p.scale_log2;
-    float m_last = -INFINITY, l_sum = 0.f;
     bool ok = true;
-    for (int j = wg; j < n && ok; j += 2) {
-      const uint32_t u = (uint32_t)(j >> 1);
-      if (!d3b::warp_wait(&bars.s_full[wg], u & 1, abort_flag, p.err, kSiteDuSFull)) { ok = false; break; }
-      d3b::tc_fence_after();
-      float s[BN];
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c)
-        d3b::tmem_ld32(lane_addr + col_s + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
-      d3b::tmem_wait_ld();
-      d3b::tc_fence_before();
-      d3b::mbar_arrive(&bars.s_free[wg]);
-      const int kt = SPLIT ? reinterpret_cast<volatile int*>(work_s)[3] + j : j;  // key tile of the unit
-      const int valid = kt < n_s ? p.S - kt * BN : len_b - (kt - n_s) * BN;
-      if (valid < BN) {
-#pragma unroll
-        for (int c = 0; c < BN; ++c)
-          if (c >= valid) s[c] = -INFINITY;
+    int jg = 0, ie = 0;
+    Work w;
+    for (int i = 0; ok && work_item<SPLIT>(p, i, n_s, w); ++i) {
+      if (w.n == 0) {
+        if (wg == 0) zero_tile_rows<D>(p, w.b, w.g, w.tok0, quarter, lane);
+        continue;
       }
-      const float m_tile = max_n<BN>(s) * sl2;
-      float m_prev = -INFINITY;
-      if (j > 0) {
-        if (!d3b::warp_wait(&bars.mdone[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1, abort_flag, p.err, kSiteDuXMax)) {
-          ok = false;
-          break;
-        }
-        m_prev = mref_s[(j - 1) & 1][r];
-      }
-      // Lazy rescale, decided per warp: tcgen05.ld/st are warp-collective.
-      const bool rescale = __any_sync(0xffffffffu, m_tile > m_prev + kRescaleThreshold);
-      const float m_new = rescale ? fmaxf(m_prev, m_tile) : m_prev;
-      mref_s[wg][r] = m_new;
-      d3b::mbar_arrive(&bars.mdone[wg]);
-      if (rescale && j > 0) {
-        // O holds PV(0..j-1) scaled to m_prev: wait for PV(j-1), then rescale
-        if (!d3b::warp_wait(&bars.p_free[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1, abort_flag, p.err,
-                            kSiteDuPFree)) {
-          ok = false;
-          break;
-        }
+      float m_last = -INFINITY, l_sum = 0.f;
+      for (int j = (wg ^ jg) & 1; j < w.n; j += 2) {
+        const int t = jg + j;
+        const uint32_t u = (uint32_t)(t >> 1);
+        if (!d3b::warp_wait(&bars.s_full[wg], u & 1, abort_flag, p.err, kSiteDuSFull)) { ok = false; break; }
         d3b::tc_fence_after();
-        scale_cols<D>(lane_addr + C::COL_O, d3b::ex2_approx(m_prev - m_new));
-      }
-      // P[wg] is free once PV(j-2) has completed
-      if (!d3b::warp_wait(&bars.p_free[wg], (u & 1) ^ 1, abort_flag, p.err, kSiteDuPFree)) { ok = false; break; }
-      d3b::tc_fence_after();
-      float rowsum = 0.f;
+        float s[BN];
 #pragma unroll
-      for (int qq = 0; qq < BN / 32; ++qq) {
-        uint32_t pk[16];
-        rowsum += exp_row<32, FP16, D3B_POLY8>(s + qq * 32, sl2, m_new, pk);
-        d3b::tmem_st16(lane_addr + col_p + qq * 16, pk);
+        for (int c = 0; c < BN / 32; ++c)
+          d3b::tmem_ld32(lane_addr + col_s + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
+        d3b::tmem_wait_ld();
+        d3b::tc_fence_before();
+        d3b::mbar_arrive(&bars.s_free[wg]);
+        const int kt = w.a + j;  // key tile of the unit
+        const int valid = kt < n_s ? p.S - kt * BN : w.len_b - (kt - n_s) * BN;
+        if (valid < BN) {
+#pragma unroll
+          for (int c = 0; c < BN; ++c)
+            if (c >= valid) s[c] = -INFINITY;
+        }
+        const float m_tile = max_n<BN>(s) * sl2;
+        float m_prev = -INFINITY;
+        if (t > 0) {
+          if (!d3b::warp_wait(&bars.mdone[(t - 1) & 1], (uint32_t)((t - 1) >> 1) & 1, abort_flag, p.err,
+                              kSiteDuXMax)) {
+            ok = false;
+            break;
+          }
+          if (j > 0) m_prev = mref_s[(t - 1) & 1][r];
+        }
+        // Lazy rescale, decided per warp: tcgen05.ld/st are warp-collective.
+        const bool rescale = __any_sync(0xffffffffu, m_tile > m_prev + kRescaleThreshold);
+        const float m_new = rescale ? fmaxf(m_prev, m_tile) : m_prev;
+        mref_s[wg][r] = m_new;
+        d3b::mbar_arrive(&bars.mdone[wg]);
+        if (rescale && j > 0) {
+          // O holds PV(0..j-1) scaled to m_prev: wait for PV(j-1), then rescale
+          if (!d3b::warp_wait(&bars.p_free[(t - 1) & 1], (uint32_t)((t - 1) >> 1) & 1, abort_flag, p.err,
+                              kSiteDuPFree)) {
+            ok = false;
+            break;
+          }
+          d3b::tc_fence_after();
+          scale_cols<D>(lane_addr + C::COL_O, d3b::ex2_approx(m_prev - m_new));
+        }
+        // P[wg] is free once PV(t-2) has completed
+        if (!d3b::warp_wait(&bars.p_free[wg], (u & 1) ^ 1, abort_flag, p.err, kSiteDuPFree)) { ok = false; break; }
+        d3b::tc_fence_after();
+        float rowsum = 0.f;
+#pragma unroll
+        for (int qq = 0; qq < BN / 32; ++qq) {
+          uint32_t pk[16];
+          rowsum += exp_row<32, FP16, D3B_POLY8>(s + qq * 32, sl2, m_new, pk);
+          d3b::tmem_st16(lane_addr + col_p + qq * 16, pk);
+        }
+        d3b::tmem_wait_st();
+        d3b::tc_fence_before();
+        d3b::mbar_arrive(&bars.p_full[wg]);
+        l_sum = (m_last == m_new ? l_sum : l_sum * d3b::ex2_approx(m_last - m_new)) + rowsum;
+        m_last = m_new;
       }
-      d3b::tmem_wait_st();
-      d3b::tc_fence_before();
-      d3b::mbar_arrive(&bars.p_full[wg]);
-      l_sum = (m_last == m_new ? l_sum : l_sum * d3b::ex2_approx(m_last - m_new)) + rowsum;
-      m_last = m_new;
-    }
-    if (ok) ok = d3b::warp_wait(&bars.o_final, 0, abort_flag, p.err, kSiteDuFinal);
-    if (ok) {
-      lsum_s[wg][r] = l_sum;
-      mlast_s[wg][r] = m_last;
-      d3b::mbar_arrive(&bars.xsum[quarter]);
-      ok = d3b::warp_wait(&bars.xsum[quarter], 0, abort_flag, p.err, kSiteDuXMax);
-    }
-    if (ok) {
+      if (ok) ok = d3b::warp_wait(&bars.o_final, (uint32_t)ie & 1, abort_flag, p.err, kSiteDuFinal);
+      if (ok) {
+        lsum_s[wg][r] = l_sum;
+        mlast_s[wg][r] = m_last;
+        d3b::mbar_arrive(&bars.xsum[quarter]);
+        ok = d3b::warp_wait(&bars.xsum[quarter], (uint32_t)ie & 1, abort_flag, p.err, kSiteDuXMax);
+      }
+      if (!ok) break;
       d3b::tc_fence_after();
       // O is scaled to the last tile's reference, the larger of the two groups' last references
       const float m0 = mlast_s[0][r], m1 = mlast_s[1][r];
       const float m_fin = fmaxf(m0, m1);
       const float l = lsum_s[0][r] * d3b::ex2_approx(m0 - m_fin) + lsum_s[1][r] * d3b::ex2_approx(m1 - m_fin);
-      const int tok = tok0 + r / G, h = r % G;
+      const int tok = w.tok0 + r / G, h = r % G;
       const bool in_tensor = r < rows_used && tok < p.L;
-      const bool real = tok < len_b;
+      const bool real = tok < w.len_b;
       const float inv_l = 1.f / l;
       // each group normalises and stores half of the D columns (a piece of a
       // split unit writes its raw half of O, with m and l, to its slot instead)
-      uint16_t* dst_row = static_cast<uint16_t*>(p.out) + (int64_t)b * p.out_sb + (int64_t)(g * G + h) * p.out_sh +
-                          (int64_t)tok * p.out_sl + wg * C::OH;
+      uint16_t* dst_row = static_cast<uint16_t*>(p.out) + (int64_t)w.b * p.out_sb +
+                          (int64_t)(w.g * G + h) * p.out_sh + (int64_t)tok * p.out_sl + wg * C::OH;
       float* ps = nullptr;
       if constexpr (SPLIT) {
         const int slot_e = reinterpret_cast<volatile int*>(work_s)[2];
@@ -1047,61 +1131,74 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
         ps[BM * D + BM + r] = l;
       }
       if constexpr (C::OH % 32 == 0) {
-#pragma unroll 1
-        for (int c = 0; c < C::OH / 32; ++c) {
-          uint32_t o[32];
-          d3b::tmem_ld32(lane_addr + C::COL_O + wg * C::OH + c * 32, o);
-          d3b::tmem_wait_ld();
-          if (ps) {
-            uint4* os = reinterpret_cast<uint4*>(ps);
+        uint32_t o[C::OH];
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
-              os[(wg * C::OH + c * 32 + 4 * k) / 4 * BM + r] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
-          } else if (in_tensor) {
-            uint32_t w[16];
+        for (int c = 0; c < C::OH / 32; ++c)
+          d3b::tmem_ld32(lane_addr + C::COL_O + wg * C::OH + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[c * 32]));
+        d3b::tmem_wait_ld();
+        // O is in registers: the next unit's first PV may overwrite it
+        d3b::tc_fence_before();
+        d3b::mbar_arrive(&bars.o_free);
+        if (ps) {
+          uint4* os = reinterpret_cast<uint4*>(ps);
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-              w[i] = real ? pack2<FP16>(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l)
+          for (int k = 0; k < C::OH / 4; ++k)
+            os[(wg * C::OH + 4 * k) / 4 * BM + r] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+        } else if (in_tensor) {
+          uint4* dst = reinterpret_cast<uint4*>(dst_row);
+#pragma unroll
+          for (int i8 = 0; i8 < C::OH / 8; ++i8) {
+            uint32_t v[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              v[k] = real ? pack2<FP16>(__uint_as_float(o[8 * i8 + 2 * k]) * inv_l,
+                                        __uint_as_float(o[8 * i8 + 2 * k + 1]) * inv_l)
                           : 0u;
-            uint4* dst = reinterpret_cast<uint4*>(dst_row + c * 32);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            dst[i8] = make_uint4(v[0], v[1], v[2], v[3]);
           }
         }
       } else {
         uint32_t o[16];
         d3b::tmem_ld16(lane_addr + C::COL_O + wg * C::OH, o);
         d3b::tmem_wait_ld();
+        d3b::tc_fence_before();
+        d3b::mbar_arrive(&bars.o_free);
         if (ps) {
           uint4* os = reinterpret_cast<uint4*>(ps);
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             os[(wg * C::OH + 4 * k) / 4 * BM + r] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
         } else if (in_tensor) {
-          uint32_t w[8];
+          uint32_t v[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            w[i] = real ? pack2<FP16>(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l) : 0u;
+          for (int k = 0; k < 8; ++k)
+            v[k] = real ? pack2<FP16>(__uint_as_float(o[2 * k]) * inv_l, __uint_as_float(o[2 * k + 1]) * inv_l) : 0u;
           uint4* dst = reinterpret_cast<uint4*>(dst_row);
-          dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-          dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+          dst[0] = make_uint4(v[0], v[1], v[2], v[3]);
+          dst[1] = make_uint4(v[4], v[5], v[6], v[7]);
         }
       }
+      jg += w.n;
+      ++ie;
     }
-    const volatile int* wv = work_s;
-    if (SPLIT && wv[2] >= 0) {
-      const int unit_e = wv[0], end_e = wv[1];
-      // Piece of a split unit: count it in; the piece that completes the unit
-      // merges every piece's partial. Every softmax thread reaches this point
-      // exactly once (failed waits only skip work above), so the named barrier
-      // over the 256 softmax threads cannot be left waiting.
-      __threadfence();
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      if (threadIdx.x == 0) bars.last_arrival = *abort_flag ? 0 : (int)count_piece(p, unit_e - p.whole_units, end_e - wv[3]);
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      if (bars.last_arrival) {
+    if constexpr (SPLIT) {
+      const volatile int* wv = work_s;
+      if (wv[2] >= 0) {
+        const int unit_e = wv[0], end_e = wv[1];
+        const int b = unit_e / (p.tiles * p.Hkv), g = (unit_e / p.tiles) % p.Hkv, tok0 = (unit_e % p.tiles) * T;
+        // Piece of a split unit: count it in; the piece that completes the unit
+        // merges every piece's partial. Every softmax thread reaches this point
+        // exactly once (failed waits only skip work above), so the named barrier
+        // over the 256 softmax threads cannot be left waiting.
         __threadfence();
-        merge_unit<D, FP16>(p, unit_e - p.whole_units, b, g, tok0, len_b, wg, r);
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        if (threadIdx.x == 0)
+          bars.last_arrival = *abort_flag ? 0 : (int)count_piece(p, unit_e - p.whole_units, end_e - wv[3]);
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        if (bars.last_arrival) {
+          __threadfence();
+          merge_unit<D, FP16>(p, unit_e - p.whole_units, b, g, tok0, block_length(p, b), wg, r);
+        }
       }
     }
   }
@@ -1368,7 +1465,11 @@ static int prefix_bidir_impl(const void* q, const int64_t* q_strides, const void
   }
   if (ctas > 0x7FFFFFFF) return D3B_EINVAL;
   const dim3 grid((unsigned)tiles, Hkv, B);
-  const dim3 grid_dual = prm.split_units ? dim3((unsigned)ctas) : grid;
+  // D <= 128: one CTA per unit or piece in a split launch, else a persistent
+  // grid of at most one CTA per SM looping over the units
+  const int64_t sms = d3b_host::num_sms(d3b_host::current_device());
+  const dim3 grid_dual = prm.split_units ? dim3((unsigned)ctas)
+                                         : dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(units, sms)));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   return dtype == D3B_F16 ? dispatch<1>(D, maps, prm, grid, grid_dual, s)
                           : dispatch<0>(D, maps, prm, grid, grid_dual, s);

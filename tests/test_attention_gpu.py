@@ -272,3 +272,34 @@ def test_workspace_shared_by_shapes():
         ref = oattn.questions(q, ks, vs, kq, vq, lens, D**-0.5, dtype=torch.float32)
         assert float((out.float().cpu() - ref).abs().max()) <= TOL, (B, S)
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("B,H,Hkv,S,L,D,dtype,seed", [(300, 4, 2, 200, 40, 32, torch.bfloat16, 41),
+                                                       (64, 16, 4, 1000, 260, 64, torch.float16, 42),
+                                                       (150, 8, 8, 300, 130, 128, torch.bfloat16, 43)])
+def test_persistent_units_ragged_against_oracle(B, H, Hkv, S, L, D, dtype, seed):
+    """More units than SMs, so every CTA of the persistent launch walks several
+    units: empty blocks (units with no key tile) between full ones, blocks of
+    one to three own key tiles (units of different lengths in one CTA's
+    sequence), an odd number of key tiles per unit (the softmax groups swap
+    roles from one unit to the next), fp16, G in {1, 2, 4}. Two launches give
+    the same bits."""
+    g = torch.Generator().manual_seed(seed)
+    q = _rand((B, H, L, D), g, dtype)
+    ks, vs = _rand((Hkv, S, D), g, dtype), _rand((Hkv, S, D), g, dtype)
+    kq, vq = _rand((B, Hkv, L, D), g, dtype), _rand((B, Hkv, L, D), g, dtype)
+    lens = torch.randint(0, L + 1, (B,), generator=g)
+    lens[::7] = 0
+    lens[1::5] = L
+    lens = lens.tolist()
+    args = (q.to(DEV), ks.to(DEV), vs.to(DEV), kq.to(DEV), vq.to(DEV), lens)
+    out = pb.prefix_bidir_attention(*args, scale=D**-0.5)
+    out_again = pb.prefix_bidir_attention(*args, scale=D**-0.5)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    assert torch.equal(out, out_again)
+    ref = oattn.questions(q, ks, vs, kq, vq, lens, D**-0.5, dtype=torch.float32)
+    got = out.float().cpu()
+    assert float((got - ref).abs().max()) <= TOL
+    for b, n in enumerate(lens):
+        assert bool((got[b, :, n:] == 0).all())
