@@ -80,6 +80,7 @@ SIGNATURES: list[tuple[str, Any, list[Any]]] = [
          _I, _I, _I, _I, _I, _I, _I, _F, _I, _I, _VP, _SZ, _VP],
     ),
     ("d3b_gated_delta_workspace_size", _SZ, [_I, _I, _I]),
+    ("d3b_gated_delta_state_workspace_size", _SZ, [_I, _I, _I, _I, _I]),
     ("d3b_copy_segments", _I, [ctypes.POINTER(CopySegment), _I, _VP]),
     ("d3b_arena_create", _I, [_U64, _U64, ctypes.POINTER(ctypes.c_void_p)]),
     ("d3b_arena_alloc", _I, [_VP, _U64, _U64P]),

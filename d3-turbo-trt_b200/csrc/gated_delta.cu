@@ -748,12 +748,690 @@ int launch_chunk(const GdrParams& p, int beta_dtype, uint8_t* s0_tiles, cudaStre
   }
 }
 
+// ---------------------------------------------------------------------------
+// Chunked form for long sequences (the state pass: one row of thousands of
+// tokens with a final state; FLA's chunk_gated_delta_rule, the reference's
+// path for it, d3trt/model/ops.py:287-324). Chunks of 64 tokens; gamma is the
+// running sum of g inside a chunk, gL its last value. WY form per chunk, with
+// the state S_c entering the chunk:
+//   A   = strictly-lower( beta_i (k_i . k_j) e^(gamma_i - gamma_j) ),  T = (I + A)^-1
+//   W   = T diag(beta e^gamma) K,   U = T diag(beta) V                  (state-free)
+//   V'  = U - W S_c
+//   S_{c+1} = e^gL S_c + K^T diag(e^(gL - gamma)) V'
+//   O   = e^gamma (Q S_c) + lower-incl( (q_i . k_j) e^(gamma_i - gamma_j) ) V'
+// Two kernels. gdr_state_prep_kernel (parallel over row x chunk pair x value
+// head, persistent) forms everything that does not depend on the state: the
+// products K K^T and Q K^T, A, T (forward substitution, one thread per row of
+// T), W and U (tcgen05, T as a block-diagonal A operand), and writes each
+// chunk's operand tiles to a workspace in the exact shared-memory layouts the
+// second kernel's MMAs read. gdr_state_scan_kernel (one CTA per row x value
+// head x 64 state columns) carries the state through the chunks in fp32
+// registers (one thread per state row); per chunk three tcgen05 products:
+//   [W; Q] S_c (M = 128: rows 0-63 W, 64-127 Q)   K^T (e^(gL-gamma) V')   P V'
+// with the chunk's tiles double-buffered by bulk copies. Numerics follow FLA's
+// chunked kernels: bf16 operands (T, W, U, V', the state image), fp32
+// accumulation, fp32 state.
+// ---------------------------------------------------------------------------
+namespace gds {
+
+using gdc::CHUNK;
+using gdc::KD;
+using gdc::M;
+using gdc::TILE;
+using gdc::sw_off;
+
+// ---- workspace: one record per (row, value head, chunk) ----
+constexpr int WS_WQ = 0;       // [128 x 128] K-major SW128: rows 0-63 W, rows 64-127 q (normalised, scaled)
+constexpr int WS_KH = 32768;   // k (normalised) as the MN-major [M = 128 state rows x K = 64 tokens] operand
+constexpr int WS_P = 49152;    // P, [64 x 64] K-major SW128 (rows 64-127 of the scan's [128 x 64] operand)
+constexpr int WS_U = 57344;    // U, two [64 tokens x 64 columns] halves, rows of 8 granules at g ^ (token % 8)
+constexpr int WS_G = 73728;    // gamma, 64 floats
+constexpr int WS_CHUNK = 74752;
+
+// ---- prep kernel ----
+constexpr int P_THREADS = 256;
+constexpr int P_OFF_KN = 0, P_OFF_QN = TILE, P_OFF_KB = 2 * TILE, P_OFF_VB = 3 * TILE, P_OFF_T = 4 * TILE;
+constexpr int P_OFF_P = 5 * TILE, P_OFF_A = 5 * TILE + 16384;
+constexpr int P_A_STRIDE = 68;  // fp32 row stride of A (row-major)
+constexpr int P_SMEM_BYTES = P_OFF_A + M * P_A_STRIDE * 4 + 1024;
+constexpr uint32_t P_TMEM_COLS = 512;
+constexpr int P_COL_KK = 0, P_COL_QK = 128, P_COL_W = 256, P_COL_U = 384;
+
+enum : int { kSitePrepLoad = 3101, kSitePrepMma1 = 3102, kSitePrepMma2 = 3103, kSitePrepDrain = 3104,
+             kSiteScanFull = 3111, kSiteScanH = 3112, kSiteScanX = 3113, kSiteScanV = 3114, kSiteScanHV = 3115,
+             kSiteScanEmpty = 3116, kSiteScanDrain = 3117 };
+
+struct PBars {
+  uint64_t load, mma1, mma2, drain;
+  uint32_t tmem_slot;
+  int abort_flag;
+  alignas(16) float gam[M];  // gamma per row (bulk-copied out per chunk: 16-byte aligned)
+  float beta[M];
+};
+
+__device__ __forceinline__ uint4 pack8_bf16(const float* f) {
+  return make_uint4(gdc::pack2<__nv_bfloat16>(f[0], f[1]), gdc::pack2<__nv_bfloat16>(f[2], f[3]),
+                    gdc::pack2<__nv_bfloat16>(f[4], f[5]), gdc::pack2<__nv_bfloat16>(f[6], f[7]));
+}
+
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(d3b::smem_u32(src)),
+               "r"(bytes)
+               : "memory");
+}
+
+// Waits (bounded, ignoring the abort flag) for a phase of a barrier that bulk
+// copies complete, so a CTA that gave up does not exit with copies into its
+// shared memory in flight.
+__device__ __forceinline__ void settle(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = d3b::smem_u32(bar);
+  const uint64_t t0 = d3b::globaltimer_ns();
+  while (!d3b::mbar_try_wait(addr, parity))
+    if (d3b::globaltimer_ns() - t0 > D3B_WAIT_LIMIT_NS) break;
+}
+
+template <typename In, typename BetaT>
+__global__ void __launch_bounds__(P_THREADS, 1)
+    gdr_state_prep_kernel(const __grid_constant__ GdrParams p, uint8_t* ws, int NC, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ PBars bars;
+  __shared__ float part[2][2][M];  // [q, k][column half][row] partial sums of squares
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = tid & (M - 1), half = tid >> 7;  // row phases: one row, 64 of its 128 columns
+  const int blk = row >> 6, tl = row & 63;        // the row's token tl of chunk blk of the pair
+  volatile int* abort_flag = &bars.abort_flag;
+  const int c0 = half * 64;
+  const int npairs = (NC + 1) / 2, n_items = p.B * npairs * p.HV;
+
+  if (tid == 0) {
+    d3b::mbar_init(&bars.load, P_THREADS);
+    d3b::mbar_init(&bars.mma1, 1);
+    d3b::mbar_init(&bars.mma2, 1);
+    d3b::mbar_init(&bars.drain, 1);
+    bars.abort_flag = 0;
+    d3b::fence_barrier_init();
+  }
+  if (warp == 0) d3b::tmem_alloc(&bars.tmem_slot, P_TMEM_COLS);
+  d3b::tc_fence_before();
+  __syncthreads();
+  d3b::tc_fence_after();
+  const uint32_t tmem = bars.tmem_slot;
+  const uint32_t s_base = d3b::smem_u32(smem);
+  const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+  auto gx = [&](int x) { return (x + row) & 7; };  // row-rotated granule order (conflict-free row reads)
+  bool alive = true;
+  int it = 0;
+#pragma unroll 1
+  for (int item = blockIdx.x; item < n_items && alive; item += gridDim.x, ++it) {
+    const uint32_t ph = (uint32_t)it & 1u;
+    // value heads fastest: the items of one q/k head follow each other (q/k rows reused from L2)
+    const int hv = item % p.HV, pair = (item / p.HV) % npairs, b = item / (p.HV * npairs);
+    const int h = hv / (p.HV / p.H);
+    const int chunk = pair * 2 + blk, tok = chunk * 64 + tl;
+    const bool valid = tok < p.T;
+    // ---- phase 1: raw q, k, v rows (256 B each) by bulk copies into the regions their
+    // normalised tiles later take (every thread reads its row into registers first)
+    uint8_t* stage_q = smem + P_OFF_QN;
+    uint8_t* stage_k = smem + P_OFF_KN;
+    uint8_t* stage_v = smem + P_OFF_VB;
+    if (half == 0 && !valid) {  // padding rows: zeros (beta = g = 0: they add nothing)
+#pragma unroll
+      for (int x = 0; x < 16; ++x) {
+        reinterpret_cast<uint4*>(stage_q + row * 256)[x] = make_uint4(0, 0, 0, 0);
+        reinterpret_cast<uint4*>(stage_k + row * 256)[x] = make_uint4(0, 0, 0, 0);
+        reinterpret_cast<uint4*>(stage_v + row * 256)[x] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    __syncthreads();  // the previous item's shared-memory users (and its copies out) are done
+    d3b::fence_proxy_async_smem();
+    if (half == 0 && valid) {
+      d3b::mbar_arrive_expect_tx(&bars.load, 3 * 256);
+      gdc::bulk_load(stage_q + row * 256,
+                     static_cast<const In*>(p.q) + b * p.qs[0] + (long long)tok * p.qs[1] + h * p.qs[2], 256,
+                     &bars.load);
+      gdc::bulk_load(stage_k + row * 256,
+                     static_cast<const In*>(p.k) + b * p.ks[0] + (long long)tok * p.ks[1] + h * p.ks[2], 256,
+                     &bars.load);
+      gdc::bulk_load(stage_v + row * 256,
+                     static_cast<const In*>(p.v) + b * p.vs[0] + (long long)tok * p.vs[1] + hv * p.vs[2], 256,
+                     &bars.load);
+    } else {
+      d3b::mbar_arrive(&bars.load);
+    }
+    if (half == 0) {
+      bars.gam[row] = valid ? p.g[b * p.gs[0] + (long long)tok * p.gs[1] + hv * p.gs[2]] : 0.f;
+      bars.beta[row] = valid ? to_f32(static_cast<const BetaT*>(p.beta)[b * p.bs[0] + (long long)tok * p.bs[1] +
+                                                                       hv * p.bs[2]])
+                             : 0.f;
+    }
+    bool ok = d3b::warp_wait(&bars.load, ph, abort_flag, err, kSitePrepLoad);
+    uint4 rq[8], rk[8], rv[8];  // rq[x] holds columns c0 + gx(x) * 8 .. + 7
+#pragma unroll
+    for (int x = 0; x < 8; ++x) {
+      rq[x] = reinterpret_cast<const uint4*>(stage_q + row * 256 + half * 128)[gx(x)];
+      rk[x] = reinterpret_cast<const uint4*>(stage_k + row * 256 + half * 128)[gx(x)];
+      rv[x] = reinterpret_cast<const uint4*>(stage_v + row * 256 + half * 128)[gx(x)];
+    }
+    {
+      float sq = 0.f, sk = 0.f;
+#pragma unroll
+      for (int x = 0; x < 8; ++x) {
+        float fq[8], fk[8];
+        gdc::unpack8<In>(rq[x], fq);
+        gdc::unpack8<In>(rk[x], fk);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          sq = fmaf(fq[e], fq[e], sq);
+          sk = fmaf(fk[e], fk[e], sk);
+        }
+      }
+      part[0][half][row] = sq;
+      part[1][half][row] = sk;
+    }
+    __syncthreads();  // raw rows are in registers; partial sums and raw g visible
+    float gam = 0.f;
+    for (int s = blk * 64; s <= row; ++s) gam += bars.gam[s];
+    const float sq = part[0][0][row] + part[0][1][row], sk = part[1][0][row] + part[1][1][row];
+    const float iq = (p.l2norm ? 1.f / sqrtf(sq + 1e-6f) : 1.f) * p.scale;
+    const float ik = p.l2norm ? 1.f / sqrtf(sk + 1e-6f) : 1.f;
+    __syncthreads();  // every thread has read the raw g values
+    if (half == 0) bars.gam[row] = gam;
+    {
+      const float bt = bars.beta[row], bte = bt * __expf(gam);
+#pragma unroll
+      for (int x = 0; x < 8; ++x) {
+        float fq[8], fk[8], fv[8], kb[8], vb[8];
+        gdc::unpack8<In>(rq[x], fq);
+        gdc::unpack8<In>(rk[x], fk);
+        gdc::unpack8<In>(rv[x], fv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          fq[e] *= iq;
+          fk[e] = __bfloat162float(__float2bfloat16_rn(fk[e] * ik));  // the bf16 k every product uses
+          kb[e] = fk[e] * bte;
+          vb[e] = fv[e] * bt;
+        }
+        const uint32_t off = sw_off(row, c0 + gx(x) * 8);
+        *reinterpret_cast<uint4*>(smem + P_OFF_QN + off) = pack8_bf16(fq);
+        *reinterpret_cast<uint4*>(smem + P_OFF_KN + off) = pack8_bf16(fk);
+        *reinterpret_cast<uint4*>(smem + P_OFF_KB + off) = pack8_bf16(kb);
+        *reinterpret_cast<uint4*>(smem + P_OFF_VB + off) = pack8_bf16(vb);
+      }
+    }
+    d3b::fence_proxy_async_smem();
+    d3b::tc_fence_before();
+    __syncthreads();
+    d3b::tc_fence_after();
+
+    // ---- phase 2: K K^T, Q K^T ------------------------------------------------
+    if (tid == 0 && ok) {
+      constexpr uint32_t id_kk = d3b::make_idesc(1, 1, 1, 0, 0, M, KD);
+#pragma unroll
+      for (int k = 0; k < KD / 16; ++k) {
+        const uint32_t koff = (uint32_t)((k >> 2) * CHUNK + (k & 3) * 32);
+        const uint64_t a_k = d3b::make_smem_desc(s_base + P_OFF_KN + koff, 16, 1024, d3b::kLayoutSW128);
+        const uint64_t a_q = d3b::make_smem_desc(s_base + P_OFF_QN + koff, 16, 1024, d3b::kLayoutSW128);
+        d3b::mma_f16_ss(tmem + P_COL_KK, a_k, a_k, id_kk, k > 0);
+        d3b::mma_f16_ss(tmem + P_COL_QK, a_q, a_k, id_kk, k > 0);
+      }
+      d3b::mma_commit(&bars.mma1);
+    }
+    if (ok) ok = d3b::warp_wait(&bars.mma1, ph, abort_flag, err, kSitePrepMma1);
+    d3b::tc_fence_after();
+
+    // ---- phase 3 (row, column half of the own chunk): A (row-major fp32) and P (bf16) --
+    float* Am = reinterpret_cast<float*>(smem + P_OFF_A);
+    if (ok) {
+      const float beta_i = bars.beta[row];
+      const int jl0 = half * 32;
+      uint32_t r[32];
+      d3b::tmem_ld32(lane_addr + P_COL_KK + blk * 64 + jl0, r);
+      d3b::tmem_wait_ld();
+#pragma unroll
+      for (int x = 0; x < 32; x += 4) {
+        float4 a4;
+        float* af = reinterpret_cast<float*>(&a4);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int jl = jl0 + x + e;
+          af[e] = jl < tl ? beta_i * __uint_as_float(r[x + e]) * __expf(gam - bars.gam[blk * 64 + jl]) : 0.f;
+        }
+        *reinterpret_cast<float4*>(Am + row * P_A_STRIDE + jl0 + x) = a4;
+      }
+      d3b::tmem_ld32(lane_addr + P_COL_QK + blk * 64 + jl0, r);
+      d3b::tmem_wait_ld();
+#pragma unroll
+      for (int x = 0; x < 32; x += 8) {
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int jl = jl0 + x + e;
+          f[e] = jl <= tl ? __uint_as_float(r[x + e]) * __expf(gam - bars.gam[blk * 64 + jl]) : 0.f;
+        }
+        const int g8 = (jl0 + x) >> 3;
+        *reinterpret_cast<uint4*>(smem + P_OFF_P + row * 128 + ((g8 ^ (row & 7)) << 4)) = pack8_bf16(f);
+      }
+    }
+    __syncthreads();  // A and P complete
+
+    // ---- phase 4: T = (I + A)^-1, one thread per row of T (threads 0-127) ----------
+    // Row i of T solves x (I + A) = e_i from the right: going down from m = 63, x_m
+    // is final once every later row has been subtracted, then x_j -= x_m A[m][j]
+    // for j < m. Every thread runs the same unrolled steps (rows m > i give x_m = 0),
+    // so all lanes read the same A row at the same time (a broadcast).
+    if (ok && tid < M) {
+      float x[64];
+#pragma unroll
+      for (int m = 0; m < 64; ++m) x[m] = m == tl ? 1.f : 0.f;
+      const float* Ab = Am + blk * 64 * P_A_STRIDE;
+#pragma unroll
+      for (int m = 63; m >= 1; --m) {
+        const float xm = x[m];
+        const float* arow = Ab + m * P_A_STRIDE;
+#pragma unroll
+        for (int j = 0; j < (m & ~3); j += 4) {
+          const float4 a4 = *reinterpret_cast<const float4*>(arow + j);
+          x[j] = fmaf(-a4.x, xm, x[j]);
+          x[j + 1] = fmaf(-a4.y, xm, x[j + 1]);
+          x[j + 2] = fmaf(-a4.z, xm, x[j + 2]);
+          x[j + 3] = fmaf(-a4.w, xm, x[j + 3]);
+        }
+#pragma unroll
+        for (int j = m & ~3; j < m; ++j) x[j] = fmaf(-arow[j], xm, x[j]);
+      }
+#pragma unroll
+      for (int x8 = 0; x8 < 8; ++x8)
+        *reinterpret_cast<uint4*>(smem + P_OFF_T + sw_off(row, blk * 64 + x8 * 8)) = pack8_bf16(x + x8 * 8);
+    } else if (ok) {
+      // T is block-diagonal: zeros in the other chunk's 64 columns of row tid - 128
+      const int r2 = tid - M, ob = 1 - (r2 >> 6);
+#pragma unroll
+      for (int x8 = 0; x8 < 8; ++x8)
+        *reinterpret_cast<uint4*>(smem + P_OFF_T + sw_off(r2, ob * 64 + x8 * 8)) = make_uint4(0, 0, 0, 0);
+    }
+    d3b::fence_proxy_async_smem();
+    d3b::tc_fence_before();
+    __syncthreads();
+    d3b::tc_fence_after();
+
+    // ---- phase 5: W = T (beta e^gamma K), U = T (beta V) -------------------------
+    if (tid == 0 && ok) {
+      constexpr uint32_t id_w = d3b::make_idesc(1, 1, 1, 0, 1, M, KD);  // B MN-major
+#pragma unroll
+      for (int k = 0; k < M / 16; ++k) {
+        const uint32_t koff = (uint32_t)((k >> 2) * CHUNK + (k & 3) * 32);
+        const uint64_t a_t = d3b::make_smem_desc(s_base + P_OFF_T + koff, 16, 1024, d3b::kLayoutSW128);
+        const uint64_t b_k = d3b::make_smem_desc(s_base + P_OFF_KB + k * 16 * 128, CHUNK, 1024, d3b::kLayoutSW128);
+        const uint64_t b_v = d3b::make_smem_desc(s_base + P_OFF_VB + k * 16 * 128, CHUNK, 1024, d3b::kLayoutSW128);
+        d3b::mma_f16_ss(tmem + P_COL_W, a_t, b_k, id_w, k > 0);
+        d3b::mma_f16_ss(tmem + P_COL_U, a_t, b_v, id_w, k > 0);
+      }
+      d3b::mma_commit(&bars.mma2);
+    }
+    if (ok) ok = d3b::warp_wait(&bars.mma2, ph, abort_flag, err, kSitePrepMma2);
+    d3b::tc_fence_after();
+
+    // ---- phase 6 (row, column half): W as bf16 into the dead KB tile (K-major), U as
+    // bf16 rows into the dead VB tile ([chunk][column half][token][64]) -----------
+    if (ok) {
+      uint32_t r[64];
+      d3b::tmem_ld32(lane_addr + P_COL_W + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+      d3b::tmem_ld32(lane_addr + P_COL_W + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      d3b::tmem_wait_ld();
+#pragma unroll
+      for (int x = 0; x < 8; ++x) {
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[x * 8 + e]);
+        *reinterpret_cast<uint4*>(smem + P_OFF_KB + sw_off(row, c0 + x * 8)) = pack8_bf16(f);
+      }
+      d3b::tmem_ld32(lane_addr + P_COL_U + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+      d3b::tmem_ld32(lane_addr + P_COL_U + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      d3b::tmem_wait_ld();
+      uint8_t* urow = smem + P_OFF_VB + ((blk * 2 + half) * 64 + tl) * 128;
+#pragma unroll
+      for (int x = 0; x < 8; ++x) {  // granule x of the row at x ^ (token % 8): conflict-free on both sides
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[x * 8 + e]);
+        *reinterpret_cast<uint4*>(urow + ((x ^ (tl & 7)) << 4)) = pack8_bf16(f);
+      }
+    }
+    d3b::fence_proxy_async_smem();
+    __syncthreads();
+    // ---- copies out: ten per chunk, one per thread --------------------------------
+    if (ok && tid < 20) {
+      const int cb = tid / 10, which = tid % 10;
+      const int chunk_c = pair * 2 + cb;
+      if (chunk_c < NC) {
+        uint8_t* dst = ws + (((size_t)b * p.HV + hv) * NC + chunk_c) * WS_CHUNK;
+        const uint8_t* src = nullptr;
+        uint32_t bytes = 8192;
+        switch (which) {
+          case 0: dst += WS_WQ; src = smem + P_OFF_KB + cb * 8192; break;                     // W, columns 0-63
+          case 1: dst += WS_WQ + 8192; src = smem + P_OFF_QN + cb * 8192; break;              // q, columns 0-63
+          case 2: dst += WS_WQ + 16384; src = smem + P_OFF_KB + CHUNK + cb * 8192; break;     // W, columns 64-127
+          case 3: dst += WS_WQ + 24576; src = smem + P_OFF_QN + CHUNK + cb * 8192; break;     // q, columns 64-127
+          case 4: dst += WS_KH; src = smem + P_OFF_KN + cb * 8192; break;                     // k, state rows 0-63
+          case 5: dst += WS_KH + 8192; src = smem + P_OFF_KN + CHUNK + cb * 8192; break;      // k, state rows 64-127
+          case 6: dst += WS_P; src = smem + P_OFF_P + cb * 8192; break;
+          case 7: dst += WS_U; src = smem + P_OFF_VB + (cb * 2) * 8192; break;
+          case 8: dst += WS_U + 8192; src = smem + P_OFF_VB + (cb * 2 + 1) * 8192; break;
+          default: dst += WS_G; src = reinterpret_cast<const uint8_t*>(&bars.gam[cb * 64]); bytes = 256; break;
+        }
+        bulk_store(dst, src, bytes);
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // the staging may be reused
+      }
+    }
+    d3b::tc_fence_before();
+    alive = __syncthreads_and(ok) != 0;
+    d3b::tc_fence_after();
+    if (!alive) settle(&bars.load, ph);  // no load copy of this item is left in flight
+  }
+
+  // ---- teardown: every copy out and every MMA has completed -------------------
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  if (tid == 0) {
+    d3b::mma_commit(&bars.drain);
+    const uint32_t addr = d3b::smem_u32(&bars.drain);
+    const uint64_t t0 = d3b::globaltimer_ns();
+    while (!d3b::mbar_try_wait(addr, 0)) {
+      if (d3b::globaltimer_ns() - t0 > D3B_WAIT_LIMIT_NS) {
+        d3b::record_device_error(err, kSitePrepDrain);
+        break;
+      }
+    }
+  }
+  d3b::tc_fence_before();
+  __syncthreads();
+  d3b::tc_fence_after();
+  if (warp == 0) d3b::tmem_dealloc(tmem, P_TMEM_COLS);
+}
+
+// ---- scan kernel ----
+constexpr int R_THREADS = 192;  // warps 0-3: state rows (TMEM lanes 0-127); warp 4: copies; warp 5: MMAs
+constexpr int R_VC = 64;        // state columns per CTA
+constexpr int ST_WQ = 0, ST_KH = 32768, ST_PZ = 49152, ST_U = 65536, ST_G = 73728, R_STAGE = 74752;
+constexpr int R_OFF_HB = 2 * R_STAGE, R_OFF_VB = R_OFF_HB + 16384, R_OFF_VD = R_OFF_VB + 8192;
+constexpr int R_SMEM_BYTES = R_OFF_VD + 8192 + 1024;
+constexpr uint32_t R_STAGE_TX = 32768 + 16384 + 8192 + 8192 + 256;
+constexpr uint32_t R_TMEM_COLS = 256;
+constexpr int R_COL_X = 0, R_COL_D = 64, R_COL_O = 128;
+
+struct RBars {
+  uint64_t full[2], empty[2];
+  uint64_t h_ready;   // the state image of this chunk is in shared memory (128 row threads)
+  uint64_t x_ready;   // [W; Q] S_c is in TMEM
+  uint64_t v_ready;   // V' and its decayed copy are in shared memory (64 token threads)
+  uint64_t hv_ready;  // K^T V'' and P V' are in TMEM; the state image and V' tiles are free
+  uint64_t drain;
+  uint32_t tmem_slot;
+  int abort_flag;
+};
+
+template <typename In>
+__global__ void __launch_bounds__(R_THREADS, 1)
+    gdr_state_scan_kernel(const __grid_constant__ GdrParams p, const uint8_t* ws, int NC, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ RBars bars;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int half = (int)(blockIdx.x & 1), bh = (int)(blockIdx.x >> 1);
+  const int hv = bh % p.HV, b = bh / p.HV;
+  const int c0 = half * R_VC;
+  const uint8_t* wsh = ws + ((size_t)b * p.HV + hv) * (size_t)NC * WS_CHUNK;
+  volatile int* abort_flag = &bars.abort_flag;
+  if (tid == 0) {
+    for (int s = 0; s < 2; ++s) {
+      d3b::mbar_init(&bars.full[s], 1);
+      d3b::mbar_init(&bars.empty[s], 1);
+    }
+    d3b::mbar_init(&bars.h_ready, 128);
+    d3b::mbar_init(&bars.x_ready, 1);
+    d3b::mbar_init(&bars.v_ready, 64);
+    d3b::mbar_init(&bars.hv_ready, 1);
+    d3b::mbar_init(&bars.drain, 1);
+    bars.abort_flag = 0;
+    d3b::fence_barrier_init();
+  }
+  // rows 0-63 of each stage's P operand stay zero (rows 64-127 are P)
+  for (int i = tid; i < 2 * 512; i += R_THREADS)
+    reinterpret_cast<uint4*>(smem + (i >> 9) * R_STAGE + ST_PZ)[i & 511] = make_uint4(0, 0, 0, 0);
+  d3b::fence_proxy_async_smem();
+  if (warp == 5) d3b::tmem_alloc(&bars.tmem_slot, R_TMEM_COLS);
+  d3b::tc_fence_before();
+  __syncthreads();
+  d3b::tc_fence_after();
+  const uint32_t tmem = bars.tmem_slot;
+  const uint32_t s_base = d3b::smem_u32(smem);
+
+  if (warp == 4) {
+    // ================= copies: chunk c's tiles into stage c % 2 =================
+    if (lane == 0) {
+      int c = 0;
+      for (; c < NC; ++c) {
+        const int s = c & 1;
+        if (!d3b::mbar_wait(&bars.empty[s], ((uint32_t)(c >> 1) & 1) ^ 1, abort_flag, err, kSiteScanEmpty)) break;
+        uint8_t* st = smem + s * R_STAGE;
+        const uint8_t* src = wsh + (size_t)c * WS_CHUNK;
+        d3b::mbar_arrive_expect_tx(&bars.full[s], R_STAGE_TX);
+        gdc::bulk_load(st + ST_WQ, src + WS_WQ, 32768, &bars.full[s]);
+        gdc::bulk_load(st + ST_KH, src + WS_KH, 16384, &bars.full[s]);
+        gdc::bulk_load(st + ST_PZ + 8192, src + WS_P, 8192, &bars.full[s]);
+        gdc::bulk_load(st + ST_U, src + WS_U + half * 8192, 8192, &bars.full[s]);
+        gdc::bulk_load(st + ST_G, src + WS_G, 256, &bars.full[s]);
+      }
+      // the last two stages' copies have landed before the CTA can leave (after an abort too)
+      for (int cc = c - 2 < 0 ? 0 : c - 2; cc < c; ++cc) settle(&bars.full[cc & 1], (uint32_t)(cc >> 1) & 1);
+    }
+  } else if (warp == 5) {
+    // ================= MMA issuer =================
+    if (lane == 0) {
+      constexpr uint32_t id_x = d3b::make_idesc(1, 1, 1, 0, 1, M, R_VC);  // [W; Q] K-major, S image MN-major
+      constexpr uint32_t id_d = d3b::make_idesc(1, 1, 1, 1, 1, M, R_VC);  // K^T: A MN-major
+      constexpr uint32_t id_o = d3b::make_idesc(1, 1, 1, 0, 1, M, R_VC);  // [0; P] K-major
+      for (int c = 0; c < NC; ++c) {
+        const int s = c & 1;
+        const uint32_t pc = (uint32_t)c & 1;
+        const uint32_t st = s_base + s * R_STAGE;
+        if (!d3b::mbar_wait(&bars.full[s], (uint32_t)(c >> 1) & 1, abort_flag, err, kSiteScanFull)) break;
+        if (!d3b::mbar_wait(&bars.h_ready, pc, abort_flag, err, kSiteScanH)) break;
+        d3b::tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < KD / 16; ++k) {
+          const uint64_t a = d3b::make_smem_desc(st + ST_WQ + (k >> 2) * CHUNK + (k & 3) * 32, 16, 1024,
+                                                 d3b::kLayoutSW128);
+          const uint64_t bd = d3b::make_smem_desc(s_base + R_OFF_HB + k * 2048, 16384, 1024, d3b::kLayoutSW128);
+          d3b::mma_f16_ss(tmem + R_COL_X, a, bd, id_x, k > 0);
+        }
+        d3b::mma_commit(&bars.x_ready);
+        if (!d3b::mbar_wait(&bars.v_ready, pc, abort_flag, err, kSiteScanV)) break;
+        d3b::tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 64 / 16; ++k) {
+          const uint64_t a_k = d3b::make_smem_desc(st + ST_KH + k * 2048, 8192, 1024, d3b::kLayoutSW128);
+          const uint64_t b_vd = d3b::make_smem_desc(s_base + R_OFF_VD + k * 2048, 8192, 1024, d3b::kLayoutSW128);
+          d3b::mma_f16_ss(tmem + R_COL_D, a_k, b_vd, id_d, k > 0);
+        }
+#pragma unroll
+        for (int k = 0; k < 64 / 16; ++k) {
+          const uint64_t a_p = d3b::make_smem_desc(st + ST_PZ + k * 32, 16, 1024, d3b::kLayoutSW128);
+          const uint64_t b_vb = d3b::make_smem_desc(s_base + R_OFF_VB + k * 2048, 8192, 1024, d3b::kLayoutSW128);
+          d3b::mma_f16_ss(tmem + R_COL_O, a_p, b_vb, id_o, k > 0);
+        }
+        d3b::mma_commit(&bars.hv_ready);
+        d3b::mma_commit(&bars.empty[s]);
+      }
+      d3b::mma_commit(&bars.drain);
+      const uint32_t addr = d3b::smem_u32(&bars.drain);
+      const uint64_t t0 = d3b::globaltimer_ns();
+      while (!d3b::mbar_try_wait(addr, 0)) {
+        if (d3b::globaltimer_ns() - t0 > D3B_WAIT_LIMIT_NS) {
+          d3b::record_device_error(err, kSiteScanDrain);
+          break;
+        }
+      }
+    }
+  } else {
+    // ================= state rows (thread i = state row i = TMEM lane i) =================
+    const int i = tid;
+    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+    float hs[R_VC];
+    if (p.h0) {
+      const float* src = p.h0 + b * p.h0s[0] + hv * p.h0s[1] + (long long)i * p.h0s[2] + c0;
+#pragma unroll
+      for (int j = 0; j < R_VC; ++j) hs[j] = src[j];
+    } else {
+#pragma unroll
+      for (int j = 0; j < R_VC; ++j) hs[j] = 0.f;
+    }
+    const int t = i & 63;  // warps 0-1: token t's V' row; warps 2-3: token t's output row
+    bool ok = true;
+    for (int c = 0; c < NC; ++c) {
+      const int s = c & 1;
+      const uint32_t pc = (uint32_t)c & 1;
+      const uint8_t* st = smem + s * R_STAGE;
+      if (!(ok = d3b::warp_wait(&bars.full[s], (uint32_t)(c >> 1) & 1, abort_flag, err, kSiteScanFull))) break;
+      // the chunk's gammas, read before h_ready (after it the stage may be refilled)
+      const float gl = reinterpret_cast<const float*>(st + ST_G)[63];
+      const float gt = reinterpret_cast<const float*>(st + ST_G)[t];
+      // the state image S_c (bf16, MN-major [K = state rows x N = 64 columns])
+#pragma unroll
+      for (int x8 = 0; x8 < 8; ++x8)
+        *reinterpret_cast<uint4*>(smem + R_OFF_HB + i * 128 + ((x8 ^ (i & 7)) << 4)) = pack8_bf16(hs + x8 * 8);
+      d3b::fence_proxy_async_smem();
+      d3b::tc_fence_before();
+      d3b::mbar_arrive(&bars.h_ready);
+      if (!(ok = d3b::warp_wait(&bars.x_ready, pc, abort_flag, err, kSiteScanX))) break;
+      d3b::tc_fence_after();
+      if (warp < 2) {
+        // V' = U - W S_c for token t; V'' = e^(gL - gamma_t) V' for the state update
+        uint32_t xr[64];
+        d3b::tmem_ld32(lane_addr + R_COL_X, *reinterpret_cast<uint32_t(*)[32]>(&xr[0]));
+        d3b::tmem_ld32(lane_addr + R_COL_X + 32, *reinterpret_cast<uint32_t(*)[32]>(&xr[32]));
+        d3b::tmem_wait_ld();
+        const float dk = __expf(gl - gt);
+#pragma unroll
+        for (int x8 = 0; x8 < 8; ++x8) {
+          const uint32_t off = t * 128 + ((x8 ^ (t & 7)) << 4);  // U rows arrive in the same swizzle
+          float fu[8], vn[8], vd[8];
+          gdc::unpack8<__nv_bfloat16>(*reinterpret_cast<const uint4*>(st + ST_U + off), fu);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            vn[e] = fu[e] - __uint_as_float(xr[x8 * 8 + e]);
+            vd[e] = vn[e] * dk;
+          }
+          *reinterpret_cast<uint4*>(smem + R_OFF_VB + off) = pack8_bf16(vn);
+          *reinterpret_cast<uint4*>(smem + R_OFF_VD + off) = pack8_bf16(vd);
+        }
+        d3b::fence_proxy_async_smem();
+        d3b::tc_fence_before();
+        d3b::mbar_arrive(&bars.v_ready);
+      }
+      if (!(ok = d3b::warp_wait(&bars.hv_ready, pc, abort_flag, err, kSiteScanHV))) break;
+      d3b::tc_fence_after();
+      const float eg = __expf(gl);
+#pragma unroll
+      for (int q2 = 0; q2 < 2; ++q2) {
+        uint32_t d[32];
+        d3b::tmem_ld32(lane_addr + R_COL_D + q2 * 32, d);
+        d3b::tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) hs[q2 * 32 + j] = fmaf(eg, hs[q2 * 32 + j], __uint_as_float(d[j]));
+      }
+      if (warp >= 2) {
+        // O = e^gamma_t (Q S_c) + (P V') for token t
+        const int tok = c * 64 + t;
+        const float eq = __expf(gt);
+        In* orow = static_cast<In*>(p.o) + b * p.os[0] + (long long)tok * p.os[1] + hv * p.os[2] + c0;
+#pragma unroll
+        for (int q2 = 0; q2 < 2; ++q2) {
+          uint32_t xq[32], xo[32];
+          d3b::tmem_ld32(lane_addr + R_COL_X + q2 * 32, xq);
+          d3b::tmem_ld32(lane_addr + R_COL_O + q2 * 32, xo);
+          d3b::tmem_wait_ld();
+          if (tok < p.T) {
+#pragma unroll
+            for (int x = 0; x < 32; x += 8) {
+              float f[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) f[e] = fmaf(eq, __uint_as_float(xq[x + e]), __uint_as_float(xo[x + e]));
+              *reinterpret_cast<uint4*>(orow + q2 * 32 + x) =
+                  make_uint4(gdc::pack2<In>(f[0], f[1]), gdc::pack2<In>(f[2], f[3]), gdc::pack2<In>(f[4], f[5]),
+                             gdc::pack2<In>(f[6], f[7]));
+            }
+          }
+        }
+      }
+      d3b::tc_fence_before();
+    }
+    if (ok && p.ht) {
+      float* dst = p.ht + (((long long)b * p.HV + hv) * KD + i) * KD + c0;
+#pragma unroll
+      for (int j = 0; j < R_VC; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(hs[j], hs[j + 1], hs[j + 2], hs[j + 3]);
+    }
+  }
+
+  d3b::tc_fence_before();
+  __syncthreads();
+  d3b::tc_fence_after();
+  if (warp == 5) d3b::tmem_dealloc(tmem, R_TMEM_COLS);
+}
+
+}  // namespace gds
+
+size_t state_workspace_bytes(long long B, long long T, long long HV) {
+  const long long NC = (T + 63) / 64;
+  return (size_t)(B * HV * NC) * gds::WS_CHUNK;
+}
+
+template <typename In>
+int launch_state(const GdrParams& p, int beta_dtype, uint8_t* ws, cudaStream_t s) {
+  static int attr_set[64][4] = {{0}};
+  const int dev = d3b_host::current_device();
+  int* err = d3b_host::device_error_word();
+  if (!err) return D3B_ECUDA;
+  const int NC = (p.T + 63) / 64;
+  const long long n_items = (long long)p.B * ((NC + 1) / 2) * p.HV;
+  const dim3 grid_p((unsigned)std::min<long long>(n_items, d3b_host::num_sms(dev)));  // persistent
+  auto set_smem = [&](auto kernel, int which, int bytes) -> bool {
+    if (dev >= 0 && dev < 64 && !attr_set[dev][which]) {
+      if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+        return false;
+      attr_set[dev][which] = 1;
+    }
+    return true;
+  };
+  auto prep = [&](auto kernel, int which) -> int {
+    if (!set_smem(kernel, which, gds::P_SMEM_BYTES)) return D3B_ECUDA;
+    kernel<<<grid_p, gds::P_THREADS, gds::P_SMEM_BYTES, s>>>(p, ws, NC, err);
+    return d3b_host::check_launch();
+  };
+  int st;
+  switch (beta_dtype) {
+    case D3B_F32: st = prep(gds::gdr_state_prep_kernel<In, float>, 0); break;
+    case D3B_BF16: st = prep(gds::gdr_state_prep_kernel<In, __nv_bfloat16>, 1); break;
+    case D3B_F16: st = prep(gds::gdr_state_prep_kernel<In, __half>, 2); break;
+    default: return D3B_EUNSUPPORTED;
+  }
+  if (st) return st;
+  if (!set_smem(gds::gdr_state_scan_kernel<In>, 3, gds::R_SMEM_BYTES)) return D3B_ECUDA;
+  gds::gdr_state_scan_kernel<In><<<(unsigned)(2LL * p.B * p.HV), gds::R_THREADS, gds::R_SMEM_BYTES, s>>>(p, ws, NC, err);
+  return d3b_host::check_launch();
+}
+
 bool aligned(const void* ptr, int bytes) { return reinterpret_cast<uintptr_t>(ptr) % bytes == 0; }
 
 }  // namespace
 
 extern "C" size_t d3b_gated_delta_workspace_size(int HV, int K, int V) {
   return (HV > 0 && K == 128 && V == 128) ? (size_t)HV * gdc::TILE : 0;
+}
+
+extern "C" size_t d3b_gated_delta_state_workspace_size(int B, int T, int HV, int K, int V) {
+  return (B > 0 && T > 0 && HV > 0 && K == 128 && V == 128) ? state_workspace_bytes(B, T, HV) : 0;
 }
 
 extern "C" int d3b_gated_delta_rule(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
@@ -807,7 +1485,7 @@ extern "C" int d3b_gated_delta_rule(const void* q, const int64_t* q_strides, con
   p.scale = scale;
   p.l2norm = l2norm ? 1 : 0;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (algo < 0 || algo > 2) return D3B_EINVAL;
+  if (algo < 0 || algo > 3) return D3B_EINVAL;
   // the chunked form: blocks of <= 64 tokens, K = V = 128, one state for all rows, no final state,
   // 16-byte rows (q, k, v, o: strides in multiples of 8 elements; h0: of 4)
   bool rows16 = aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(o, 16) && (!h0 || aligned(h0, 16));
@@ -823,6 +1501,15 @@ extern "C" int d3b_gated_delta_rule(const void* q, const int64_t* q_strides, con
   if (algo == 2 || (algo == 0 && chunk_ok && T > 0))
     return dtype == D3B_BF16 ? launch_chunk<__nv_bfloat16>(p, beta_dtype, static_cast<uint8_t*>(workspace), s)
                              : launch_chunk<__half>(p, beta_dtype, static_cast<uint8_t*>(workspace), s);
+  // the chunked form with the inter-chunk recurrence: any length, K = V = 128, any initial
+  // states, final state, 16-byte rows, a workspace of d3b_gated_delta_state_workspace_size()
+  const bool state_ok = K == 128 && V == 128 && T > 0 && rows16 && (!ht || aligned(ht, 16)) && workspace &&
+                        aligned(workspace, 256) &&
+                        workspace_bytes >= state_workspace_bytes(B, T, HV) && (long long)B * HV * 2 < (1ll << 31);
+  if (algo == 3 && !state_ok) return D3B_EUNSUPPORTED;
+  if (algo == 3 || (algo == 0 && state_ok))
+    return dtype == D3B_BF16 ? launch_state<__nv_bfloat16>(p, beta_dtype, static_cast<uint8_t*>(workspace), s)
+                             : launch_state<__half>(p, beta_dtype, static_cast<uint8_t*>(workspace), s);
   if (K == 128)
     return dtype == D3B_BF16 ? launch_k<128, __nv_bfloat16>(p, beta_dtype, blocks, s)
                              : launch_k<128, __half>(p, beta_dtype, blocks, s);

@@ -47,7 +47,7 @@ def _strides3(t: torch.Tensor, what: str) -> object:
     return _lib.i64_array(t.stride()[:3])
 
 
-ALGOS = {"auto": 0, "recurrent": 1, "chunk": 2}
+ALGOS = {"auto": 0, "recurrent": 1, "chunk": 2, "chunk_state": 3}
 
 
 def gated_delta_rule(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, g: torch.Tensor, beta: torch.Tensor,
@@ -58,7 +58,10 @@ def gated_delta_rule(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, g: to
 
     ``algo``: "recurrent" (token recurrence, fp32 throughout), "chunk" (the chunked form on
     the tensor cores: blocks of <= 64 tokens, K = V = 128, one initial state for all rows,
-    no final state) or "auto" (the chunked form where it applies).
+    no final state), "chunk_state" (64-token chunks carried through an inter-chunk state
+    recurrence on the tensor cores: any length, K = V = 128, final state; FLA's
+    chunk_gated_delta_rule numerics) or "auto" ("chunk" where it applies, else
+    "chunk_state" where it applies, else "recurrent").
     """
     if algo not in ALGOS:
         raise ValueError(f"algo must be one of {sorted(ALGOS)}, got {algo!r}")
@@ -101,7 +104,14 @@ def gated_delta_rule(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, g: to
     elif out.shape != (B, T, HV, V) or out.dtype != v.dtype or out.stride(-1) != 1:
         raise RuntimeError("gated_delta_rule: out must be [B,T,HV,V] in v's dtype with a contiguous last dim")
     ht = torch.empty(B, HV, K, V, dtype=torch.float32, device=v.device) if output_final_state else None
-    ws = _workspace(v.device, int(_lib.lib().d3b_gated_delta_workspace_size(HV, K, V))) if algo != "recurrent" else None
+    question_form = (K == 128 and V == 128 and T <= 64 and not output_final_state
+                     and (h0 is None or h0.stride(0) == 0 or B == 1))
+    if algo == "recurrent":
+        ws = None
+    elif algo == "chunk" or (algo == "auto" and question_form):
+        ws = _workspace(v.device, int(_lib.lib().d3b_gated_delta_workspace_size(HV, K, V)))
+    else:  # the inter-chunk form: every chunk's operand tiles
+        ws = _workspace(v.device, int(_lib.lib().d3b_gated_delta_state_workspace_size(B, T, HV, K, V)))
     with torch.cuda.device(v.device):
         st = _lib.lib().d3b_gated_delta_rule(
             _lib.ptr(q), _strides3(q, "q"), _lib.ptr(k), _strides3(k, "k"), _lib.ptr(v), _strides3(v, "v"),
@@ -123,10 +133,9 @@ def recurrent_gated_delta_rule(q, k, v, *, g, beta, initial_state, output_final_
 
 
 def chunk_gated_delta_rule(q, k, v, *, g, beta, initial_state, output_final_state, use_qk_l2norm_in_kernel=True):
-    """Drop-in for d3trt/model/ops.py:287-324 (FLA chunk_gated_delta_rule): the chunked form on the tensor
-    cores where it applies (question blocks), else the token recurrence. There is no inter-chunk form yet:
-    for the 4096-token state pass the recurrence is slower than FLA's chunked kernel (3.0 vs 0.65 ms per
-    layer on B200), so keep FLA for that call."""
+    """Drop-in for d3trt/model/ops.py:287-324 (FLA chunk_gated_delta_rule): on the tensor cores, the
+    question blocks' chunked form where it applies (blocks of <= 64 tokens sharing one state, no final
+    state), else 64-token chunks with the inter-chunk state recurrence (the state pass)."""
     return gated_delta_rule(q, k, v, g=g, beta=beta, initial_state=initial_state,
                             output_final_state=output_final_state, use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel)
 

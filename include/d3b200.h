@@ -291,7 +291,12 @@ D3B_API int d3b_selftest_wait_timeout(int limit_ms, d3b_stream_t stream);
  *   2 = chunked form on the tensor cores (bf16 products, fp32 accumulate and
  *   solve; T <= 64, K = V = 128, h0 NULL or shared by all rows, ht NULL, 16-byte
  *   rows, a workspace of d3b_gated_delta_workspace_size() bytes when h0 is given,
- *   else D3B_EUNSUPPORTED); 0 = the chunked form where it applies, else 1.
+ *   else D3B_EUNSUPPORTED); 3 = chunked form with the inter-chunk state
+ *   recurrence (FLA's chunk_gated_delta_rule numerics: 64-token chunks, bf16
+ *   products, fp32 accumulation and state; any T, K = V = 128, per-row or shared
+ *   h0, ht allowed, 16-byte rows, a 256-byte aligned workspace of
+ *   d3b_gated_delta_state_workspace_size() bytes, else D3B_EUNSUPPORTED);
+ *   0 = form 2 where it applies, else form 3 where it applies, else 1.
  */
 D3B_API int d3b_gated_delta_rule(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
                                  const void* v, const int64_t* v_strides, const float* g, const int64_t* g_strides,
@@ -303,6 +308,12 @@ D3B_API int d3b_gated_delta_rule(const void* q, const int64_t* q_strides, const 
 /* Device workspace the chunked form needs with an initial state: HV bf16 copies of
  * the state, 32 KiB each (0 where the chunked form does not apply). */
 D3B_API size_t d3b_gated_delta_workspace_size(int HV, int K, int V);
+
+/* Device workspace of the chunked form with the inter-chunk recurrence (algo 3;
+ * the state pass, ops.py:287-324 with output_final_state): 74752 bytes per
+ * (row, value head, 64-token chunk), the chunk's operand tiles (0 where the form
+ * does not apply). */
+D3B_API size_t d3b_gated_delta_state_workspace_size(int B, int T, int HV, int K, int V);
 
 /*
  * State snapshots (the per-layer K/V and GDN states one state pass leaves

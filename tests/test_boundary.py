@@ -138,11 +138,16 @@ def test_gated_delta_rejects_bad_arguments():
     assert call(strides=None) == _lib.EINVAL
     assert call(ptr=ctypes.c_void_p(257)) == _lib.EALIGN
     assert call(B=0) == _lib.OK  # nothing to do: no launch
-    assert call(algo=3) == _lib.EINVAL
+    assert call(algo=4) == _lib.EINVAL
     assert call(algo=2) == _lib.EUNSUPPORTED  # the chunked form needs K = V = 128
     assert call(algo=2, K=128, V=128, T=65) == _lib.EUNSUPPORTED  # and blocks of <= 64 tokens
+    assert call(algo=3) == _lib.EUNSUPPORTED  # the inter-chunk form needs K = V = 128
+    assert call(algo=3, K=128, V=128) == _lib.EUNSUPPORTED  # and a workspace
     assert lib.d3b_gated_delta_workspace_size(48, 128, 128) == 48 * 32768
     assert lib.d3b_gated_delta_workspace_size(48, 64, 64) == 0
+    assert lib.d3b_gated_delta_state_workspace_size(1, 4096, 48, 128, 128) == 48 * 64 * 74752
+    assert lib.d3b_gated_delta_state_workspace_size(2, 65, 3, 128, 128) == 2 * 3 * 2 * 74752
+    assert lib.d3b_gated_delta_state_workspace_size(1, 4096, 48, 64, 64) == 0
 
 
 def test_wait_selftest_rejects_bad_limit():
