@@ -645,20 +645,16 @@ def cfg4_e2e(dev, stream, flush, peaks):
     MLP 17408, 16 full-attention layers (32 q / 4 kv heads, head_dim 128), 48 Gated DeltaNet
     layers (16 / 48 heads), every Linear W8A8 FP8, bf16 RMSNorm; token ids uniform over a
     151k vocabulary; a 4096-token state and 255 question blocks of 48 tokens; the 255-way
-    fp32 readout (N(0, 0.02)) at each block's last token. The GDN state scan runs on FLA's
-    chunked kernel (config 4 keeps the GDN layers on the existing path), the question scan
-    on this library's chunked form. Timed on the device: state pass, question pass, readout;
+    fp32 readout (N(0, 0.02)) at each block's last token. Both GDN scans run on this
+    library's chunked forms (the state pass with the inter-chunk recurrence, the question
+    pass with one shared state). Timed on the device: state pass, question pass, readout;
     end to end: token ids from pinned host memory and probabilities back to it."""
     from d3_turbo_trt_b200.model.backbone import BackboneConfig, D3Backbone
     from d3_turbo_trt_b200.model.batching import QuestionBatcher
 
     cfg = BackboneConfig()
     vocab, S, nb, L, n_opt = 151_936, 4096, 255, 48, 255
-    try:
-        import fla.ops.gated_delta_rule  # noqa: F401
-        gdn_state = "fla"
-    except Exception:  # noqa: BLE001 - the library's recurrence otherwise
-        gdn_state = "ours"
+    gdn_state = "ours"
     t0 = time.perf_counter()
     bb = D3Backbone(cfg, _RandomWeights(cfg, vocab, dev), device=dev, mode="fp8", gdn_state=gdn_state)
     torch.cuda.synchronize()
@@ -860,6 +856,7 @@ def secondary(dev, stream, flush, peaks, quant, pb, d3b):
     # one GDN layer's question pass (255 blocks x 48 tokens, 48 value heads), against the
     # reference's GPU library kernels on the inputs the reference builds for them
     res["gdn_question_pass_255x48"] = gdn_line(dev, stream, flush)
+    res["gdn_state_pass_4096x48"] = gdn_state_line(dev, stream, flush)
     # readout: 255 blocks x 5120 x 255 options
     hidden = torch.randn(255, 5120, generator=g).to(torch.bfloat16).to(dev)
     ro = (torch.randn(255, 5120, generator=g) * 0.02).to(dev)
@@ -912,6 +909,38 @@ def gdn_line(dev, stream, flush):
     o_chk, _ = chunk_gated_delta_rule(qr, kr, x["v"], **kw)
     o, _ = gdn.gated_delta_rule(x["q"], x["k"], x["v"], g=x["g"], beta=x["beta"], initial_state=h0, algo="chunk")
     line["max_abs_diff_chunk_vs_fla_chunk"] = float((o.float() - o_chk.float()).abs().max())
+    return line
+
+
+def gdn_state_line(dev, stream, flush):
+    """One GDN layer's state pass (config 4): one row of 4096 tokens, 16 q/k heads feeding 48
+    value heads, K = V = 128, final state; the inter-chunk form against FLA's chunked kernel
+    (the reference's GPU path for ops.chunk_gated_delta_rule) on the same inputs."""
+    from d3_turbo_trt_b200.model import gdn
+
+    g = torch.Generator().manual_seed(5)
+    B, T, H, HV, K, V = 1, 4096, 16, 48, 128, 128
+    q = torch.randn(B, T, H, K, generator=g).to(torch.bfloat16).to(dev)
+    k = torch.randn(B, T, H, K, generator=g).to(torch.bfloat16).to(dev)
+    v = torch.randn(B, T, HV, V, generator=g).to(torch.bfloat16).to(dev)
+    gl = (-torch.rand(B, T, HV, generator=g) * 0.5).to(dev)
+    beta = torch.sigmoid(torch.randn(B, T, HV, generator=g)).to(torch.bfloat16).to(dev)
+    kw = dict(g=gl, beta=beta, initial_state=None, output_final_state=True, use_qk_l2norm_in_kernel=True)
+    line = {"workload": f"{B} row x {T} tokens, {H} q/k heads -> {HV} value heads, K=V={K}, final state",
+            "ours_chunk_state_ms": statistics.median(time_steps(
+                lambda: gdn.chunk_gated_delta_rule(q, k, v, **kw), 5, 3, stream, flush))}
+    try:
+        from fla.ops.gated_delta_rule import chunk_gated_delta_rule
+    except Exception as exc:  # noqa: BLE001 - the library is optional on the box
+        line["fla"] = f"unavailable: {type(exc).__name__}"
+        return line
+    qr, kr = q.repeat_interleave(HV // H, 2), k.repeat_interleave(HV // H, 2)
+    line["fla_chunk_ms"] = statistics.median(time_steps(lambda: chunk_gated_delta_rule(qr, kr, v, **kw), 5, 3,
+                                                        stream, flush))
+    o_ref, s_ref = chunk_gated_delta_rule(qr, kr, v, **kw)
+    o, s_ours = gdn.chunk_gated_delta_rule(q, k, v, **kw)
+    line["max_abs_diff_vs_fla_chunk"] = float((o.float() - o_ref.float()).abs().max())
+    line["max_abs_diff_final_state_vs_fla_chunk"] = float((s_ours - s_ref.float()).abs().max())
     return line
 
 

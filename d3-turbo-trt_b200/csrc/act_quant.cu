@@ -1,14 +1,20 @@
 // Per-token activation quantisation (d3trt/model/quant.py:92-100) and, on a
 // weight matrix, per-output-channel weight quantisation (quant.py:77-89).
 //
-// One warp owns one row. bf16 rows up to 6144 elements (the model's hidden
-// and attention widths) are read once into registers (all of a lane's 16-byte
-// loads in flight together), reduced and quantised from there. Longer rows
-// (and f16/f32 input) take two passes: pass 1 reads the row with 16-byte loads
-// (batches of 8 per lane in flight) and reduces max|x| with warp shuffles;
-// pass 2 re-reads the row, which the first pass has just brought into L2, and
-// writes the 8-bit codes with 8-byte stores. HBM traffic is the algorithmic
-// minimum either way: read x once, write q and the scale.
+// bf16 rows of 1025 to 18432 elements (every width of the model: hidden 5120,
+// attention 6144, MLP 17408) run one CTA of 128 or 256 threads per row: each
+// thread reads at most nine 16-byte vectors of the row into registers (all in
+// flight together), max|x| is reduced through the warps and shared memory, and
+// the codes are written from the same registers. With under 64 registers per
+// thread many rows are in flight per SM, so one row's loads overlap other
+// rows' arithmetic (a warp per row held only ~9 warps per SM and left loads
+// and arithmetic in separate phases: 1.5-1.9x slower). Narrower bf16 rows run
+// one warp per row from registers; f16/f32 input takes two passes: pass 1
+// reads the row with 16-byte loads (batches of 8 per lane in flight) and
+// reduces max|x| with warp shuffles; pass 2 re-reads the row, which the first
+// pass has just brought into L2, and writes the 8-bit codes with 8-byte stores.
+// HBM traffic is the algorithmic minimum every way: read x once, write q and
+// the scale.
 //
 // Bit-exactness with the reference formulas:
 //   amax  = max(max_k |x|, 1e-12f)                (fp32, order independent)
@@ -200,6 +206,62 @@ __global__ void __launch_bounds__(kRegWarps * 32) act_quant_reg_kernel(const __n
       *reinterpret_cast<uint2*>(qr + (int64_t)(lane + 32 * u) * 8) = quant8_bf16<MODE>(raw[u], scale, rcp);
 }
 
+// ---------------------------------------------------------------------------
+// bf16 rows, one CTA of NT threads per row, NV 16-byte vectors per thread
+// (K <= NT * 8 * NV): few registers per thread, so many rows are in flight per
+// SM and one row's loads overlap other rows' arithmetic. max|x| is reduced
+// within each warp (packed u16 max, shuffles) and across the CTA's warps
+// through shared memory; every thread then forms the same scale.
+// ---------------------------------------------------------------------------
+template <int MODE, int NT, int NV>
+__global__ void __launch_bounds__(NT) act_quant_cta_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                                           uint8_t* __restrict__ q, float* __restrict__ scale_out,
+                                                           int64_t K) {
+  constexpr int NW = NT / 32;
+  __shared__ uint32_t wmax[NW];
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int64_t row = blockIdx.x;
+  const uint4* src = reinterpret_cast<const uint4*>(x + row * ldx);
+  uint8_t* qr = q + row * K;
+  const int nvec = static_cast<int>(K / 8);
+  uint4 raw[NV];
+#pragma unroll
+  for (int u = 0; u < NV; ++u)
+    raw[u] = tid + NT * u < nvec ? __ldg(src + tid + NT * u) : make_uint4(0, 0, 0, 0);
+  uint32_t m0 = 0, m1 = 0;
+#pragma unroll
+  for (int u = 0; u < NV; ++u) {
+    m0 = umax2(m0, raw[u].x & 0x7FFF7FFFu);
+    m1 = umax2(m1, raw[u].y & 0x7FFF7FFFu);
+    m0 = umax2(m0, raw[u].z & 0x7FFF7FFFu);
+    m1 = umax2(m1, raw[u].w & 0x7FFF7FFFu);
+  }
+  uint32_t m = umax2(m0, m1);
+  m = max(m & 0xFFFFu, m >> 16);  // the largest |x| bit pattern (non-negative bf16 order as integers)
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) wmax[tid >> 5] = m;
+  __syncthreads();
+  m = wmax[0];
+#pragma unroll
+  for (int w = 1; w < NW; ++w) m = max(m, wmax[w]);
+  const float amax = fmaxf(__uint_as_float(m << 16), 1e-12f);
+  const float scale = __fdiv_rn(amax, MODE == D3B_MODE_FP8 ? 448.f : 127.f);
+  const float rcp = __frcp_rn(scale);
+  if (tid == 0) scale_out[row] = scale;
+#pragma unroll
+  for (int u = 0; u < NV; ++u)
+    if (tid + NT * u < nvec)
+      *reinterpret_cast<uint2*>(qr + (int64_t)(tid + NT * u) * 8) = quant8_bf16<MODE>(raw[u], scale, rcp);
+}
+
+template <int NT, int NV>
+void launch_cta(const __nv_bfloat16* x, int64_t ldx, uint8_t* q, float* scale, int64_t M, int64_t K, int mode,
+                cudaStream_t stream) {
+  if (mode == D3B_MODE_FP8) act_quant_cta_kernel<D3B_MODE_FP8, NT, NV><<<(unsigned)M, NT, 0, stream>>>(x, ldx, q, scale, K);
+  else act_quant_cta_kernel<D3B_MODE_INT8, NT, NV><<<(unsigned)M, NT, 0, stream>>>(x, ldx, q, scale, K);
+}
+
 template <int NV>
 void launch_reg(const __nv_bfloat16* x, int64_t ldx, uint8_t* q, float* scale, int64_t M, int64_t K, int mode,
                 cudaStream_t stream) {
@@ -215,6 +277,16 @@ int launch_typed(const void* x, int64_t ldx, void* q, float* scale, int64_t M, i
   const bool vec = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((ldx * elem) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(q) % 16 == 0) && (K % 8 == 0);
   if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    if (vec && K > 1024 && K <= 256 * 8 * 9 && M <= 0x7FFFFFFF) {
+      const auto* xb = static_cast<const __nv_bfloat16*>(x);
+      auto* qb = static_cast<uint8_t*>(q);
+      const int64_t nv = K / 8;
+      if (nv <= 128 * 4) launch_cta<128, 4>(xb, ldx, qb, scale, M, K, mode, stream);
+      else if (nv <= 128 * 6) launch_cta<128, 6>(xb, ldx, qb, scale, M, K, mode, stream);
+      else if (nv <= 128 * 8) launch_cta<128, 8>(xb, ldx, qb, scale, M, K, mode, stream);
+      else launch_cta<256, 9>(xb, ldx, qb, scale, M, K, mode, stream);
+      return d3b_host::check_launch();
+    }
     if (vec && K <= 32 * 8 * 24 && (M + kRegWarps - 1) / kRegWarps <= 0x7FFFFFFF) {
       const auto* xb = static_cast<const __nv_bfloat16*>(x);
       auto* qb = static_cast<uint8_t*>(q);

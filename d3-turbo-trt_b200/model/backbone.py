@@ -23,8 +23,9 @@ library:
   place of the reference's concatenation), its q/k/v handed on as strided views;
 * the GDN scan of the question pass: ``gdn.question_gated_delta_rule`` (one
   shared initial state, no per-row copy or head repeat); of the state pass:
-  the library's recurrence, or FLA's chunked kernel when the caller selects it
-  (``gdn_state="fla"``: the reference's own GPU path for that call);
+  ``gdn.chunk_gated_delta_rule`` (64-token chunks with the inter-chunk state
+  recurrence on the tensor cores), or FLA's chunked kernel when the caller selects
+  it (``gdn_state="fla"``: the reference's own GPU path for that call);
 * SiLU(gate) * up fused with down_proj's quantisation (``fused.silu_mul_quant``) and
   the GDN output's gated RMSNorm fused with out_proj's (``fused.gated_rmsnorm_quant``);
 * the 255-way readout: ``readout.probabilities_tensor``.
@@ -333,4 +334,4 @@ class D3Backbone:
                                           g=g, beta=beta, initial_state=None, output_final_state=True,
                                           use_qk_l2norm_in_kernel=True)
         return gdn.gated_delta_rule(query, key, value, g=g, beta=beta, initial_state=None, output_final_state=True,
-                                    use_qk_l2norm_in_kernel=True, algo="recurrent")
+                                    use_qk_l2norm_in_kernel=True, algo="chunk_state")
