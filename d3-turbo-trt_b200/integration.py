@@ -13,6 +13,7 @@ kernels/prefix_bidir.py ``triton_available``            kernels.prefix_bidir.ker
 model/ops.py:227 ``question_attention``                 model.ops.question_attention
 model/ops.py:174 ``flash_state``                        model.ops.flash_state
 model/ops.py:327 ``recurrent_gated_delta_rule``         model.gdn.question_gated_delta_rule
+model/ops.py:287 ``chunk_gated_delta_rule``             model.gdn.chunk_gated_delta_rule
 model/quant.py ``quantize_rows``, ``quantize_weight``,  model.quant (same names)
 ``QuantLinear``, ``make_linear``
 model/trtllm_stack.py ``QuantLinear``, ``make_linear``  model.quant (same names)
@@ -20,7 +21,6 @@ model/trtllm_stack.py:451 ``TrtllmStack.probabilities``  model.readout.ReadoutHe
 backends/trtllm.py ``StateCache``                       model.cache.StateCache with an arena
 =====================================================  ======================================
 
-The GDN state pass (``ops.chunk_gated_delta_rule``) stays on FLA's chunked kernel.
 ``D3Core`` calls the ops through the module (``ops.question_attention(...)``), so
 rebinding the module attributes is enough; nothing in d3trt is edited.
 """
@@ -69,6 +69,7 @@ def install(package: str = "d3trt", *, cache: bool = True) -> dict[str, Any]:
     bind(ref_ops, "question_attention", _ops.question_attention)
     bind(ref_ops, "flash_state", _ops.flash_state)
     bind(ref_ops, "recurrent_gated_delta_rule", _gdn.question_gated_delta_rule)
+    bind(ref_ops, "chunk_gated_delta_rule", _gdn.chunk_gated_delta_rule)
     for name in ("quantize_rows", "quantize_weight", "QuantLinear", "make_linear"):
         bind(ref_quant, name, getattr(_quant, name))
     try:

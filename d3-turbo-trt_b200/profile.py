@@ -9,7 +9,9 @@ BASELINE.json: cfg3a (4096-token state + 16 x 64-token blocks), cfg3b (16384 +
 255 x 48), state4k (the state pass of cfg3a), cfg2 (W8A8 4096 x 5120 x 13824),
 cfg4 (readout 255 x 5120 x 255; snapshot: the 64-layer state snapshot at a
 4096-token state, packed by one copy launch; gdn: one GDN layer's question pass,
-255 blocks x 48 tokens x 48 value heads). Inputs are seeded synthetic tensors.
+255 blocks x 48 tokens x 48 value heads; gdn_state: one GDN layer's state pass,
+4096 tokens x 48 value heads with a final state). Inputs are seeded synthetic
+tensors.
 """
 
 from __future__ import annotations
@@ -149,6 +151,21 @@ def _gdn(dev: torch.device, algo: str):
     return fn, {"flops": flops}
 
 
+def _gdn_state(dev: torch.device, T: int = 4096, H: int = 16, HV: int = 48, K: int = 128, V: int = 128):
+    """One GDN layer's state pass (config 4): one row of 4096 tokens, final state, the inter-chunk form."""
+    g = torch.Generator(device=dev).manual_seed(7)
+    q = torch.randn(1, T, H, K, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(1, T, H, K, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(1, T, HV, V, generator=g, device=dev).to(torch.bfloat16)
+    gl = -torch.rand(1, T, HV, generator=g, device=dev) * 0.5
+    beta = torch.sigmoid(torch.randn(1, T, HV, generator=g, device=dev)).to(torch.bfloat16)
+    fn = lambda: gdn.chunk_gated_delta_rule(q, k, v, g=gl, beta=beta, initial_state=None, output_final_state=True)
+    # tensor products per (64-token chunk, value head): K K^T, Q K^T, W, U (64 x 64 x 128 each),
+    # [W; Q] S (2 x 64 x 128 x 128), K^T V'' (128 x 64 x 128), P V' (64 x 64 x 128)
+    macs = 4 * 64 * 64 * 128 + 2 * 64 * 128 * 128 + 128 * 64 * 128 + 64 * 64 * 128
+    return fn, {"flops": 2.0 * macs * ((T + 63) // 64) * HV}
+
+
 def build(kernel: str, config: str, dev: torch.device):
     if kernel == "attention":
         return _state(dev) if config == "state4k" else _attention(config, dev)
@@ -168,6 +185,8 @@ def build(kernel: str, config: str, dev: torch.device):
         return _gdn(dev, "chunk")
     if kernel == "gdn_recurrent":
         return _gdn(dev, "recurrent")
+    if kernel == "gdn_state":
+        return _gdn_state(dev)
     raise SystemExit(f"unknown kernel {kernel!r}")
 
 
@@ -175,7 +194,7 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", required=True,
                     choices=["attention", "gemm_fp8", "gemm_int8", "act_quant_fp8", "act_quant_int8", "readout",
-                             "snapshot", "gdn", "gdn_recurrent"])
+                             "snapshot", "gdn", "gdn_recurrent", "gdn_state"])
     ap.add_argument("--config", default="cfg3a", choices=[*ATTN, "state4k", "cfg2", "cfg4"])
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=1)

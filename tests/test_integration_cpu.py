@@ -48,6 +48,7 @@ def test_install_rebinds_every_hot_path_name(d3trt):
         assert ref_ops.question_attention is ops.question_attention
         assert ref_ops.flash_state is ops.flash_state
         assert ref_ops.recurrent_gated_delta_rule is gdn.question_gated_delta_rule
+        assert ref_ops.chunk_gated_delta_rule is gdn.chunk_gated_delta_rule
         assert ref_quant.QuantLinear is quant.QuantLinear
         assert ref_quant.make_linear is quant.make_linear
         assert ref_quant.quantize_rows is quant.quantize_rows
