@@ -72,6 +72,10 @@ SIGNATURES: list[tuple[str, Any, list[Any]]] = [
     ("d3b_readout_workspace_size", _SZ, [_I, _I]),
     ("d3b_readout", _I, [_VP, _I, _VP, _VP, _F, _VP, _I, _I, _I, _VP, _SZ, _VP]),
     ("d3b_readout_noalloc", _I, [_VP, _I, _VP, _VP, _F, _VP, _I, _I, _I, _VP]),
+    ("d3b_readout_planes_size", _SZ, [_I, _I]),
+    ("d3b_readout_split", _I, [_VP, _I, _I, _VP, _VP]),
+    ("d3b_readout_planes_workspace_size", _SZ, [_I, _I, _I]),
+    ("d3b_readout_planes", _I, [_VP, _VP, _VP, _F, _VP, _I, _I, _I, _VP, _SZ, _VP]),
     ("d3b_selftest_wait_timeout", _I, [_I, _VP]),
     (
         "d3b_gated_delta_rule",

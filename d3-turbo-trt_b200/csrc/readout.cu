@@ -539,6 +539,236 @@ extern "C" int d3b_readout(const void* hidden, int h_dtype, const float* readout
   return d3b_host::check_launch();
 }
 
+namespace {
+
+// ===========================================================================
+// Tensor-core readout for bf16 hidden rows (the model's final-norm output).
+//
+// The fp32 readout matrix is split once into three bf16 planes,
+// R = r0 + r1 + r2 with r0 = bf16(R), r1 = bf16(R - r0), r2 = bf16(R - r0 - r1)
+// (each difference is exact in fp32, and the three planes carry all 24 bits of
+// R). Every product of a bf16 hidden value with a plane value is exact in fp32,
+// so hidden . R = sum_p hidden . r_p is an fp32 dot product that differs from
+// the reference's SGEMM only in summation order. The products run on tcgen05
+// (kind::f16, bf16 x bf16, fp32 accumulate in TMEM): one CTA per (128-row tile,
+// 256-option tile, K split) streams its hidden rows and the three planes' rows
+// by TMA in 64-wide K chunks (two stages), accumulates all three planes into one
+// 128 x 256 fp32 accumulator, and writes it as one split's partial logits; the
+// reduce/softmax kernel above then adds the splits in order and applies the mask,
+// the temperature and the softmax.
+// ===========================================================================
+constexpr int kTcRows = 128, kTcOpts = 256, kTcK = 64;   // tile and K chunk
+constexpr int kTcChunkA = kTcRows * kTcK * 2;            // 16 KB
+constexpr int kTcChunkB = kTcOpts * kTcK * 2;            // 32 KB per plane
+constexpr int kTcStage = kTcChunkA + 3 * kTcChunkB;      // 112 KB
+constexpr int kTcSmem = 2 * kTcStage + 1024;
+constexpr int kTcChunksPerCta = 4;  // 2-5 chunks per CTA time alike at 255 x 5120 x 255 (23.5 us); 4 halves the partials of 2
+constexpr int kTcMaxSplit = 128;
+
+enum : int { kSiteTcFull = 4101, kSiteTcEmpty = 4102, kSiteTcDone = 4103 };
+
+struct TcBars {
+  uint64_t full[2], empty[2], done;
+  uint32_t tmem_slot;
+  int abort_flag;
+};
+
+__global__ void __launch_bounds__(128, 1)
+    readout_tc_kernel(const __grid_constant__ CUtensorMap mapH, const __grid_constant__ CUtensorMap mapP, int K,
+                      int o_pad, int b_pad, int kper, float* __restrict__ partials, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ TcBars bars;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int r0 = blockIdx.x * kTcRows, o0 = blockIdx.y * kTcOpts, kz = blockIdx.z;
+  const int kb = kz * kper, ke = min(K, kb + kper);
+  const int nch = (ke - kb + kTcK - 1) / kTcK;
+  volatile int* abort_flag = &bars.abort_flag;
+  if (tid == 0) {
+    for (int s = 0; s < 2; ++s) {
+      d3b::mbar_init(&bars.full[s], 1);
+      d3b::mbar_init(&bars.empty[s], 1);
+    }
+    d3b::mbar_init(&bars.done, 1);
+    bars.abort_flag = 0;
+    d3b::fence_barrier_init();
+  }
+  if (warp == 0) d3b::tmem_alloc(&bars.tmem_slot, 256);
+  d3b::tc_fence_before();
+  __syncthreads();
+  d3b::tc_fence_after();
+  const uint32_t tmem = bars.tmem_slot;
+  bool ok = true;
+  if (tid == 0) {
+    // one thread loads and issues: chunk c in stage c % 2; planes p at option rows p * o_pad + o0
+    d3b::tma_prefetch_desc(&mapH);
+    d3b::tma_prefetch_desc(&mapP);
+    auto load = [&](int c) {
+      uint8_t* st = smem + (c & 1) * kTcStage;
+      const int k0 = kb + c * kTcK;
+      d3b::mbar_arrive_expect_tx(&bars.full[c & 1], kTcStage);
+      d3b::tma_load_2d(st, &mapH, &bars.full[c & 1], k0, r0);
+#pragma unroll
+      for (int p = 0; p < 3; ++p)
+        d3b::tma_load_2d(st + kTcChunkA + p * kTcChunkB, &mapP, &bars.full[c & 1], k0, p * o_pad + o0);
+    };
+    constexpr uint32_t idesc = d3b::make_idesc(1, 1, 1, 0, 0, kTcRows, kTcOpts);
+    const uint32_t s_base = d3b::smem_u32(smem);
+    for (int c = 0; c < nch && c < 2; ++c) load(c);
+    for (int c = 0; c < nch; ++c) {
+      const int s = c & 1;
+      if (!(ok = d3b::mbar_wait(&bars.full[s], (uint32_t)(c >> 1) & 1, abort_flag, err, kSiteTcFull))) break;
+      d3b::tc_fence_after();
+      const uint32_t st = s_base + s * kTcStage;
+#pragma unroll
+      for (int p = 0; p < 3; ++p)
+#pragma unroll
+        for (int k = 0; k < kTcK / 16; ++k) {
+          const uint64_t a = d3b::make_smem_desc(st + k * 32, 16, 1024, d3b::kLayoutSW128);
+          const uint64_t b = d3b::make_smem_desc(st + kTcChunkA + p * kTcChunkB + k * 32, 16, 1024, d3b::kLayoutSW128);
+          d3b::mma_f16_ss(tmem, a, b, idesc, (c > 0 || p > 0 || k > 0) ? 1u : 0u);
+        }
+      d3b::mma_commit(&bars.empty[s]);
+      if (c + 2 < nch) {
+        if (!(ok = d3b::mbar_wait(&bars.empty[s], (uint32_t)(c >> 1) & 1, abort_flag, err, kSiteTcEmpty))) break;
+        load(c + 2);
+      }
+    }
+    d3b::mma_commit(&bars.done);
+  }
+  __syncwarp();
+  // epilogue: thread = row r0 + tid (TMEM lane), 256 partial logits of this split
+  ok = d3b::warp_wait(&bars.done, 0, abort_flag, err, kSiteTcDone);
+  d3b::tc_fence_after();
+  if (ok) {
+    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+    float* dst = partials + ((int64_t)kz * b_pad + r0 + tid) * o_pad + o0;
+#pragma unroll 1
+    for (int c = 0; c < kTcOpts / 32; ++c) {
+      uint32_t v[32];
+      d3b::tmem_ld32(lane_addr + c * 32, v);
+      d3b::tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(dst + c * 32 + i) =
+            make_float4(__uint_as_float(v[i]), __uint_as_float(v[i + 1]), __uint_as_float(v[i + 2]),
+                        __uint_as_float(v[i + 3]));
+    }
+  }
+  d3b::tc_fence_before();
+  __syncthreads();
+  d3b::tc_fence_after();
+  if (warp == 0) d3b::tmem_dealloc(tmem, 256);
+}
+
+// R fp32 [n_opt, K] -> three bf16 planes [3][o_pad][K] (rows >= n_opt zero)
+__global__ void __launch_bounds__(256) readout_split_kernel(const float* __restrict__ R, int n_opt, int K, int o_pad,
+                                                            __nv_bfloat16* __restrict__ planes) {
+  const int64_t n = (int64_t)o_pad * K;
+  for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (int64_t)gridDim.x * 256) {
+    const int64_t o = i / K;
+    const float x = o < n_opt ? R[i] : 0.f;
+    const __nv_bfloat16 a = __float2bfloat16_rn(x);
+    const float r1 = x - __bfloat162float(a);  // exact
+    const __nv_bfloat16 b = __float2bfloat16_rn(r1);
+    const __nv_bfloat16 c = __float2bfloat16_rn(r1 - __bfloat162float(b));  // exact difference
+    planes[i] = a;
+    planes[n + i] = b;
+    planes[2 * n + i] = c;
+  }
+}
+
+struct TcShape {
+  int b_pad, o_pad, kper, ksplit;
+};
+
+inline TcShape tc_shape(int B, int K, int n_opt) {
+  TcShape sh;
+  sh.b_pad = (B + kTcRows - 1) / kTcRows * kTcRows;
+  sh.o_pad = (n_opt + kTcOpts - 1) / kTcOpts * kTcOpts;
+  const int chunks = (K + kTcK - 1) / kTcK;
+  sh.ksplit = std::min(kTcMaxSplit, std::max(1, (chunks + kTcChunksPerCta - 1) / kTcChunksPerCta));
+  sh.kper = (chunks + sh.ksplit - 1) / sh.ksplit * kTcK;
+  sh.ksplit = (K + sh.kper - 1) / sh.kper;
+  return sh;
+}
+
+}  // namespace
+
+extern "C" size_t d3b_readout_planes_size(int n_opt, int K) {
+  if (n_opt <= 0 || K <= 0) return 0;
+  return (size_t)3 * ((n_opt + kTcOpts - 1) / kTcOpts * kTcOpts) * K * 2;
+}
+
+extern "C" int d3b_readout_split(const float* readout, int n_opt, int K, void* planes, d3b_stream_t stream) {
+  if (n_opt <= 0 || K <= 0 || !readout || !planes) return D3B_EINVAL;
+  const int o_pad = (n_opt + kTcOpts - 1) / kTcOpts * kTcOpts;
+  const int64_t n = (int64_t)o_pad * K;
+  const int blocks = (int)std::min<int64_t>((n + 255) / 256, 4096);
+  readout_split_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      readout, n_opt, K, o_pad, static_cast<__nv_bfloat16*>(planes));
+  return d3b_host::check_launch();
+}
+
+extern "C" size_t d3b_readout_planes_workspace_size(int B, int K, int n_opt) {
+  if (B <= 0 || K <= 0 || n_opt <= 0) return 0;
+  const TcShape sh = tc_shape(B, K, n_opt);
+  return (size_t)sh.ksplit * sh.b_pad * sh.o_pad * sizeof(float);
+}
+
+extern "C" int d3b_readout_planes(const void* hidden, const void* planes, const int32_t* counts, float temperature,
+                                  float* probs, int B, int K, int n_opt, void* workspace, size_t workspace_bytes,
+                                  d3b_stream_t stream) {
+  if (B < 0 || K <= 0 || n_opt <= 0 || n_opt > kMaxOpts) return D3B_EINVAL;
+  if (!(temperature > 0.f)) return D3B_EINVAL;
+  if (B == 0) return D3B_OK;
+  if (!hidden || !planes || !counts || !probs || !workspace) return D3B_EINVAL;
+  if (K % 8) return D3B_EUNSUPPORTED;  // rows of 16-byte multiples (TMA)
+  if (reinterpret_cast<uintptr_t>(hidden) % 16 || reinterpret_cast<uintptr_t>(planes) % 16 ||
+      reinterpret_cast<uintptr_t>(workspace) % 16)
+    return D3B_EALIGN;
+  if (workspace_bytes < d3b_readout_planes_workspace_size(B, K, n_opt)) return D3B_ENOSPACE;
+  const TcShape sh = tc_shape(B, K, n_opt);
+  int* err = d3b_host::device_error_word();
+  if (!err) return D3B_ECUDA;
+  CUtensorMap maps[2];
+  int rc;
+  {  // hidden [B, K] bf16: dims {K, B}, box {64, 128}; rows past B read as zero
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)B};
+    const uint64_t st[1] = {(uint64_t)K * 2};
+    const uint32_t box[2] = {(uint32_t)kTcK, (uint32_t)kTcRows};
+    if ((rc = d3b_host::encode_tiled(&maps[0], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, hidden, dims, st, box,
+                                     CU_TENSOR_MAP_SWIZZLE_128B)))
+      return rc;
+  }
+  {  // planes [3 * o_pad, K] bf16: box {64, 256}
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)3 * sh.o_pad};
+    const uint64_t st[1] = {(uint64_t)K * 2};
+    const uint32_t box[2] = {(uint32_t)kTcK, (uint32_t)kTcOpts};
+    if ((rc = d3b_host::encode_tiled(&maps[1], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, planes, dims, st, box,
+                                     CU_TENSOR_MAP_SWIZZLE_128B)))
+      return rc;
+  }
+  static int attr_set[64] = {0};
+  const int dev = d3b_host::current_device();
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(readout_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem) != cudaSuccess)
+      return D3B_ECUDA;
+    attr_set[dev] = 1;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  float* partials = static_cast<float*>(workspace);
+  const dim3 grid(sh.b_pad / kTcRows, sh.o_pad / kTcOpts, sh.ksplit);
+  readout_tc_kernel<<<grid, 128, kTcSmem, s>>>(maps[0], maps[1], K, sh.o_pad, sh.b_pad, sh.kper, partials, err);
+  if (const int st = d3b_host::check_launch()) return st;
+  readout_reduce_softmax_kernel<<<B, 256, 0, s>>>(partials, counts, temperature, probs, n_opt, sh.ksplit, sh.b_pad,
+                                                  sh.o_pad);
+  return d3b_host::check_launch();
+}
+
+namespace {
+}  // namespace
+
 // ===========================================================================
 // Readout without any allocation.
 //

@@ -6,9 +6,16 @@ d3trt/model/trtllm_stack.py:451-468, identical to hf_stack.py:67-84).
     probs  = softmax(logits / temperature)
     return [row[:count] for row, count in zip(probs.tolist(), counts)]
 
-One kernel launch computes the fp32 dot products, the mask, the temperature
-and the softmax (libd3b200 ``d3b_readout``); the only host work left is the
-device-to-host copy of the result, as in the reference (``.cpu().tolist()``).
+For bf16 hidden rows (the model's final-norm output) the dot products run on the
+tensor cores: the fp32 readout matrix is split once into three bf16 planes that
+carry all of its 24 bits (``d3b_readout_split``, cached per readout tensor), every
+product of a bf16 hidden value with a plane value is exact in fp32, and the
+planes' products accumulate in fp32 (``d3b_readout_planes``): an fp32 dot product
+that differs from the reference's only in summation order. Other hidden dtypes
+take the fp32 FMA kernels (``d3b_readout``). Either way a second kernel adds the
+K splits and applies the mask, the temperature and the softmax; the only host
+work left is the device-to-host copy of the result, as in the reference
+(``.cpu().tolist()``).
 """
 
 from __future__ import annotations
@@ -21,6 +28,27 @@ from .. import _lib
 
 KERNEL_NAME = "sm100a"
 _WORKSPACES: dict[tuple[int, int], torch.Tensor] = {}
+_PARTIALS: dict[tuple[int, int], torch.Tensor] = {}  # the tensor-core path's partial logits (no zeroing needed)
+_PLANES: dict[tuple, torch.Tensor] = {}  # readout matrix -> its three bf16 planes (a few recent ones)
+
+
+def readout_planes(readout: torch.Tensor) -> torch.Tensor:
+    """The three bf16 planes of an fp32 readout matrix on its device, cached by the tensor's
+    storage, shape and version (an in-place change of the matrix makes new planes)."""
+    key = (readout.device.index, readout.data_ptr(), tuple(readout.shape), readout._version)
+    planes = _PLANES.get(key)
+    if planes is None:
+        n_opt, k = readout.shape
+        lib = _lib.lib()
+        planes = torch.empty(int(lib.d3b_readout_planes_size(n_opt, k)) // 2, dtype=torch.bfloat16,
+                             device=readout.device)
+        with torch.cuda.device(readout.device):
+            _lib.check(lib.d3b_readout_split(_lib.ptr(readout), n_opt, k, _lib.ptr(planes), _lib.stream_of(readout)),
+                       "d3b_readout_split")
+        if len(_PLANES) >= 4:
+            _PLANES.pop(next(iter(_PLANES)))
+        _PLANES[key] = planes
+    return planes
 
 
 def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
@@ -61,6 +89,21 @@ def probabilities_tensor(
         return probs
     lib = _lib.lib()
     stream = _lib.stream_of(hidden)
+    if hidden.dtype == torch.bfloat16 and k % 8 == 0 and hidden.data_ptr() % 16 == 0:
+        planes = readout_planes(readout)
+        nbytes = int(lib.d3b_readout_planes_workspace_size(rows, k, n_opt))
+        # its own buffer: d3b_readout's workspace holds ticket counters that must stay zero
+        key = (hidden.device.index, int(stream.value or 0))
+        ws = _PARTIALS.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=hidden.device)
+            _PARTIALS[key] = ws
+        status = lib.d3b_readout_planes(
+            _lib.ptr(hidden), _lib.ptr(planes), _lib.ptr(counts_t), float(temperature), _lib.ptr(probs), rows, k,
+            n_opt, _lib.ptr(ws), ws.numel(), stream,
+        )
+        _lib.check(status, "d3b_readout_planes")
+        return probs
     nbytes = int(lib.d3b_readout_workspace_size(rows, n_opt))
     ws = _workspace(hidden.device, int(stream.value or 0), nbytes)
     status = lib.d3b_readout(

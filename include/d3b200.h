@@ -246,6 +246,27 @@ D3B_API int d3b_readout(const void* hidden, int h_dtype, const float* readout, c
                 d3b_stream_t stream);
 
 /*
+ * The same readout on the tensor cores for bf16 hidden rows (the model's
+ * final-norm output; trtllm_stack.py:451-468 as above). The fp32 readout matrix
+ * is first split, once, into three bf16 planes r0 + r1 + r2 = readout (all 24
+ * bits): d3b_readout_split writes them as [3][o_pad][K] bf16 (o_pad = n_opt
+ * rounded up to 256, padding rows zero) into a buffer of
+ * d3b_readout_planes_size(n_opt, K) bytes. d3b_readout_planes then computes
+ * every logit as sum_p hidden . r_p with exact bf16 x bf16 products and fp32
+ * accumulation (an fp32 dot product in another summation order), split over K
+ * across the SMs, and applies the mask, temperature and softmax like d3b_readout.
+ *   hidden [B, K] bf16 contiguous, 16-byte aligned; K % 8 == 0
+ *   workspace: d3b_readout_planes_workspace_size(B, K, n_opt) bytes (the K
+ *   splits' partial logits; no zero-filling needed), 16-byte aligned
+ */
+D3B_API size_t d3b_readout_planes_size(int n_opt, int K);
+D3B_API int d3b_readout_split(const float* readout, int n_opt, int K, void* planes, d3b_stream_t stream);
+D3B_API size_t d3b_readout_planes_workspace_size(int B, int K, int n_opt);
+D3B_API int d3b_readout_planes(const void* hidden, const void* planes, const int32_t* counts, float temperature,
+                               float* probs, int B, int K, int n_opt, void* workspace, size_t workspace_bytes,
+                               d3b_stream_t stream);
+
+/*
  * The readout above for callers that cannot allocate device memory when they
  * call (for example code that runs during CUDA graph capture, or a host
  * runtime that only hands over its input and output buffers). It has no

@@ -104,6 +104,23 @@ def test_readout_rejects_bad_arguments():
     assert lib.d3b_readout(a, _lib.BF16, a, a, 1.0, a, 8 * 4096 + 1, 64, 255, a, 1 << 40, None) == _lib.EINVAL
 
 
+def test_readout_planes_rejects_bad_arguments():
+    lib = _lib.lib()
+    a = ctypes.c_void_p(256)
+    assert lib.d3b_readout_planes_size(255, 5120) == 3 * 256 * 5120 * 2
+    assert lib.d3b_readout_planes_size(257, 64) == 3 * 512 * 64 * 2
+    need = lib.d3b_readout_planes_workspace_size(255, 5120, 255)
+    assert need >= 256 * 256 * 4  # at least one split of padded partial logits
+    assert lib.d3b_readout_planes(a, a, a, 1.0, a, 255, 5120, 255, a, need - 1, None) == _lib.ENOSPACE
+    assert lib.d3b_readout_planes(a, a, a, 0.0, a, 255, 5120, 255, a, need, None) == _lib.EINVAL
+    assert lib.d3b_readout_planes(a, a, a, 1.0, a, 4, 64, 2000, a, need, None) == _lib.EINVAL
+    assert lib.d3b_readout_planes(a, a, a, 1.0, a, 4, 100, 255, a, 1 << 30, None) == _lib.EUNSUPPORTED  # K % 8
+    assert lib.d3b_readout_planes(ctypes.c_void_p(258), a, a, 1.0, a, 4, 64, 255, a, 1 << 30, None) == _lib.EALIGN
+    assert lib.d3b_readout_planes(a, a, a, 1.0, a, 0, 64, 255, a, 0, None) == _lib.OK  # no rows: nothing to do
+    assert lib.d3b_readout_split(None, 255, 64, a, None) == _lib.EINVAL
+    assert lib.d3b_readout_split(a, 0, 64, a, None) == _lib.EINVAL
+
+
 def test_copy_segments_rejects_bad_arguments():
     lib = _lib.lib()
     seg = _lib.CopySegment

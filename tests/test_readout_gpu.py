@@ -51,3 +51,36 @@ def test_readout_odd_sizes():
         ref = oread.probabilities(hidden.numpy(), readout.numpy(), counts, 0.5)
         got = d3b.probabilities_tensor(hidden.to(DEV), readout.to(DEV), counts, temperature=0.5).cpu().numpy()
         assert np.abs(got - ref).max() <= 1e-5
+
+
+def test_readout_planes_path_against_fp32_path():
+    """bf16 hidden rows take the tensor-core path (the fp32 readout split into three bf16
+    planes, exact products, fp32 accumulation): within 1e-5 of the oracle and of the fp32
+    FMA path (fp32 hidden of the same values), including the model's shape, rows past one
+    128-row tile, options past 256, counts of 1 and n_opt, and a K that is not a multiple
+    of the 64-wide K chunk; an in-place change of the readout makes new planes."""
+    from d3_turbo_trt_b200.model import readout as ro
+
+    g = torch.Generator().manual_seed(23)
+    for rows, k, n_opt in ((255, 5120, 255), (130, 1000, 300), (3, 64, 1), (200, 5128, 1024)):
+        hidden = torch.randn(rows, k, generator=g).to(torch.bfloat16)
+        readout = torch.randn(n_opt, k, generator=g) * 0.02
+        counts = [1 + (i * 37) % n_opt for i in range(rows)]
+        counts[0] = n_opt
+        ref = oread.probabilities(hidden.float().numpy(), readout.numpy(), counts, 0.7)
+        rd = readout.to(DEV)
+        got = d3b.probabilities_tensor(hidden.to(DEV), rd, counts, temperature=0.7)
+        fp32 = d3b.probabilities_tensor(hidden.float().to(DEV), rd, counts, temperature=0.7)
+        assert np.abs(got.cpu().numpy() - ref).max() <= 1e-5, (rows, k, n_opt)
+        assert float((got - fp32).abs().max()) <= 1e-5
+        assert np.argmax(got.cpu().numpy(), 1).tolist() == np.argmax(ref, 1).tolist()
+    # planes follow in-place updates of the readout matrix
+    hidden = torch.randn(8, 256, generator=g).to(torch.bfloat16).to(DEV)
+    rd = (torch.randn(16, 256, generator=g) * 0.05).to(DEV)
+    first = d3b.probabilities_tensor(hidden, rd, [16] * 8, temperature=1.0)
+    rd.mul_(-1.0)
+    second = d3b.probabilities_tensor(hidden, rd, [16] * 8, temperature=1.0)
+    ref = oread.probabilities(hidden.float().cpu().numpy(), rd.cpu().numpy(), [16] * 8, 1.0)
+    assert np.abs(second.cpu().numpy() - ref).max() <= 1e-5
+    assert not torch.equal(first, second)
+    assert len(ro._PLANES) <= 4
