@@ -301,6 +301,16 @@ int launch_k(const GdrParams& p, int beta_dtype, long long blocks, cudaStream_t 
 // P V' runs on tcgen05 into the freed columns 0..127. q, k, v rows and the state's
 // bf16 image arrive by bulk copies during the first phase.
 // ---------------------------------------------------------------------------
+// Waits (bounded, ignoring the abort flag) for a phase of a barrier that bulk
+// copies complete, so a CTA that gave up does not exit with copies into its
+// shared memory in flight.
+__device__ __forceinline__ void settle(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = d3b::smem_u32(bar);
+  const uint64_t t0 = d3b::globaltimer_ns();
+  while (!d3b::mbar_try_wait(addr, parity))
+    if (d3b::globaltimer_ns() - t0 > D3B_WAIT_LIMIT_NS) break;
+}
+
 namespace gdc {
 
 constexpr int KD = 128;             // K = V = 128
@@ -695,6 +705,7 @@ __global__ void __launch_bounds__(THREADS, 1) gdr_chunk_kernel(const __grid_cons
   d3b::tc_fence_before();
   alive = __syncthreads_and(ok) != 0;
   d3b::tc_fence_after();
+  if (!alive) settle(&bars.load, ph);  // no load copy of this item is left in flight
   }
 
   // ---- teardown: every issued MMA and output copy has completed ---------------
@@ -820,15 +831,6 @@ __device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t 
                : "memory");
 }
 
-// Waits (bounded, ignoring the abort flag) for a phase of a barrier that bulk
-// copies complete, so a CTA that gave up does not exit with copies into its
-// shared memory in flight.
-__device__ __forceinline__ void settle(uint64_t* bar, uint32_t parity) {
-  const uint32_t addr = d3b::smem_u32(bar);
-  const uint64_t t0 = d3b::globaltimer_ns();
-  while (!d3b::mbar_try_wait(addr, parity))
-    if (d3b::globaltimer_ns() - t0 > D3B_WAIT_LIMIT_NS) break;
-}
 
 template <typename In, typename BetaT>
 __global__ void __launch_bounds__(P_THREADS, 1)

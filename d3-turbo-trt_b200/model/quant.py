@@ -49,10 +49,13 @@ def _mode_code(mode: str) -> int:
 
 
 def fp8_supported(device: Any) -> bool:
-    """FP8 tensor cores present (reference: quant.py:37-40). These kernels need sm_100."""
+    """FP8 tensor cores present and usable by this library (reference: quant.py:37-40).
+
+    The reference answers True from sm_89 up; the kernels here are built for sm_100a only
+    (arch-specific code does not run on other compute capabilities), so only 10.0 counts."""
     if not torch.cuda.is_available():
         return False
-    return torch.cuda.get_device_capability(torch.device(device)) >= (8, 9)
+    return torch.cuda.get_device_capability(torch.device(device)) == (10, 0)
 
 
 def resolve_mode(mode: str, device: Any, weight_bytes: int | None = None) -> str:

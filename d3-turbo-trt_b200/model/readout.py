@@ -20,6 +20,7 @@ work left is the device-to-host copy of the result, as in the reference
 
 from __future__ import annotations
 
+import weakref
 from typing import Sequence
 
 import torch
@@ -29,14 +30,17 @@ from .. import _lib
 KERNEL_NAME = "sm100a"
 _WORKSPACES: dict[tuple[int, int], torch.Tensor] = {}
 _PARTIALS: dict[tuple[int, int], torch.Tensor] = {}  # the tensor-core path's partial logits (no zeroing needed)
-_PLANES: dict[tuple, torch.Tensor] = {}  # readout matrix -> its three bf16 planes (a few recent ones)
+_PLANES: dict[tuple, tuple] = {}  # readout matrix -> (weak ref to it, its three bf16 planes); a few recent ones
 
 
 def readout_planes(readout: torch.Tensor) -> torch.Tensor:
-    """The three bf16 planes of an fp32 readout matrix on its device, cached by the tensor's
-    storage, shape and version (an in-place change of the matrix makes new planes)."""
+    """The three bf16 planes of an fp32 readout matrix on its device, cached per tensor
+    object, address, shape and version: an in-place change of the matrix makes new planes,
+    and so does a new matrix that the allocator placed where a freed one was (the entry
+    holds a weak reference to the tensor it was made from and is used only for that tensor)."""
     key = (readout.device.index, readout.data_ptr(), tuple(readout.shape), readout._version)
-    planes = _PLANES.get(key)
+    entry = _PLANES.get(key)
+    planes = entry[1] if entry is not None and entry[0]() is readout else None
     if planes is None:
         n_opt, k = readout.shape
         lib = _lib.lib()
@@ -45,15 +49,16 @@ def readout_planes(readout: torch.Tensor) -> torch.Tensor:
         with torch.cuda.device(readout.device):
             _lib.check(lib.d3b_readout_split(_lib.ptr(readout), n_opt, k, _lib.ptr(planes), _lib.stream_of(readout)),
                        "d3b_readout_split")
+        _PLANES.pop(key, None)
         if len(_PLANES) >= 4:
             _PLANES.pop(next(iter(_PLANES)))
-        _PLANES[key] = planes
+        _PLANES[key] = (weakref.ref(readout), planes)
     return planes
 
 
 def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
     """A zero-filled scratch buffer per (device, stream); calls on one stream never overlap."""
-    key = (device.index or 0, stream)
+    key = (device.index if device.index is not None else torch.cuda.current_device(), stream)
     ws = _WORKSPACES.get(key)
     if ws is None or ws.numel() < nbytes:
         ws = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)

@@ -279,7 +279,9 @@ D3B_API int d3b_readout_planes(const void* hidden, const void* planes, const int
  *   Calls on one device share the array: calls whose work overlaps on the
  *   GPU (unordered streams) race and give wrong results.
  *   The first call on a device looks up the array's device address; make it
- *   before any stream capture begins.
+ *   before any stream capture begins. The address is kept per device ordinal
+ *   for the life of the process and is not looked up again after a
+ *   cudaDeviceReset; do not call this entry point on a device after resetting it.
  * Calls no allocating routine (no cudaMalloc / cudaFree).
  */
 D3B_API int d3b_readout_noalloc(const void* hidden, int h_dtype, const float* readout, const int32_t* counts,

@@ -84,3 +84,19 @@ def test_readout_planes_path_against_fp32_path():
     assert np.abs(second.cpu().numpy() - ref).max() <= 1e-5
     assert not torch.equal(first, second)
     assert len(ro._PLANES) <= 4
+
+
+def test_readout_planes_not_reused_for_a_new_matrix_at_a_freed_address():
+    """A readout matrix freed and a new one of the same shape allocated in its place (the
+    caching allocator hands the same block back) gets its own planes, not the freed one's."""
+    g = torch.Generator().manual_seed(31)
+    hidden = torch.randn(16, 512, generator=g).to(torch.bfloat16).to(DEV)
+    counts = [40] * 16
+    rd = (torch.randn(40, 512, generator=g) * 0.05).to(DEV)
+    d3b.probabilities_tensor(hidden, rd, counts, temperature=1.0)
+    addr = rd.data_ptr()
+    del rd
+    rd = (torch.randn(40, 512, generator=g) * 0.05).to(DEV)
+    got = d3b.probabilities_tensor(hidden, rd, counts, temperature=1.0)
+    ref = oread.probabilities(hidden.float().cpu().numpy(), rd.cpu().numpy(), counts, 1.0)
+    assert np.abs(got.cpu().numpy() - ref).max() <= 1e-5, ("same address" if rd.data_ptr() == addr else "moved")
