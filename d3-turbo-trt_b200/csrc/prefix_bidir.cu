@@ -43,6 +43,7 @@
 #include "common.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <queue>
@@ -1231,6 +1232,453 @@ int launch_dual(const CUtensorMap* maps, const Params& prm, dim3 grid, cudaStrea
                          : launch_dual_as<D, FP16, false>(maps, prm, grid, stream);
 }
 
+// ===========================================================================
+// CTA-pair form of the D = 128 kernel (cluster of 2, tcgen05 cta_group::2).
+//
+// Bounds of the one-CTA kernel above, per 128-key tile: tensor 1024 cycles,
+// MUFU ~900, shared memory 160 KB at ~128 B/cycle (~1250 cycles) - the SS
+// QK^T at N = 128 alone reads its operands at the full shared-memory rate. A
+// pair of CTAs on two SMs takes two Q tiles of the same (block, kv head) as one
+// M = 256 operand: S = Q K^T is one M256·N128 MMA whose B operand (the key
+// tile) is split between the CTAs (CTA r holds keys 64r .. 64r+63, both
+// 64-column halves of D), and O += P V one M256·N128 MMA whose B operand (the
+// value tile) is split by columns (CTA r holds all 128 keys, columns
+// 64r .. 64r+63). Each SM then writes 32 KB of K/V per tile instead of 64 and
+// reads 96 KB of operands instead of 128: ~96 KB per tile, under the tensor
+// bound.
+//   rank 0, warp 9  (lane 0)  S[j%2] = Q K_j^T for both CTAs
+//   rank 0, warp 10 (lane 0)  O += P[j%2] V_j for both CTAs
+//   both ranks, warp 8: this CTA's Q tile and key halves; warp 11: value halves;
+//     the loads complete on rank 0's full barriers, which rank 0 arms with the
+//     pair's bytes
+//   both ranks, warps 0-7: softmax and epilogue of this CTA's 128 rows, as in
+//     the one-CTA kernel; the barriers the issuers wait on (s_free, p_full,
+//     o_free) live in rank 0 and count both CTAs' threads, the ones the CTA's
+//     own threads wait on (s_full, p_free, o_final, q_empty, k/v_empty) get the
+//     issuer's commits in both CTAs (tcgen05.commit multicast).
+// Units: pair unit = (block b, kv head g, Q tiles 2t and 2t+1); rank r takes
+// tile 2t + r. Both ranks run the same number of key tiles (the lower tile's
+// count: it always holds the block's first tokens), so a tile with no real
+// token computes rows that its epilogue writes as zeros. Launch: persistent,
+// one cluster per two SMs, clusters walking the pair units; used when every
+// (block, kv head) has an even number of Q tiles.
+// ===========================================================================
+struct CfgPair {
+  static constexpr int D = 128, BN = 128, CH = 64, ROWB = 128, NCH = 2;
+  static constexpr uint32_t LAYOUT = d3b::kLayoutSW128;
+  static constexpr int SBO = 8 * ROWB;
+  static constexpr int Q_BYTES = BM * D * 2;      // this CTA's 128 rows
+  static constexpr int Q_CHUNK = BM * ROWB;
+  static constexpr int K_ROWS = BN / 2;           // this CTA's keys of a key tile
+  static constexpr int K_CHUNK = K_ROWS * ROWB;   // 8 KB
+  static constexpr int SLOT_BYTES = NCH * K_CHUNK;  // 16 KB: a key half, or a value half (128 keys x 64 columns)
+  static constexpr int NSLOT = (227 * 1024 - 4096 - 1024 - Q_BYTES) / SLOT_BYTES;
+  static constexpr int NK = NSLOT / 2 + NSLOT % 2 > 8 ? 8 : NSLOT / 2 + NSLOT % 2;
+  static constexpr int NV = NSLOT - NK > 8 ? 8 : NSLOT - NK;
+  static constexpr int SMEM_BYTES = Q_BYTES + (NK + NV) * SLOT_BYTES + 1024;
+  static constexpr int COL_O = 0, COL_S = 128, COL_P = 384, OH = D / 2;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static_assert(NK >= 2 && NV >= 2, "smem budget");
+};
+
+// Pair unit i of this cluster (persistent: clusters walk the pair units).
+__device__ __forceinline__ bool pair_item(const Params& p, int i, int n_s, uint32_t rank, Work& w) {
+  const int half_tiles = p.tiles >> 1;
+  const int pu = (int)(blockIdx.x >> 1) + i * (int)(gridDim.x >> 1);
+  if (pu >= p.whole_units) return false;  // whole_units counts pair units in this launch
+  const int tp = pu % half_tiles;
+  w.g = (pu / half_tiles) % p.Hkv;
+  w.b = pu / (half_tiles * p.Hkv);
+  w.unit = pu;
+  w.len_b = block_length(p, w.b);
+  w.tok0 = (2 * tp + (int)rank) * p.T;
+  w.a = 0;
+  const int tok_lo = 2 * tp * p.T;
+  w.n = tok_lo >= w.len_b ? 0 : min(p.n_full, n_s + (w.len_b + 127) / 128);
+  return true;
+}
+
+template <int FP16>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(DU_THREADS, 1)
+    prefix_bidir_pair_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapKs,
+                             const __grid_constant__ CUtensorMap mapVs, const __grid_constant__ CUtensorMap mapKq,
+                             const __grid_constant__ CUtensorMap mapVq, const Params p) {
+  using C = CfgPair;
+  constexpr int D = C::D, BN = C::BN;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ BarsDual bars;
+  __shared__ float mref_s[2][BM];
+  __shared__ float lsum_s[2][BM];
+  __shared__ float mlast_s[2][BM];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = d3b::cluster_ctarank();
+  const int G = p.G;
+  const int rows_used = G * p.T;
+  const int n_s = (p.S + BN - 1) / BN;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + C::Q_BYTES;
+  uint8_t* sV = sK + C::NK * C::SLOT_BYTES;
+  volatile int* abort_flag = &bars.abort_flag;
+
+  if (threadIdx.x == 0) {
+    d3b::mbar_init(&bars.q_full, 1);
+    d3b::mbar_init(&bars.q_empty, 1);
+    for (int i = 0; i < 8; ++i) {
+      d3b::mbar_init(&bars.k_full[i], 1);
+      d3b::mbar_init(&bars.k_empty[i], 1);
+      d3b::mbar_init(&bars.v_full[i], 1);
+      d3b::mbar_init(&bars.v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      d3b::mbar_init(&bars.s_full[i], 1);
+      d3b::mbar_init(&bars.s_free[i], 2 * 128);  // rank 0's: both CTAs' group i
+      d3b::mbar_init(&bars.p_full[i], 2 * 128);  // rank 0's: both CTAs' group i
+      d3b::mbar_init(&bars.p_free[i], 1);
+      d3b::mbar_init(&bars.mdone[i], 128);
+    }
+    for (int q = 0; q < 4; ++q) d3b::mbar_init(&bars.xsum[q], 64);
+    d3b::mbar_init(&bars.o_final, 1);
+    d3b::mbar_init(&bars.o_free, 2 * 256);  // rank 0's: both CTAs' epilogues
+    d3b::mbar_init(&bars.drain_qk, 1);
+    d3b::mbar_init(&bars.drain_pv, 1);
+    bars.abort_flag = 0;
+    d3b::fence_barrier_init();
+  }
+  if (rows_used < BM) {  // rows no Q box covers stay zero for every unit
+    const int per_chunk = (BM - rows_used) * C::ROWB / 16;
+    for (int i = threadIdx.x; i < C::NCH * per_chunk; i += DU_THREADS) {
+      const int c = i / per_chunk, o = i % per_chunk;
+      reinterpret_cast<uint4*>(sQ + c * C::Q_CHUNK + rows_used * C::ROWB)[o] = make_uint4(0, 0, 0, 0);
+    }
+    d3b::fence_proxy_async_smem();
+  }
+  if (warp == 9) d3b::tmem_alloc_pair(&bars.tmem_slot, C::TMEM_COLS);
+  d3b::tc_fence_before();
+  d3b::cluster_sync();  // both CTAs' barriers initialised before any remote arrive, load or commit
+  d3b::tc_fence_after();
+  const uint32_t tmem_base = bars.tmem_slot;
+  constexpr uint32_t fmt = FP16 ? 0u : 1u;
+
+  if (warp >= 8) {
+    // Register split as in the one-CTA kernel: 128 * 48 + 256 * 224 <= 384 * 168.
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 48;" ::: "memory");
+   if (warp == 8 || warp == 11) {
+    // ======== TMA producers (both ranks): warp 8 Q and key halves, warp 11 value halves ========
+    if (lane == 0) {
+      const bool is_v = warp == 11;
+      if (is_v) {
+        if (n_s) d3b::tma_prefetch_desc(&mapVs);
+        d3b::tma_prefetch_desc(&mapVq);
+      } else {
+        d3b::tma_prefetch_desc(&mapQ);
+        d3b::tma_prefetch_desc(&mapKq);
+        if (n_s) d3b::tma_prefetch_desc(&mapKs);
+      }
+      const int nslot = is_v ? C::NV : C::NK;
+      uint64_t* fulls = is_v ? bars.v_full : bars.k_full;
+      uint64_t* empties = is_v ? bars.v_empty : bars.k_empty;
+      uint8_t* ring = is_v ? sV : sK;
+      int slot = 0, ie = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      Work w;
+      for (int i = 0; ok && pair_item(p, i, n_s, rank, w); ++i) {
+        if (w.n == 0) continue;
+        if (!is_v) {
+          // this CTA's Q tile: the previous unit's QK^T MMAs have all completed
+          if (ie > 0 && !(ok = d3b::mbar_wait(&bars.q_empty, (uint32_t)(ie - 1) & 1, abort_flag, p.err, kSiteDuQ)))
+            break;
+          if (rank == 0) d3b::mbar_arrive_expect_tx(&bars.q_full, 2 * C::NCH * rows_used * C::ROWB);
+          const uint32_t leader_q = d3b::cluster_addr(&bars.q_full, 0);
+#pragma unroll
+          for (int c = 0; c < C::NCH; ++c)
+            d3b::tma_load_4d_pair(sQ + c * C::Q_CHUNK, &mapQ, leader_q, c * C::CH, w.g * G, w.tok0, w.b);
+        }
+        for (int j = 0; j < w.n; ++j) {
+          if (!(ok = d3b::mbar_wait(&empties[slot], ph ^ 1, abort_flag, p.err, kSiteDuSlotEmpty))) break;
+          // rank 0 arms the slot with both CTAs' bytes; rank 1's copies may land first
+          if (rank == 0) d3b::mbar_arrive_expect_tx(&fulls[slot], 2 * C::SLOT_BYTES);
+          const uint32_t leader_full = d3b::cluster_addr(&fulls[slot], 0);
+          uint8_t* dst = ring + slot * C::SLOT_BYTES;
+          const int kt = w.a + j;  // key tile of the unit
+          if (is_v) {  // all 128 keys, this CTA's 64 columns
+            if (kt < n_s)
+              d3b::tma_load_3d_pair(dst, &mapVs, leader_full, (int)rank * C::CH, kt * BN, w.g);
+            else
+              d3b::tma_load_4d_pair(dst, &mapVq, leader_full, (int)rank * C::CH, (kt - n_s) * BN, w.g, w.b);
+          } else {  // this CTA's 64 keys, both column halves
+#pragma unroll
+            for (int c = 0; c < C::NCH; ++c) {
+              if (kt < n_s)
+                d3b::tma_load_3d_pair(dst + c * C::K_CHUNK, &mapKs, leader_full, c * C::CH,
+                                      kt * BN + (int)rank * C::K_ROWS, w.g);
+              else
+                d3b::tma_load_4d_pair(dst + c * C::K_CHUNK, &mapKq, leader_full, c * C::CH,
+                                      (kt - n_s) * BN + (int)rank * C::K_ROWS, w.g, w.b);
+            }
+          }
+          if (++slot == nslot) { slot = 0; ph ^= 1; }
+        }
+        ++ie;
+      }
+    }
+  } else if (warp == 9) {
+    // ================= QK^T issuer (rank 0) =================
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc_qk = d3b::make_idesc(1, fmt, fmt, 0, 0, 2 * BM, BN);
+      const uint64_t dq0 = d3b::make_smem_desc(d3b::smem_u32(sQ), 16, C::SBO, C::LAYOUT);
+      const uint64_t dk0 = d3b::make_smem_desc(d3b::smem_u32(sK), 16, C::SBO, C::LAYOUT);
+      bool ok = true;
+      int jg = 0, ie = 0;
+      Work w;
+      for (int i = 0; ok && pair_item(p, i, n_s, rank, w); ++i) {
+        if (w.n == 0) continue;
+        if (!(ok = d3b::mbar_wait(&bars.q_full, (uint32_t)ie & 1, abort_flag, p.err, kSiteDuQ))) break;
+        for (int j = 0; j < w.n; ++j, ++jg) {
+          const int sb = jg & 1;
+          const uint32_t u = (uint32_t)(jg >> 1);
+          // S[sb] was last read by both CTAs' softmax of tile jg-2
+          if (!(ok = d3b::mbar_wait(&bars.s_free[sb], (u & 1) ^ 1, abort_flag, p.err, kSiteDuSFree))) break;
+          const int slot = jg % C::NK;
+          if (!(ok = d3b::mbar_wait(&bars.k_full[slot], (uint32_t)(jg / C::NK) & 1, abort_flag, p.err,
+                                    kSiteDuSlotK)))
+            break;
+          d3b::tc_fence_after();
+          const uint64_t dk = dk0 + (uint64_t)((slot * C::SLOT_BYTES) >> 4);
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const int c = (k * 16) / C::CH, off = ((k * 16) % C::CH) * 2;
+            d3b::mma_f16_ss_pair(tmem_base + C::COL_S + sb * BN, dq0 + (uint64_t)((c * C::Q_CHUNK + off) >> 4),
+                                 dk + (uint64_t)((c * C::K_CHUNK + off) >> 4), idesc_qk, k > 0 ? 1u : 0u);
+          }
+          d3b::mma_commit_pair(&bars.s_full[sb], 0x3);
+          d3b::mma_commit_pair(&bars.k_empty[slot], 0x3);
+        }
+        if (!ok) break;
+        d3b::mma_commit_pair(&bars.q_empty, 0x3);  // the unit's QK^T MMAs have read both Q tiles
+        ++ie;
+      }
+      d3b::mma_commit_pair(&bars.drain_qk, 0x1);
+      const uint32_t addr = d3b::smem_u32(&bars.drain_qk);
+      const uint64_t t0 = d3b::globaltimer_ns();
+      while (!d3b::mbar_try_wait(addr, 0)) {
+        if (d3b::globaltimer_ns() - t0 > D3B_WAIT_LIMIT_NS) {
+          d3b::record_device_error(p.err, kSiteDuDrain);
+          break;
+        }
+      }
+    }
+  } else if (warp == 10) {
+    // ================= PV issuer (rank 0) =================
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc_pv = d3b::make_idesc(1, fmt, fmt, 0, 1, 2 * BM, D);
+      const uint64_t dv0 = d3b::make_smem_desc(d3b::smem_u32(sV), C::SLOT_BYTES, C::SBO, C::LAYOUT);
+      bool ok = true;
+      int jg = 0, ie = 0;
+      Work w;
+      for (int i = 0; ok && pair_item(p, i, n_s, rank, w); ++i) {
+        if (w.n == 0) continue;
+        for (int j = 0; j < w.n; ++j, ++jg) {
+          const int sb = jg & 1;
+          const uint32_t u = (uint32_t)(jg >> 1);
+          if (!(ok = d3b::mbar_wait(&bars.p_full[sb], u & 1, abort_flag, p.err, kSiteDuPFull))) break;
+          // both CTAs' epilogues have read the previous unit's O
+          if (j == 0 && ie > 0 &&
+              !(ok = d3b::mbar_wait(&bars.o_free, (uint32_t)(ie - 1) & 1, abort_flag, p.err, kSiteDuFinal)))
+            break;
+          const int slot = jg % C::NV;
+          if (!(ok = d3b::mbar_wait(&bars.v_full[slot], (uint32_t)(jg / C::NV) & 1, abort_flag, p.err,
+                                    kSiteDuSlotV)))
+            break;
+          d3b::tc_fence_after();
+          const uint64_t dv = dv0 + (uint64_t)((slot * C::SLOT_BYTES) >> 4);
+#pragma unroll
+          for (int k = 0; k < BN / 16; ++k)
+            d3b::mma_f16_ts_pair(tmem_base + C::COL_O, tmem_base + C::COL_P + sb * (BN / 2) + k * 8,
+                                 dv + (uint64_t)((k * 16 * C::ROWB) >> 4), idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+          d3b::mma_commit_pair(&bars.p_free[sb], 0x3);
+          d3b::mma_commit_pair(&bars.v_empty[slot], 0x3);
+        }
+        if (!ok) break;
+        d3b::mma_commit_pair(&bars.o_final, 0x3);  // both CTAs' O hold the unit's PV(0..n-1)
+        ++ie;
+      }
+      d3b::mma_commit_pair(&bars.drain_pv, 0x1);
+      const uint32_t addr = d3b::smem_u32(&bars.drain_pv);
+      const uint64_t t0 = d3b::globaltimer_ns();
+      while (!d3b::mbar_try_wait(addr, 0)) {
+        if (d3b::globaltimer_ns() - t0 > D3B_WAIT_LIMIT_NS) {
+          d3b::record_device_error(p.err, kSiteDuDrain);
+          break;
+        }
+      }
+    }
+  }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;" ::: "memory");
+    // ================= softmax + epilogue (warps 0-7 of both ranks) =================
+    // As in the one-CTA kernel, on this CTA's 128 rows; the arrivals the issuers
+    // wait for go to rank 0's barriers.
+    const int wg = warp >> 2, quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
+    const uint32_t col_s = C::COL_S + wg * BN, col_p = C::COL_P + wg * (BN / 2);
+    const uint32_t s_free_r = d3b::cluster_addr(&bars.s_free[wg], 0);
+    const uint32_t p_full_r = d3b::cluster_addr(&bars.p_full[wg], 0);
+    const uint32_t o_free_r = d3b::cluster_addr(&bars.o_free, 0);
+    const float sl2 = p.scale_log2;
+    bool ok = true;
+    int jg = 0, ie = 0;
+    Work w;
+    for (int i = 0; ok && pair_item(p, i, n_s, rank, w); ++i) {
+      if (w.n == 0) {
+        if (wg == 0) zero_tile_rows<D>(p, w.b, w.g, w.tok0, quarter, lane);
+        continue;
+      }
+      float m_last = -INFINITY, l_sum = 0.f;
+      for (int j = (wg ^ jg) & 1; j < w.n; j += 2) {
+        const int t = jg + j;
+        const uint32_t u = (uint32_t)(t >> 1);
+        if (!d3b::warp_wait(&bars.s_full[wg], u & 1, abort_flag, p.err, kSiteDuSFull)) { ok = false; break; }
+        d3b::tc_fence_after();
+        float s[BN];
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c)
+          d3b::tmem_ld32(lane_addr + col_s + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&s[c * 32]));
+        d3b::tmem_wait_ld();
+        d3b::tc_fence_before();
+        d3b::mbar_arrive_cluster(s_free_r);
+        const int kt = w.a + j;
+        const int valid = kt < n_s ? p.S - kt * BN : w.len_b - (kt - n_s) * BN;
+        if (valid < BN) {
+#pragma unroll
+          for (int c = 0; c < BN; ++c)
+            if (c >= valid) s[c] = -INFINITY;
+        }
+        const float m_tile = max_n<BN>(s) * sl2;
+        float m_prev = -INFINITY;
+        if (t > 0) {
+          if (!d3b::warp_wait(&bars.mdone[(t - 1) & 1], (uint32_t)((t - 1) >> 1) & 1, abort_flag, p.err,
+                              kSiteDuXMax)) {
+            ok = false;
+            break;
+          }
+          if (j > 0) m_prev = mref_s[(t - 1) & 1][r];
+        }
+        const bool rescale = __any_sync(0xffffffffu, m_tile > m_prev + kRescaleThreshold);
+        const float m_new = rescale ? fmaxf(m_prev, m_tile) : m_prev;
+        mref_s[wg][r] = m_new;
+        d3b::mbar_arrive(&bars.mdone[wg]);
+        if (rescale && j > 0) {
+          if (!d3b::warp_wait(&bars.p_free[(t - 1) & 1], (uint32_t)((t - 1) >> 1) & 1, abort_flag, p.err,
+                              kSiteDuPFree)) {
+            ok = false;
+            break;
+          }
+          d3b::tc_fence_after();
+          scale_cols<D>(lane_addr + C::COL_O, d3b::ex2_approx(m_prev - m_new));
+        }
+        if (!d3b::warp_wait(&bars.p_free[wg], (u & 1) ^ 1, abort_flag, p.err, kSiteDuPFree)) { ok = false; break; }
+        d3b::tc_fence_after();
+        float rowsum = 0.f;
+#pragma unroll
+        for (int qq = 0; qq < BN / 32; ++qq) {
+          uint32_t pk[16];
+          rowsum += exp_row<32, FP16, D3B_POLY8>(s + qq * 32, sl2, m_new, pk);
+          d3b::tmem_st16(lane_addr + col_p + qq * 16, pk);
+        }
+        d3b::tmem_wait_st();
+        d3b::tc_fence_before();
+        d3b::mbar_arrive_cluster(p_full_r);
+        l_sum = (m_last == m_new ? l_sum : l_sum * d3b::ex2_approx(m_last - m_new)) + rowsum;
+        m_last = m_new;
+      }
+      if (ok) ok = d3b::warp_wait(&bars.o_final, (uint32_t)ie & 1, abort_flag, p.err, kSiteDuFinal);
+      if (ok) {
+        lsum_s[wg][r] = l_sum;
+        mlast_s[wg][r] = m_last;
+        d3b::mbar_arrive(&bars.xsum[quarter]);
+        ok = d3b::warp_wait(&bars.xsum[quarter], (uint32_t)ie & 1, abort_flag, p.err, kSiteDuXMax);
+      }
+      if (!ok) break;
+      d3b::tc_fence_after();
+      const float m0 = mlast_s[0][r], m1 = mlast_s[1][r];
+      const float m_fin = fmaxf(m0, m1);
+      const float l = lsum_s[0][r] * d3b::ex2_approx(m0 - m_fin) + lsum_s[1][r] * d3b::ex2_approx(m1 - m_fin);
+      const int tok = w.tok0 + r / G, h = r % G;
+      const bool in_tensor = r < rows_used && tok < p.L;
+      const bool real = tok < w.len_b;
+      const float inv_l = 1.f / l;
+      uint16_t* dst_row = static_cast<uint16_t*>(p.out) + (int64_t)w.b * p.out_sb +
+                          (int64_t)(w.g * G + h) * p.out_sh + (int64_t)tok * p.out_sl + wg * C::OH;
+      uint32_t o[C::OH];
+#pragma unroll
+      for (int c = 0; c < C::OH / 32; ++c)
+        d3b::tmem_ld32(lane_addr + C::COL_O + wg * C::OH + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[c * 32]));
+      d3b::tmem_wait_ld();
+      // O is in registers: the next unit's first PV may overwrite it
+      d3b::tc_fence_before();
+      d3b::mbar_arrive_cluster(o_free_r);
+      if (in_tensor) {
+        uint4* dst = reinterpret_cast<uint4*>(dst_row);
+#pragma unroll
+        for (int i8 = 0; i8 < C::OH / 8; ++i8) {
+          uint32_t v[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            v[k] = real ? pack2<FP16>(__uint_as_float(o[8 * i8 + 2 * k]) * inv_l,
+                                      __uint_as_float(o[8 * i8 + 2 * k + 1]) * inv_l)
+                        : 0u;
+          dst[i8] = make_uint4(v[0], v[1], v[2], v[3]);
+        }
+      }
+      jg += w.n;
+      ++ie;
+    }
+  }
+
+  __syncwarp();  // lanes that skipped a role loop rejoin before the aligned cluster barrier
+  d3b::tc_fence_before();
+  d3b::cluster_sync();  // rank 0's MMAs (which write both TMEMs) are drained before either CTA frees TMEM
+  d3b::tc_fence_after();
+  if (warp == 9) d3b::tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+}
+
+template <int FP16>
+int launch_pair(const CUtensorMap* maps, const Params& prm, int pair_units, cudaStream_t stream) {
+  using C = CfgPair;
+  static int attr_set[64] = {0};
+  const int dev = d3b_host::current_device();
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(prefix_bidir_pair_kernel<FP16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::SMEM_BYTES) != cudaSuccess)
+      return D3B_ECUDA;
+    attr_set[dev] = 1;
+  }
+  // Pairs that fit at once (an SM left alone in its GPC takes none), queried once per device.
+  static int max_pairs_of[64] = {0};
+  int max_pairs = (dev >= 0 && dev < 64) ? max_pairs_of[dev] : 0;
+  if (max_pairs <= 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 256);
+    cfg.blockDim = dim3(DU_THREADS);
+    cfg.dynamicSmemBytes = C::SMEM_BYTES;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, prefix_bidir_pair_kernel<FP16>, &cfg) != cudaSuccess ||
+        clusters <= 0) {
+      cudaGetLastError();
+      clusters = d3b_host::num_sms(dev) / 2;
+    }
+    max_pairs = clusters;
+    if (dev >= 0 && dev < 64) max_pairs_of[dev] = clusters;
+  }
+  const int pairs = std::max(1, std::min(pair_units, max_pairs));
+  prefix_bidir_pair_kernel<FP16><<<dim3(2 * pairs), DU_THREADS, C::SMEM_BYTES, stream>>>(maps[0], maps[5], maps[2],
+                                                                                         maps[6], maps[4], prm);
+  return d3b_host::check_launch();
+}
+
 template <int D, int BN, int FP16>
 int launch(const CUtensorMap* maps, const Params& prm, dim3 grid, cudaStream_t stream) {
   using C = Cfg<D, BN>;
@@ -1346,6 +1794,21 @@ TailPlan cached_plan(int units, int n, int P) {
   return t;
 }
 
+// The CTA-pair kernel serves D = 128 with an even number of Q tiles per
+// (block, kv head) in long launches: at least kPairMinWaves units per SM and no
+// cut tail. B200 timings against the one-CTA kernel: 64 blocks of 64 tokens
+// over a 16384-token state (6.9 units per SM) 0.825 vs 0.855 ms; config 3a
+// (1.7 units per SM) 77 vs 76 us, so short launches stay on one CTA per unit.
+// D3B_ATTN_PAIR=0 in the environment turns it off (read once per process).
+constexpr int64_t kPairMinWaves = 4;
+bool pair_kernel_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("D3B_ATTN_PAIR");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 // Workspace layout: the per-unit counts first, in a region of fixed size for
 // every shape (split_units < SMs <= kMaxCounts), so partial slots written for
 // one shape never land where another shape's counts must read zero; then one
@@ -1394,7 +1857,8 @@ static int prefix_bidir_impl(const void* q, const int64_t* q_strides, const void
   const int BN = D == 256 ? 64 : 128;
   const int T = BM / G;
 
-  CUtensorMap maps[5];
+  // 0 Q, 1/2 state K/V, 3/4 own K/V; the pair kernel's key halves: 5 state K, 6 own K (64-key boxes)
+  CUtensorMap maps[7];
   int rc;
   {  // Q: [B, H, L, D] -> dims {D, H, L, B}, box {CH, G, T, 1}
     const uint64_t dims[4] = {(uint64_t)D, (uint64_t)H, (uint64_t)L, (uint64_t)B};
@@ -1408,6 +1872,10 @@ static int prefix_bidir_impl(const void* q, const int64_t* q_strides, const void
     const uint32_t box[4] = {(uint32_t)CH, (uint32_t)BN, 1, 1};
     if ((rc = d3b_host::encode_tiled(&maps[3], dt, 4, k_q, dims, st, box, sw))) return rc;
     if ((rc = d3b_host::encode_tiled(&maps[4], dt, 4, v_q, dims, st, box, sw))) return rc;
+    if (D == 128) {
+      const uint32_t half[4] = {(uint32_t)CH, (uint32_t)BN / 2, 1, 1};
+      if ((rc = d3b_host::encode_tiled(&maps[6], dt, 4, k_q, dims, st, half, sw))) return rc;
+    }
   }
   if (S > 0) {  // state K/V: [Hkv, S, D] -> dims {D, S, Hkv}, box {CH, BN, 1}
     const uint64_t dims[3] = {(uint64_t)D, (uint64_t)S, (uint64_t)Hkv};
@@ -1415,9 +1883,14 @@ static int prefix_bidir_impl(const void* q, const int64_t* q_strides, const void
     const uint32_t box[3] = {(uint32_t)CH, (uint32_t)BN, 1};
     if ((rc = d3b_host::encode_tiled(&maps[1], dt, 3, k_state, dims, st, box, sw))) return rc;
     if ((rc = d3b_host::encode_tiled(&maps[2], dt, 3, v_state, dims, st, box, sw))) return rc;
+    if (D == 128) {
+      const uint32_t half[3] = {(uint32_t)CH, (uint32_t)BN / 2, 1};
+      if ((rc = d3b_host::encode_tiled(&maps[5], dt, 3, k_state, dims, st, half, sw))) return rc;
+    }
   } else {  // never read when S == 0
     maps[1] = maps[3];
     maps[2] = maps[4];
+    maps[5] = maps[6];
   }
 
   Params prm;
@@ -1464,13 +1937,21 @@ static int prefix_bidir_impl(const void* q, const int64_t* q_strides, const void
     }
   }
   if (ctas > 0x7FFFFFFF) return D3B_EINVAL;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t sms = d3b_host::num_sms(d3b_host::current_device());
+  if (D == 128 && tiles % 2 == 0 && !prm.split_units && units >= kPairMinWaves * sms && pair_kernel_enabled()) {
+    // CTA pairs: both Q tiles of a pair unit share every key and value tile
+    prm.whole_units = (int)(units / 2);
+    prm.part = nullptr;
+    prm.count = nullptr;
+    return dtype == D3B_F16 ? launch_pair<1>(maps, prm, prm.whole_units, s)
+                            : launch_pair<0>(maps, prm, prm.whole_units, s);
+  }
   const dim3 grid((unsigned)tiles, Hkv, B);
   // D <= 128: one CTA per unit or piece in a split launch, else a persistent
   // grid of at most one CTA per SM looping over the units
-  const int64_t sms = d3b_host::num_sms(d3b_host::current_device());
   const dim3 grid_dual = prm.split_units ? dim3((unsigned)ctas)
                                          : dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(units, sms)));
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   return dtype == D3B_F16 ? dispatch<1>(D, maps, prm, grid, grid_dual, s)
                           : dispatch<0>(D, maps, prm, grid, grid_dual, s);
 }

@@ -303,3 +303,36 @@ def test_persistent_units_ragged_against_oracle(B, H, Hkv, S, L, D, dtype, seed)
     assert float((got - ref).abs().max()) <= TOL
     for b, n in enumerate(lens):
         assert bool((got[b, :, n:] == 0).all())
+
+
+@pytest.mark.parametrize("B,H,Hkv,S,L,dtype,seed", [(40, 32, 4, 1000, 64, torch.bfloat16, 51),
+                                                     (160, 16, 2, 300, 128, torch.float16, 52)])
+def test_cta_pair_kernel_ragged_against_oracle(B, H, Hkv, S, L, dtype, seed):
+    """Shapes the CTA-pair kernel serves (head_dim 128, an even number of Q tiles
+    per block and kv head, at least four units per SM, no cut tail): ragged
+    blocks where the upper Q tile of a pair holds no real token while the lower
+    one does (its rows are computed and written as zeros), pairs with no real
+    token at all, empty blocks, fp16 and bf16. Two launches give the same bits."""
+    D = 128
+    g = torch.Generator().manual_seed(seed)
+    q = _rand((B, H, L, D), g, dtype)
+    ks, vs = _rand((Hkv, S, D), g, dtype), _rand((Hkv, S, D), g, dtype)
+    kq, vq = _rand((B, Hkv, L, D), g, dtype), _rand((B, Hkv, L, D), g, dtype)
+    T = 128 // (H // Hkv)
+    lens = torch.randint(0, L + 1, (B,), generator=g)
+    lens[::5] = 2 * T + 3   # the pair (tiles 2, 3): lower tile partly real, upper tile empty
+    lens[1::7] = T - 1      # the pair (tiles 0, 1): upper tile empty; later pairs empty
+    lens[2::9] = 0
+    lens[3::11] = L
+    lens = lens.tolist()
+    args = (q.to(DEV), ks.to(DEV), vs.to(DEV), kq.to(DEV), vq.to(DEV), lens)
+    out = pb.prefix_bidir_attention(*args, scale=D**-0.5)
+    out_again = pb.prefix_bidir_attention(*args, scale=D**-0.5)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    assert torch.equal(out, out_again)
+    ref = oattn.questions(q, ks, vs, kq, vq, lens, D**-0.5, dtype=torch.float32)
+    got = out.float().cpu()
+    assert float((got - ref).abs().max()) <= TOL
+    for b, n in enumerate(lens):
+        assert bool((got[b, :, n:] == 0).all())
