@@ -391,10 +391,13 @@ def main():
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(pipe.copy_in)
+    cur = torch.cuda.current_stream()
+    e0.record(cur)
+    pipe.wait_stream(cur)
     for i in range(args.steps):
         pipe.submit(host["q"], host["kq"], host["vq"], lens_list, host_outs[i % depth])
-    e1.record(pipe.copy_out)
+    pipe.join(cur)
+    e1.record(cur)
     pipe.synchronize()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
