@@ -95,9 +95,52 @@ __device__ __noinline__ uint2 exact_codes8_bf16(uint4 raw, float scale) {
   for (int i = 0; i < 4; ++i) c[i] = exact_codes2<MODE>(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u), scale);
   return make_uint2(c[0] | (c[1] << 16), c[2] | (c[3] << 16));
 }
+// (d0, d1) = (a0, a1) * (k, k) + (c, c), one packed fp32x2 FMA, one rounding
+__device__ __forceinline__ void fma2_kc(float& d0, float& d1, float a0, float a1, float k, float c) {
+  asm("{.reg .b64 x, y, z; mov.b64 x, {%2, %3}; mov.b64 y, {%4, %4}; mov.b64 z, {%5, %5}; "
+      "fma.rn.f32x2 x, x, y, z; mov.b64 {%0, %1}, x;}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(k), "f"(c));
+}
+
+// int8 bracket codes of eight bf16 values, without float-to-int conversions:
+// RN(y + 1.5 * 2^23) for |y| < 2^22 is the integer nearest y (ties to even, the
+// shifter's last bit being even) plus 0x4B400000 in its bit pattern, so the low
+// byte of the bits is rint(y) as a two's-complement int8. The bracket ends are
+// the exact products v * (1 -+ 2^-21), each rounded once, straight to an
+// integer, by the fused multiply-add; byte permutes gather four codes a word.
+__device__ __forceinline__ void int8_bracket8(uint4 raw, float rcp, uint2& lo, uint2& hi) {
+  constexpr float kLo = 1.0f - 0x1p-21f, kHi = 1.0f + 0x1p-21f, kShift = 12582912.f;
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  uint32_t a[8], b[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float v0, v1, l0, l1, h0, h1;
+    mul2(v0, v1, __uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u), rcp);
+    fma2_kc(l0, l1, v0, v1, kLo, kShift);
+    fma2_kc(h0, h1, v0, v1, kHi, kShift);
+    a[2 * i] = __float_as_uint(l0);
+    a[2 * i + 1] = __float_as_uint(l1);
+    b[2 * i] = __float_as_uint(h0);
+    b[2 * i + 1] = __float_as_uint(h1);
+  }
+  lo.x = __byte_perm(__byte_perm(a[0], a[1], 0x0040), __byte_perm(a[2], a[3], 0x0040), 0x5410);
+  lo.y = __byte_perm(__byte_perm(a[4], a[5], 0x0040), __byte_perm(a[6], a[7], 0x0040), 0x5410);
+  hi.x = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
+  hi.y = __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410);
+}
+
 // Eight codes of eight bf16 values (one 16-byte load -> one 8-byte store).
 template <int MODE>
 __device__ __forceinline__ uint2 quant8_bf16(uint4 raw, float scale, float rcp) {
+  if (MODE == D3B_MODE_INT8) {
+    // |v| <= 127 (1 + 2^-21) because |x| <= amax: the reference's clamp to +-127
+    // never changes a code here, and the shifter's range holds
+    uint2 lo, hi;
+    int8_bracket8(raw, rcp, lo, hi);
+    if (__builtin_expect((lo.x == hi.x) & (lo.y == hi.y), 1)) return lo;
+    return exact_codes8_bf16<MODE>(raw, scale);
+  }
   uint32_t l0, l1, l2, l3, h0, h1, h2, h3;
   pair_codes<MODE>(raw.x, rcp, l0, h0);
   pair_codes<MODE>(raw.y, rcp, l1, h1);
