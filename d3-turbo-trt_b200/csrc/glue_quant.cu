@@ -176,6 +176,99 @@ __global__ void __launch_bounds__(kNormWarps * 32) gated_rmsnorm_quant_kernel(
   }
 }
 
+// The same, one CTA of NT threads per token row for rows of 2048 to 6144 values (the
+// model's 48 x 128 = 6144): each thread holds NV <= 3 vectors, so many rows are in
+// flight per SM (the warp-per-row form above holds 24 vectors per lane and ~12 warps
+// per SM). Vector v = t + NT * k of the row sits in thread t, so a head's LPH vectors
+// are still LPH consecutive lanes of one warp (NT is a multiple of 32) and its sum of
+// squares is the same sub-warp shuffle reduction; the row's max|out| goes through
+// shared memory.
+template <int MODE, int NT, int NV, int LPH>
+__global__ void __launch_bounds__(NT) gated_rmsnorm_quant_cta_kernel(
+    const uint16_t* __restrict__ x, int64_t ldx, const uint16_t* __restrict__ z, int64_t ldz,
+    const uint16_t* __restrict__ w, float eps, int64_t K, uint16_t* __restrict__ out, uint8_t* __restrict__ q,
+    float* __restrict__ scale_out) {
+  __shared__ uint32_t wmax[NT / 32];
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int64_t row = blockIdx.x;
+  const int nvec = (int)(K / 8);
+  const float inv_d = 1.0f / (float)(LPH * 8);
+  float wv[8];
+  {
+    const uint4 ww = __ldg(reinterpret_cast<const uint4*>(w) + (tid % LPH));
+    const uint32_t wa[4] = {ww.x, ww.y, ww.z, ww.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      wv[2 * i] = lo_bf(wa[i]);
+      wv[2 * i + 1] = hi_bf(wa[i]);
+    }
+  }
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx);
+  const uint4* zr = reinterpret_cast<const uint4*>(z + row * ldz);
+  uint4 xs[NV], zs[NV];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {  // every load in flight before any arithmetic
+    const int v = tid + NT * k;
+    const bool in = v < nvec;
+    xs[k] = in ? __ldg(xr + v) : make_uint4(0, 0, 0, 0);
+    zs[k] = in ? __ldg(zr + v) : make_uint4(0, 0, 0, 0);
+  }
+  uint4 a[NV];
+  uint32_t m0 = 0, m1 = 0;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const bool in = tid + NT * k < nvec;  // uniform per head: heads never straddle the row's end
+    const uint32_t xw[4] = {xs[k].x, xs[k].y, xs[k].z, xs[k].w}, zw[4] = {zs[k].x, zs[k].y, zs[k].z, zs[k].w};
+    float xf[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      xf[2 * i] = lo_bf(xw[i]);
+      xf[2 * i + 1] = hi_bf(xw[i]);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(xf[i], xf[i], ss);
+#pragma unroll
+    for (int o = LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rstd = rsqrtf(ss * inv_d + eps);
+    uint32_t r[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float y0 = round_bf(__fmul_rn(wv[2 * i], round_bf(__fmul_rn(xf[2 * i], rstd))));
+      const float y1 = round_bf(__fmul_rn(wv[2 * i + 1], round_bf(__fmul_rn(xf[2 * i + 1], rstd))));
+      r[i] = pack_bf(__fmul_rn(y0, silu(lo_bf(zw[i]))), __fmul_rn(y1, silu(hi_bf(zw[i]))));
+    }
+    a[k] = in ? make_uint4(r[0], r[1], r[2], r[3]) : make_uint4(0, 0, 0, 0);
+    m0 = umax2(m0, a[k].x & 0x7FFF7FFFu);
+    m1 = umax2(m1, a[k].y & 0x7FFF7FFFu);
+    m0 = umax2(m0, a[k].z & 0x7FFF7FFFu);
+    m1 = umax2(m1, a[k].w & 0x7FFF7FFFu);
+  }
+  if (out != nullptr) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+      if (tid + NT * k < nvec) reinterpret_cast<uint4*>(out + row * K)[tid + NT * k] = a[k];
+  }
+  if constexpr (MODE != D3B_MODE_NONE) {
+    uint32_t m = umax2(m0, m1);
+    m = max(m & 0xFFFFu, m >> 16);  // the largest |out| bit pattern (non-negative bf16 order as integers)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) wmax[tid >> 5] = m;
+    __syncthreads();
+    m = wmax[0];
+#pragma unroll
+    for (int i = 1; i < NT / 32; ++i) m = max(m, wmax[i]);
+    const float scale = __fdiv_rn(fmaxf(__uint_as_float(m << 16), 1e-12f), MODE == D3B_MODE_FP8 ? 448.f : 127.f);
+    const float rcp = __frcp_rn(scale);
+    if (tid == 0) scale_out[row] = scale;
+    uint8_t* qr = q + row * K;
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+      if (tid + NT * k < nvec) *reinterpret_cast<uint2*>(qr + (int64_t)(tid + NT * k) * 8) = quant8_bf16<MODE>(a[k], scale, rcp);
+  }
+}
+
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 template <int MODE, int NV>
@@ -204,9 +297,27 @@ void norm_mode(int mode, const uint16_t* x, int64_t ldx, const uint16_t* z, int6
     gated_rmsnorm_quant_kernel<D3B_MODE_NONE, NV, LPH><<<grid, kNormWarps * 32, 0, s>>>(x, ldx, z, ldz, w, eps, M, K, out, q, sc);
 }
 
+template <int NV, int LPH>
+void norm_cta_mode(int mode, const uint16_t* x, int64_t ldx, const uint16_t* z, int64_t ldz, const uint16_t* w,
+                   float eps, int64_t M, int64_t K, uint16_t* out, uint8_t* q, float* sc, cudaStream_t s) {
+  constexpr int NT = 256;
+  if (mode == D3B_MODE_FP8)
+    gated_rmsnorm_quant_cta_kernel<D3B_MODE_FP8, NT, NV, LPH><<<(unsigned)M, NT, 0, s>>>(x, ldx, z, ldz, w, eps, K, out, q, sc);
+  else if (mode == D3B_MODE_INT8)
+    gated_rmsnorm_quant_cta_kernel<D3B_MODE_INT8, NT, NV, LPH><<<(unsigned)M, NT, 0, s>>>(x, ldx, z, ldz, w, eps, K, out, q, sc);
+  else
+    gated_rmsnorm_quant_cta_kernel<D3B_MODE_NONE, NT, NV, LPH><<<(unsigned)M, NT, 0, s>>>(x, ldx, z, ldz, w, eps, K, out, q, sc);
+}
+
 template <int LPH>
 int norm_nv(int mode, const uint16_t* x, int64_t ldx, const uint16_t* z, int64_t ldz, const uint16_t* w, float eps,
             int64_t M, int64_t K, uint16_t* out, uint8_t* q, float* sc, cudaStream_t s) {
+  const int64_t nvec = K / 8;
+  if (nvec >= 256 && nvec <= 256 * 3 && M <= 0x7FFFFFFF) {  // one CTA per row (rows of 2048 to 6144 values)
+    if (nvec <= 256 * 2) norm_cta_mode<2, LPH>(mode, x, ldx, z, ldz, w, eps, M, K, out, q, sc, s);
+    else norm_cta_mode<3, LPH>(mode, x, ldx, z, ldz, w, eps, M, K, out, q, sc, s);
+    return d3b_host::check_launch();
+  }
   const int nv = (int)((K / 8 + 31) / 32);
   if (nv <= 8) norm_mode<8, LPH>(mode, x, ldx, z, ldz, w, eps, M, K, out, q, sc, s);
   else if (nv <= 16) norm_mode<16, LPH>(mode, x, ldx, z, ldz, w, eps, M, K, out, q, sc, s);
