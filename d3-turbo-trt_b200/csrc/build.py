@@ -24,7 +24,7 @@ PKG = CSRC.parent
 ROOT = PKG.parent
 BUILD = PKG / "_build"
 LIB = PKG / "libd3b200.so"
-SOURCES = ["capi.cu", "act_quant.cu", "norm_quant.cu", "readout.cu", "w8a8_gemm.cu", "prefix_bidir.cu", "snapshot.cu", "gated_delta.cu", "causal_conv.cu", "glue_quant.cu"]
+SOURCES = ["capi.cu", "act_quant.cu", "norm_quant.cu", "readout.cu", "w8a8_gemm.cu", "prefix_bidir.cu", "snapshot.cu", "gated_delta.cu", "causal_conv.cu", "glue_quant.cu", "qk_norm_rope.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
     "-O3",

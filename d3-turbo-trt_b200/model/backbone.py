@@ -272,14 +272,16 @@ class D3Backbone:
         c = self.config
         D, Hq, Hkv = c.head_dim, c.num_attention_heads, c.num_key_value_heads
         qg = L["q_proj"].from_codes(q, s, None).view(rows, T, Hq, 2 * D)
-        query, gate = qg[..., :D], qg[..., D:]
-        query = rms_norm(query, L["q_norm"], c.rms_norm_eps).transpose(1, 2)
-        key = rms_norm(L["k_proj"].from_codes(q, s, None).view(rows, T, Hkv, D), L["k_norm"], c.rms_norm_eps)
-        key = key.transpose(1, 2)
-        # the kernels read K and V through one set of strides: V in K's [B, Hkv, T, D] layout
-        value = L["v_proj"].from_codes(q, s, None).view(rows, T, Hkv, D).transpose(1, 2).contiguous()
+        gate = qg[..., D:]
         cos, sin = rope
-        query, key = apply_rotary(query, key, cos, sin)
+        # q_norm / k_norm and the partial rotary embedding in one kernel each, written
+        # token-major [rows, T, heads, D]; the attention reads [rows, heads, T, D] views
+        query = fused.qk_norm_rope(qg[..., :D], L["q_norm"], cos, sin, c.rms_norm_eps).transpose(1, 2)
+        key = fused.qk_norm_rope(L["k_proj"].from_codes(q, s, None).view(rows, T, Hkv, D), L["k_norm"], cos, sin,
+                                 c.rms_norm_eps).transpose(1, 2)
+        # the kernels read K and V through one set of strides: v_proj's output is already
+        # token-major like K, so V is a view of it
+        value = L["v_proj"].from_codes(q, s, None).view(rows, T, Hkv, D).transpose(1, 2)
         scale = D ** -0.5
         if entry is None:
             out = pb.state_attention(query, key, value, scale=scale)

@@ -203,3 +203,33 @@ def gated_rmsnorm_quant(x: torch.Tensor, z: torch.Tensor, weight: torch.Tensor, 
     """(q [M, K], scale [M, 1]): the gated norm's token rows quantised for out_proj."""
     _, q, scale = _gated_norm(x, z, weight, eps, head_dim, _mode_code(mode))
     return q, scale[:, None]
+
+
+def qk_norm_rope(x: torch.Tensor, weight: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                 eps: float) -> torch.Tensor:
+    """q_norm / k_norm (Qwen3_5RMSNorm per head) then the partial rotary embedding, one pass.
+
+    x [rows, T, heads, 128] bf16 (any row/token/head strides, last dim contiguous), weight
+    [128] (the norm's raw weight; the kernel applies 1 + w), cos/sin [rows, T, rd] bf16.
+    Returns [rows, T, heads, 128] bf16, token-major; ``.transpose(1, 2)`` gives the
+    [rows, heads, T, 128] view the attention kernels read (d3trt/model/core.py:228-252).
+    """
+    _check_bf16(x, "qk_norm_rope")
+    if x.dim() != 4 or x.stride(-1) != 1:
+        raise RuntimeError(f"qk_norm_rope: x must be [rows, T, heads, D] with a contiguous last dim, got "
+                           f"{tuple(x.shape)} strides {x.stride()}")
+    rows, T, heads, D = x.shape
+    if cos.shape != sin.shape or cos.dim() != 3 or tuple(cos.shape[:2]) != (rows, T):
+        raise RuntimeError(f"qk_norm_rope: cos/sin must be [rows, T, rd], got {tuple(cos.shape)}, {tuple(sin.shape)}")
+    cos = cos.to(torch.bfloat16)
+    sin = sin.to(torch.bfloat16)
+    if cos.stride(-1) != 1 or cos.stride() != sin.stride():
+        cos, sin = cos.contiguous(), sin.contiguous()
+    w = weight.to(device=x.device, dtype=torch.bfloat16).contiguous()
+    out = torch.empty(rows, T, heads, D, dtype=torch.bfloat16, device=x.device)
+    st = _lib.lib().d3b_qk_norm_rope(
+        _lib.ptr(x), _lib.i64_array(x.stride()[:3]), _lib.ptr(w), _lib.ptr(cos), _lib.ptr(sin),
+        _lib.i64_array(cos.stride()[:2]), _lib.ptr(out), rows, T, heads, D, int(cos.shape[-1]), float(eps),
+        _lib.stream_of(x))
+    _lib.check(st, "d3b_qk_norm_rope")
+    return out

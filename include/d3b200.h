@@ -228,6 +228,23 @@ D3B_API int d3b_gated_rmsnorm_quant(const void* x, int64_t ldx, const void* z, i
                                     int mode, d3b_stream_t stream);
 
 /*
+ * Per-head RMSNorm of queries or keys followed by the partial rotary embedding,
+ * one pass. Replaces q_norm / k_norm (transformers Qwen3_5RMSNorm) and
+ * apply_rotary_pos_emb in D3Core._attention (d3trt/model/core.py:228-252).
+ *   x [rows, T, heads, head_dim] bf16, element strides x_strides = {row, token,
+ *     head}, head_dim contiguous (the query half of q_proj's output is a slice)
+ *   y = bf16(float(x * rsqrt(mean(x^2) + eps)) * (1 + weight))   weight [head_dim] bf16
+ *   for i < rotary_dim: out_i = bf16(bf16(y_i * cos_i) + bf16(rot(y)_i * sin_i)),
+ *     rot(y) = (-y[rd/2 .. rd), y[0 .. rd/2)); out_i = y_i beyond rotary_dim
+ *   cos, sin [rows, T, rotary_dim] bf16, element strides cs_strides = {row, token}
+ *   out [rows, T, heads, head_dim] bf16 contiguous (token-major)
+ * head_dim == 128, rotary_dim in {16, 32, 64, 128}.
+ */
+D3B_API int d3b_qk_norm_rope(const void* x, const int64_t* x_strides, const void* weight, const void* cos,
+                             const void* sin, const int64_t* cs_strides, void* out, int rows, int T, int heads,
+                             int head_dim, int rotary_dim, float eps, d3b_stream_t stream);
+
+/*
  * 255-way (any n_opt <= 1024) fp32 readout softmax at the selected positions.
  * Replaces the probabilities body of d3trt/model/trtllm_stack.py:451-468
  * (= hf_stack.py:67-84): logits = f32(hidden) @ readout^T; logits[b, j] = -inf

@@ -95,3 +95,34 @@ def test_gated_rmsnorm_quant_against_torch(M, H, D):
         rq, rs = quant.quantize_rows(out, mode)
         assert torch.equal(q.view(torch.uint8), rq.view(torch.uint8)) and torch.equal(s, rs)
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("rows,T,heads,stride_heads", [(1, 300, 32, 2), (37, 48, 4, 1), (5, 7, 8, 2)])
+def test_qk_norm_rope_against_torch(rows, T, heads, stride_heads):
+    """q_norm / k_norm (Qwen3_5RMSNorm per head) then the partial rotary embedding (rd = 32 of
+    128) in one kernel, against the backbone's torch restatement of the model's functions.
+    The two sum each head's squares in different orders, so a normalised value can land one
+    bf16 step away; the rotary sum of two such terms then moves by up to about two steps at
+    the terms' magnitude (the head's), not the result's. So: every value within 2^-5 of its
+    head's largest value, and under 2 % of the values differing at all. The input is a
+    strided slice (the query half of q_proj's output) when stride_heads is 2."""
+    from d3_turbo_trt_b200.model import fused
+    from d3_turbo_trt_b200.model.backbone import BackboneConfig, apply_rotary, rms_norm, rotary_tables
+
+    D = 128
+    g = torch.Generator().manual_seed(rows * 7 + T)
+    full = (torch.randn(rows, T, heads, stride_heads * D, generator=g) * 2.0).to(torch.bfloat16).to(DEV)
+    x = full[..., :D]
+    w = (torch.randn(D, generator=g) * 0.2).to(torch.bfloat16).to(DEV)
+    positions = (torch.arange(T)[None] + 4096 * torch.arange(rows)[:, None]).to(DEV)
+    cos, sin = rotary_tables(BackboneConfig(), positions, torch.bfloat16)
+    assert cos.shape[-1] == 32
+    want, _ = apply_rotary(rms_norm(x, w, 1e-6).transpose(1, 2), x.transpose(1, 2)[:, :1], cos, sin)
+    got = fused.qk_norm_rope(x, w, cos, sin, 1e-6)
+    assert got.shape == (rows, T, heads, D) and got.is_contiguous()
+    got_h, want_f = got.transpose(1, 2).float(), want.float()
+    diff = (got_h - want_f).abs()
+    head_max = want_f.abs().amax(-1, keepdim=True)
+    assert bool((diff <= head_max * 2.0 ** -5).all()), float((diff / head_max).max())
+    assert float((diff > 0).float().mean()) < 0.02
+    assert _lib.device_error() == 0
