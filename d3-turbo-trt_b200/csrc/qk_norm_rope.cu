@@ -1,5 +1,5 @@
 // Per-head RMSNorm of the attention layers' queries and keys followed by their
-// partial rotary embedding, in one pass (d3trt/model/core.py:228-252: q_norm and
+// partial rotary embedding, in one pass (d3trt/model/core.py:233-237: q_norm and
 // k_norm are transformers' Qwen3_5RMSNorm, then apply_rotary_pos_emb over the
 // first rd = head_dim * partial_rotary_factor dimensions):
 //

@@ -212,7 +212,7 @@ def qk_norm_rope(x: torch.Tensor, weight: torch.Tensor, cos: torch.Tensor, sin: 
     x [rows, T, heads, 128] bf16 (any row/token/head strides, last dim contiguous), weight
     [128] (the norm's raw weight; the kernel applies 1 + w), cos/sin [rows, T, rd] bf16.
     Returns [rows, T, heads, 128] bf16, token-major; ``.transpose(1, 2)`` gives the
-    [rows, heads, T, 128] view the attention kernels read (d3trt/model/core.py:228-252).
+    [rows, heads, T, 128] view the attention kernels read (d3trt/model/core.py:233-237).
     """
     _check_bf16(x, "qk_norm_rope")
     if x.dim() != 4 or x.stride(-1) != 1:

@@ -230,7 +230,7 @@ D3B_API int d3b_gated_rmsnorm_quant(const void* x, int64_t ldx, const void* z, i
 /*
  * Per-head RMSNorm of queries or keys followed by the partial rotary embedding,
  * one pass. Replaces q_norm / k_norm (transformers Qwen3_5RMSNorm) and
- * apply_rotary_pos_emb in D3Core._attention (d3trt/model/core.py:228-252).
+ * apply_rotary_pos_emb in D3Core._attention (d3trt/model/core.py:233-237).
  *   x [rows, T, heads, head_dim] bf16, element strides x_strides = {row, token,
  *     head}, head_dim contiguous (the query half of q_proj's output is a slice)
  *   y = bf16(float(x * rsqrt(mean(x^2) + eps)) * (1 + weight))   weight [head_dim] bf16
