@@ -11,7 +11,8 @@
 // contiguous), so no transpose or concatenation is made: one thread owns 8
 // adjacent channels (one 16-byte load per token, a warp reads 512 contiguous
 // bytes) and slides over a run of tokens keeping the last W-1 inputs in
-// registers, so every input is read once (plus a W-1 token halo per run).
+// registers, so every input is read once (plus a W-1 token halo per run); the
+// loads run two tokens ahead of the arithmetic.
 // Sums in fp32 in kernel order j = 0..W-1, rounded to bf16, SiLU in fp32
 // (x / (1 + exp(-x))) rounded to bf16 -- the two roundings of the reference's
 // conv1d + silu on bf16 tensors.
@@ -61,8 +62,16 @@ __global__ void __launch_bounds__(kConvThreads) causal_conv_silu_kernel(
   }
   const uint16_t* xr = x + r * sx_r + c0;
   uint16_t* orow = out + ((int64_t)r * T) * C + c0;
+  // the next two tokens' inputs are loaded ahead, so their memory latency overlaps this
+  // token's arithmetic instead of stalling every step of the run
+  auto load_tok = [&](int t) {
+    return t < t1 ? *reinterpret_cast<const uint4*>(xr + (int64_t)t * sx_t) : make_uint4(0, 0, 0, 0);
+  };
+  uint4 ahead0 = load_tok(t0), ahead1 = load_tok(t0 + 1);
   for (int t = t0; t < t1; ++t) {
-    const uint4 a = *reinterpret_cast<const uint4*>(xr + (int64_t)t * sx_t);
+    const uint4 a = ahead0;
+    ahead0 = ahead1;
+    ahead1 = load_tok(t + 2);
     const uint32_t ww[4] = {a.x, a.y, a.z, a.w};
     float cur[8];
 #pragma unroll
