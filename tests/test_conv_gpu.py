@@ -126,3 +126,29 @@ def test_qk_norm_rope_against_torch(rows, T, heads, stride_heads):
     assert bool((diff <= head_max * 2.0 ** -5).all()), float((diff / head_max).max())
     assert float((diff > 0).float().mean()) < 0.02
     assert _lib.device_error() == 0
+
+
+def test_silu_mul_every_bf16_gate():
+    """Every finite bf16 value as the gate (up = 1): the kernel's SiLU equals
+    bf16(g / (1 + exp(-g))) in fp32 with torch's exp and IEEE division bit for bit, values
+    next to bf16 rounding boundaries, large |g|, zeros and subnormals included."""
+    from d3_turbo_trt_b200.model import fused
+
+    bits = torch.arange(-32768, 32768, dtype=torch.int32).to(torch.int16)
+    g = bits.view(torch.bfloat16)
+    g = g[torch.isfinite(g.float())]
+    n = g.numel()
+    I = 8 * ((n + 7) // 8)
+    gate = torch.zeros(I, dtype=torch.bfloat16)
+    gate[:n] = g
+    per = 4096  # rows of 4096 gates each (the kernel's rows hold up to 24576)
+    nrow = I // per + (1 if I % per else 0)
+    gates = torch.zeros(nrow * per, dtype=torch.bfloat16)
+    gates[:I] = gate
+    gates = gates.reshape(nrow, per)
+    gu = torch.cat([gates, torch.ones_like(gates)], 1).to(DEV)
+    act = fused.silu_mul(gu)
+    gf = gates.to(DEV).float()
+    want = (gf / (1.0 + torch.exp(-gf))).to(torch.bfloat16)
+    assert torch.equal(act.view(torch.int16), want.view(torch.int16)), int((act != want).sum())
+    assert _lib.device_error() == 0
