@@ -20,7 +20,7 @@
 
 namespace {
 
-constexpr int kThreads = 256;  // 16 heads per CTA
+constexpr int kThreads = 256;  // up to 16 heads per CTA
 
 __device__ __forceinline__ float lo_bf(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float hi_bf(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
@@ -34,15 +34,16 @@ template <int RD>  // rotary dimensions, a multiple of 16 up to 128
 __global__ void __launch_bounds__(kThreads) qk_norm_rope_kernel(
     const uint16_t* __restrict__ x, int64_t sx_r, int64_t sx_t, int64_t sx_h, const uint16_t* __restrict__ w,
     const uint16_t* __restrict__ cosv, const uint16_t* __restrict__ sinv, int64_t sc_r, int64_t sc_t,
-    uint16_t* __restrict__ out, int64_t n_heads_total, int T, int heads, float eps) {
+    uint16_t* __restrict__ out, int T, int heads, float eps) {
+  // grid: x = (row, token), y = group of blockDim.x / 16 heads; no per-thread division
   const int lane = threadIdx.x & 31, sub = lane & 15;  // sub: the lane's 8 values within its head
-  const int64_t item = (int64_t)blockIdx.x * (kThreads / 16) + (threadIdx.x >> 4);  // (row, token, head)
-  const bool live = item < n_heads_total;
-  const int64_t it = live ? item : 0;
-  const int h = (int)(it % heads);
-  const int64_t rt = it / heads;
+  const int64_t rt = blockIdx.x;
   const int t = (int)(rt % T);
   const int64_t r = rt / T;
+  const int hh = (int)blockIdx.y * (int)(blockDim.x >> 4) + (int)(threadIdx.x >> 4);
+  const bool live = hh < heads;
+  const int h = live ? hh : 0;
+  const int64_t it = rt * heads + h;  // output head index (token-major)
   const uint4 xv = live ? __ldg(reinterpret_cast<const uint4*>(x + r * sx_r + (int64_t)t * sx_t + (int64_t)h * sx_h) + sub)
                         : make_uint4(0, 0, 0, 0);
   const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w) + sub);
@@ -106,25 +107,30 @@ extern "C" int d3b_qk_norm_rope(const void* x, const int64_t* x_strides, const v
   for (int i = 0; i < 3; ++i)
     if (x_strides[i] % 8 || x_strides[i] < 0) return D3B_EALIGN;
   if (cs_strides[0] % 8 || cs_strides[1] % 8 || cs_strides[0] < 0 || cs_strides[1] < 0) return D3B_EALIGN;
-  const int64_t total = (int64_t)rows * T * heads;
-  const int64_t blocks = (total + kThreads / 16 - 1) / (kThreads / 16);
-  if (blocks > 0x7FFFFFFF) return D3B_EINVAL;
+  const int64_t tokens = (int64_t)rows * T;
+  if (tokens > 0x7FFFFFFF) return D3B_EINVAL;
+  // heads per CTA, 16 lanes each, rounded up to whole warps (the shuffles take every lane;
+  // a lane past the last head computes head 0 again and stores nothing)
+  int per_cta = heads < kThreads / 16 ? heads : kThreads / 16;
+  per_cta += per_cta & 1;
+  const int groups = (heads + per_cta - 1) / per_cta;
+  if (groups > 65535) return D3B_EINVAL;
   const auto* xs = static_cast<const uint16_t*>(x);
   const auto* ws = static_cast<const uint16_t*>(weight);
   const auto* cs = static_cast<const uint16_t*>(cos);
   const auto* sn = static_cast<const uint16_t*>(sin);
   auto* os = static_cast<uint16_t*>(out);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const dim3 grid((unsigned)blocks), block(kThreads);
+  const dim3 grid((unsigned)tokens, (unsigned)groups), block((unsigned)(16 * per_cta));
   switch (rotary_dim) {
     case 16: qk_norm_rope_kernel<16><<<grid, block, 0, s>>>(xs, x_strides[0], x_strides[1], x_strides[2], ws, cs, sn,
-                                                            cs_strides[0], cs_strides[1], os, total, T, heads, eps); break;
+                                                            cs_strides[0], cs_strides[1], os, T, heads, eps); break;
     case 32: qk_norm_rope_kernel<32><<<grid, block, 0, s>>>(xs, x_strides[0], x_strides[1], x_strides[2], ws, cs, sn,
-                                                            cs_strides[0], cs_strides[1], os, total, T, heads, eps); break;
+                                                            cs_strides[0], cs_strides[1], os, T, heads, eps); break;
     case 64: qk_norm_rope_kernel<64><<<grid, block, 0, s>>>(xs, x_strides[0], x_strides[1], x_strides[2], ws, cs, sn,
-                                                            cs_strides[0], cs_strides[1], os, total, T, heads, eps); break;
+                                                            cs_strides[0], cs_strides[1], os, T, heads, eps); break;
     default: qk_norm_rope_kernel<128><<<grid, block, 0, s>>>(xs, x_strides[0], x_strides[1], x_strides[2], ws, cs, sn,
-                                                             cs_strides[0], cs_strides[1], os, total, T, heads, eps); break;
+                                                             cs_strides[0], cs_strides[1], os, T, heads, eps); break;
   }
   return d3b_host::check_launch();
 }

@@ -10,8 +10,9 @@ BASELINE.json: cfg3a (4096-token state + 16 x 64-token blocks), cfg3b (16384 +
 cfg4 (readout 255 x 5120 x 255; snapshot: the 64-layer state snapshot at a
 4096-token state, packed by one copy launch; gdn: one GDN layer's question pass,
 255 blocks x 48 tokens x 48 value heads; gdn_state: one GDN layer's state pass,
-4096 tokens x 48 value heads with a final state). Inputs are seeded synthetic
-tensors.
+4096 tokens x 48 value heads with a final state; gated_norm_fp8, causal_conv,
+qk_norm_rope: the backbone's glue kernels at the question pass's 255 x 48 tokens).
+Inputs are seeded synthetic tensors.
 """
 
 from __future__ import annotations
@@ -167,7 +168,36 @@ def _gdn_state(dev: torch.device, T: int = 4096, H: int = 16, HV: int = 48, K: i
     return fn, {"flops": 2.0 * macs * ((T + 63) // 64) * HV}
 
 
+def _glue(kernel: str, dev: torch.device, rows: int = 255, T: int = 48):
+    """config 4's question pass (255 blocks x 48 tokens): the GDN output's gated norm + quant
+    (48 heads x 128), the GDN causal conv + SiLU (conv_dim 10240, a 3-token tail), or the
+    attention queries' norm + partial rotary (32 heads x 128, the q half of q_proj's output)."""
+    from .model import fused
+    from .model.backbone import BackboneConfig, rotary_tables
+    from .model.conv import causal_conv1d_silu
+
+    g = torch.Generator(device=dev).manual_seed(6)
+    M = rows * T
+    if kernel == "gated_norm_fp8":
+        x = (torch.randn(M, 6144, generator=g, device=dev) * 0.3).to(torch.bfloat16)
+        z = torch.randn(M, 6144, generator=g, device=dev).to(torch.bfloat16)
+        w = (1 + torch.randn(128, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+        return (lambda: fused.gated_rmsnorm_quant(x, z, w, 1e-6, 128, "fp8")), {"bytes": M * 6144 * 5 + M * 4}
+    if kernel == "causal_conv":
+        x = torch.randn(rows, T, 10240, generator=g, device=dev).to(torch.bfloat16)
+        w = (torch.randn(10240, 1, 4, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+        tail = torch.randn(rows, 10240, 3, generator=g, device=dev).to(torch.bfloat16)
+        return (lambda: causal_conv1d_silu(x, w, tail)), {"bytes": 2 * x.numel() * 2}
+    qg = torch.randn(rows, T, 32, 256, generator=g, device=dev).to(torch.bfloat16)
+    w = (torch.randn(128, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+    positions = (torch.arange(T, device=dev)[None] + 4096).expand(rows, T)
+    cos, sin = rotary_tables(BackboneConfig(), positions, torch.bfloat16)
+    return (lambda: fused.qk_norm_rope(qg[..., :128], w, cos, sin, 1e-6)), {"bytes": M * 32 * 128 * 4}
+
+
 def build(kernel: str, config: str, dev: torch.device):
+    if kernel in ("gated_norm_fp8", "causal_conv", "qk_norm_rope"):
+        return _glue(kernel, dev)
     if kernel == "attention":
         return _state(dev) if config == "state4k" else _attention(config, dev)
     if kernel == "gemm_fp8":
@@ -195,7 +225,8 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", required=True,
                     choices=["attention", "gemm_fp8", "gemm_int8", "act_quant_fp8", "act_quant_int8", "readout",
-                             "snapshot", "gdn", "gdn_recurrent", "gdn_state"])
+                             "snapshot", "gdn", "gdn_recurrent", "gdn_state", "gated_norm_fp8", "causal_conv",
+                             "qk_norm_rope"])
     ap.add_argument("--config", default="cfg3a", choices=[*ATTN, "state4k", "cfg2", "cfg4"])
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=1)

@@ -97,7 +97,8 @@ def test_gated_rmsnorm_quant_against_torch(M, H, D):
     assert _lib.device_error() == 0
 
 
-@pytest.mark.parametrize("rows,T,heads,stride_heads", [(1, 300, 32, 2), (37, 48, 4, 1), (5, 7, 8, 2)])
+@pytest.mark.parametrize("rows,T,heads,stride_heads", [(1, 300, 32, 2), (37, 48, 4, 1), (5, 7, 8, 2), (3, 9, 3, 1),
+                                                      (2, 5, 19, 2)])
 def test_qk_norm_rope_against_torch(rows, T, heads, stride_heads):
     """q_norm / k_norm (Qwen3_5RMSNorm per head) then the partial rotary embedding (rd = 32 of
     128) in one kernel, against the backbone's torch restatement of the model's functions.
