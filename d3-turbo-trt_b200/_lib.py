@@ -70,6 +70,7 @@ SIGNATURES: list[tuple[str, Any, list[Any]]] = [
     ("d3b_silu_mul_quant", _I, [_VP, _I64, _VP, _VP, _VP, _I64, _I64, _I, _VP]),
     ("d3b_gated_rmsnorm_quant", _I, [_VP, _I64, _VP, _I64, _VP, _F, _I, _VP, _VP, _VP, _I64, _I64, _I, _VP]),
     ("d3b_qk_norm_rope", _I, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _F, _VP]),
+    ("d3b_gdn_gates", _I, [_VP, _I64, _VP, _I64, _VP, _VP, _VP, _VP, _I64, _I, _VP]),
     ("d3b_readout_workspace_size", _SZ, [_I, _I]),
     ("d3b_readout", _I, [_VP, _I, _VP, _VP, _F, _VP, _I, _I, _I, _VP, _SZ, _VP]),
     ("d3b_readout_noalloc", _I, [_VP, _I, _VP, _VP, _F, _VP, _I, _I, _I, _VP]),

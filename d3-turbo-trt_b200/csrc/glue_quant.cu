@@ -327,6 +327,33 @@ int norm_nv(int mode, const uint16_t* x, int64_t ldx, const uint16_t* z, int64_t
 
 }  // namespace
 
+// ---------------------------------------------------------------------------
+// Gated DeltaNet gates (d3trt/model/core.py:341-342 through the model's module):
+//   beta = bf16(1 / (1 + exp(-b)))                      (torch's sigmoid on bf16)
+//   g    = neg_exp_a[h] * softplus(float(a) + dt_bias[h]),
+//          softplus(x) = x > 20 ? x : log1p(exp(x))      (torch's softplus, fp32)
+// with neg_exp_a = -exp(float(A_log)) and dt_bias as fp32 per value head, formed once by the
+// caller. One thread per (token row, value head); a and b are row slices of the fused input
+// projection (row strides lda, ldb).
+constexpr int kGateThreads = 256;
+
+__global__ void __launch_bounds__(kGateThreads) gdn_gates_kernel(const uint16_t* __restrict__ a, int64_t lda,
+                                                                 const uint16_t* __restrict__ b, int64_t ldb,
+                                                                 const float* __restrict__ neg_exp_a,
+                                                                 const float* __restrict__ dt_bias, float* __restrict__ g,
+                                                                 uint16_t* __restrict__ beta, int64_t n, int HV) {
+  const int64_t i = (int64_t)blockIdx.x * kGateThreads + threadIdx.x;
+  if (i >= n) return;
+  const int64_t m = i / HV;
+  const int h = (int)(i - m * HV);
+  const float x = __fadd_rn(__uint_as_float((uint32_t)a[m * lda + h] << 16), dt_bias[h]);
+  const float sp = x > 20.0f ? x : log1pf(expf(x));
+  g[i] = __fmul_rn(neg_exp_a[h], sp);
+  const float bv = __uint_as_float((uint32_t)b[m * ldb + h] << 16);
+  const __nv_bfloat16 r = __float2bfloat16_rn(1.0f / (1.0f + expf(-bv)));
+  beta[i] = *reinterpret_cast<const uint16_t*>(&r);
+}
+
 extern "C" int d3b_silu_mul_quant(const void* gate_up, int64_t ld, void* act_out, void* q, float* scale, int64_t M,
                                   int64_t I, int mode, d3b_stream_t stream) {
   if (M < 0 || I <= 0 || ld < 2 * I) return D3B_EINVAL;
@@ -374,4 +401,18 @@ extern "C" int d3b_gated_rmsnorm_quant(const void* x, int64_t ldx, const void* z
     case 128: return norm_nv<16>(mode, xs, ldx, zs, ldz, ws, eps, M, K, os, qq, scale, s);
     default: return norm_nv<32>(mode, xs, ldx, zs, ldz, ws, eps, M, K, os, qq, scale, s);
   }
+}
+
+extern "C" int d3b_gdn_gates(const void* a, int64_t lda, const void* b, int64_t ldb, const float* neg_exp_a,
+                             const float* dt_bias, float* g, void* beta, int64_t M, int HV, d3b_stream_t stream) {
+  if (M < 0 || HV <= 0 || lda < HV || ldb < HV) return D3B_EINVAL;
+  if (M == 0) return D3B_OK;
+  if (!a || !b || !neg_exp_a || !dt_bias || !g || !beta) return D3B_EINVAL;
+  const int64_t n = M * HV;
+  const int64_t blocks = (n + kGateThreads - 1) / kGateThreads;
+  if (blocks > 0x7FFFFFFF) return D3B_EINVAL;
+  gdn_gates_kernel<<<(unsigned)blocks, kGateThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(a), lda, static_cast<const uint16_t*>(b), ldb, neg_exp_a, dt_bias, g,
+      static_cast<uint16_t*>(beta), n, HV);
+  return d3b_host::check_launch();
 }

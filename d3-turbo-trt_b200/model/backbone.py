@@ -196,14 +196,21 @@ class D3Backbone:
                 L["q_norm"], L["k_norm"] = w(a + "q_norm.weight"), w(a + "k_norm.weight")
             elif kind == "linear_attention":
                 a = p + "linear_attn."
-                for n in ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a", "out_proj"):
-                    L[n] = _Linear(w(a + n + ".weight"), mode, dev)
+                # the four input projections read the same codes: one GEMM over their rows
+                # stacked (per-output-channel scales, so every output equals the separate
+                # projection's), sliced afterwards into qkv, z, b and a
+                parts = [w(a + n + ".weight") for n in ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a")]
+                L["in_proj"] = _Linear(torch.cat(parts, 0), mode, dev)
+                L["in_split"] = tuple(int(t.shape[0]) for t in parts)
+                del parts
+                L["out_proj"] = _Linear(w(a + "out_proj.weight"), mode, dev)
                 L["conv"] = w(a + "conv1d.weight").squeeze(1)
                 L["A_log"], L["dt_bias"], L["norm"] = w(a + "A_log"), w(a + "dt_bias"), w(a + "norm.weight")
+                L["neg_exp_a"] = -L["A_log"].float().exp()  # the gates' per-head constants, formed once
+                L["dt_bias_f"] = L["dt_bias"].float()
             else:
                 raise ValueError(f"unknown layer type {kind!r}")
-            fed = ("q_proj", "k_proj", "v_proj", "o_proj", "in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a",
-                   "out_proj", "gate_up", "down")
+            fed = ("q_proj", "k_proj", "v_proj", "o_proj", "in_proj", "out_proj", "gate_up", "down")
             for n in fed:
                 if n in L and not L[n].quant:
                     raise ValueError(f"layer {i} {n}: every projection reads fused-producer codes and must be "
@@ -296,13 +303,15 @@ class D3Backbone:
         c = self.config
         window = c.linear_conv_kernel_dim - 1
         HV, HK, Dk, Dv = c.linear_num_value_heads, c.linear_num_key_heads, c.linear_key_head_dim, c.linear_value_head_dim
-        mixed = L["in_proj_qkv"].from_codes(q, s, None).view(rows, T, -1)  # token-major [rows, T, conv_dim]
-        z = L["in_proj_z"].from_codes(q, s, None).view(rows, T, HV, Dv)
-        b = L["in_proj_b"].from_codes(q, s, None).view(rows, T, HV)
-        a = L["in_proj_a"].from_codes(q, s, None).view(rows, T, HV)
+        proj = L["in_proj"].from_codes(q, s, None)  # [rows * T, qkv | z | b | a]
+        nq, nz, nb, _ = L["in_split"]
+        mixed = proj[:, :nq].view(rows, T, nq)  # token-major [rows, T, conv_dim], rows of the fused width
+        z = proj[:, nq:nq + nz].view(rows, T, HV, Dv)
+        b, a = proj[:, nq + nz:nq + nz + nb], proj[:, nq + nz + nb:]
         if entry is None:
             conv = causal_conv1d_silu(mixed, L["conv"])
-            tail = mixed[:, -window:, :].transpose(1, 2)  # [1, conv_dim, window], as core.py:321
+            # [1, conv_dim, window], as core.py:321; copied so the snapshot does not hold the projection
+            tail = mixed[:, -window:, :].transpose(1, 2).contiguous()
             if tail.shape[-1] < window:
                 tail = F.pad(tail, (window - tail.shape[-1], 0))
             initial = None
@@ -314,8 +323,8 @@ class D3Backbone:
         query = conv[..., :kd].view(rows, T, HK, Dk)  # strided views: the scan reads them in place
         key = conv[..., kd:2 * kd].view(rows, T, HK, Dk)
         value = conv[..., 2 * kd:].view(rows, T, HV, Dv)
-        beta = b.sigmoid()
-        g = -L["A_log"].float().exp() * F.softplus(a.float() + L["dt_bias"])
+        g, beta = fused.gdn_gates(a, b, L["neg_exp_a"], L["dt_bias_f"])  # core.py:341-342 in one kernel
+        g, beta = g.view(rows, T, HV), beta.view(rows, T, HV)
         if entry is None:
             core, final = self._state_scan(query, key, value, g, beta)
             entry = DeltaEntry(tail=tail, recurrent=final)

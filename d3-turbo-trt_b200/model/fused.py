@@ -233,3 +233,26 @@ def qk_norm_rope(x: torch.Tensor, weight: torch.Tensor, cos: torch.Tensor, sin: 
         _lib.stream_of(x))
     _lib.check(st, "d3b_qk_norm_rope")
     return out
+
+
+def gdn_gates(a: torch.Tensor, b: torch.Tensor, neg_exp_a: torch.Tensor, dt_bias: torch.Tensor):
+    """(g [M, HV] fp32, beta [M, HV] bf16) of the Gated DeltaNet layer, one kernel:
+    beta = b.sigmoid(), g = neg_exp_a * softplus(a.float() + dt_bias) with neg_exp_a =
+    -exp(A_log.float()) and dt_bias fp32 per value head (d3trt/model/core.py:341-342).
+    a, b: [M, HV] bf16 (row slices of the input projection are read in place)."""
+    _check_bf16(a, "gdn_gates")
+    _check_bf16(b, "gdn_gates")
+    if a.dim() != 2 or a.shape != b.shape or a.stride(1) != 1 or b.stride(1) != 1:
+        raise RuntimeError(f"gdn_gates: a and b must be [M, HV] rows with a contiguous last dim, got "
+                           f"{tuple(a.shape)} {a.stride()} and {tuple(b.shape)} {b.stride()}")
+    M, HV = a.shape
+    ne = neg_exp_a.to(device=a.device, dtype=torch.float32).contiguous()
+    dtb = dt_bias.to(device=a.device, dtype=torch.float32).contiguous()
+    if ne.numel() != HV or dtb.numel() != HV:
+        raise RuntimeError(f"gdn_gates: {HV} value heads, got {ne.numel()} and {dtb.numel()} per-head values")
+    g = torch.empty(M, HV, dtype=torch.float32, device=a.device)
+    beta = torch.empty(M, HV, dtype=torch.bfloat16, device=a.device)
+    st = _lib.lib().d3b_gdn_gates(_lib.ptr(a), max(a.stride(0), HV), _lib.ptr(b), max(b.stride(0), HV), _lib.ptr(ne),
+                                  _lib.ptr(dtb), _lib.ptr(g), _lib.ptr(beta), M, HV, _lib.stream_of(a))
+    _lib.check(st, "d3b_gdn_gates")
+    return g, beta

@@ -228,6 +228,18 @@ D3B_API int d3b_gated_rmsnorm_quant(const void* x, int64_t ldx, const void* z, i
                                     int mode, d3b_stream_t stream);
 
 /*
+ * Gated DeltaNet gates of every (token row, value head). Replaces the module's
+ * beta = b.sigmoid() and g = -A_log.float().exp() * softplus(a.float() + dt_bias)
+ * (d3trt/model/core.py:341-342).
+ *   a, b [M, HV] bf16 rows of lda / ldb elements (slices of the input projection)
+ *   neg_exp_a [HV] f32 = -exp(float(A_log)); dt_bias [HV] f32
+ *   g [M, HV] f32 = neg_exp_a * softplus(float(a) + dt_bias) (softplus: x > 20 ? x : log1p(exp(x)))
+ *   beta [M, HV] bf16 = bf16(1 / (1 + exp(-b)))
+ */
+D3B_API int d3b_gdn_gates(const void* a, int64_t lda, const void* b, int64_t ldb, const float* neg_exp_a,
+                          const float* dt_bias, float* g, void* beta, int64_t M, int HV, d3b_stream_t stream);
+
+/*
  * Per-head RMSNorm of queries or keys followed by the partial rotary embedding,
  * one pass. Replaces q_norm / k_norm (transformers Qwen3_5RMSNorm) and
  * apply_rotary_pos_emb in D3Core._attention (d3trt/model/core.py:233-237).

@@ -153,3 +153,27 @@ def test_silu_mul_every_bf16_gate():
     want = (gf / (1.0 + torch.exp(-gf))).to(torch.bfloat16)
     assert torch.equal(act.view(torch.int16), want.view(torch.int16)), int((act != want).sum())
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("M,HV,stride", [(12240, 48, 16480), (37, 16, 16), (5, 48, 64)])
+def test_gdn_gates_against_torch(M, HV, stride):
+    """beta = b.sigmoid() and g = -A_log.float().exp() * softplus(a.float() + dt_bias) of the GDN
+    layer (d3trt/model/core.py:341-342) in one kernel, a and b read as row slices of a wider
+    projection: both bit-identical to torch's element-wise ops, softplus's linear branch
+    (x > 20) and large negative gates included."""
+    from d3_turbo_trt_b200.model import fused
+
+    g = torch.Generator().manual_seed(M + HV)
+    proj = (torch.randn(M, stride + 2 * HV, generator=g) * 6).to(torch.bfloat16)
+    proj[0, :HV] = 25.0  # softplus's x > 20 branch
+    proj[1, :HV] = -90.0
+    proj = proj.to(DEV)
+    a, b = proj[:, :HV], proj[:, stride - HV:stride] if stride >= 2 * HV else proj[:, HV:2 * HV]
+    A_log = torch.log(torch.rand(HV, generator=g) * 1.95 + 0.05).to(torch.bfloat16).to(DEV)
+    dt_bias = (1 + torch.randn(HV, generator=g) * 0.3).to(torch.bfloat16).to(DEV)
+    want_beta = b.sigmoid()
+    want_g = -A_log.float().exp() * torch.nn.functional.softplus(a.float() + dt_bias)
+    got_g, got_beta = fused.gdn_gates(a, b, -A_log.float().exp(), dt_bias.float())
+    assert torch.equal(got_beta.view(torch.int16), want_beta.contiguous().view(torch.int16))
+    assert torch.equal(got_g, want_g)
+    assert _lib.device_error() == 0
