@@ -793,6 +793,10 @@ def secondary(dev, stream, flush, peaks, quant, pb, d3b):
         else:
             ti = statistics.median(time_steps(lambda: torch._int_mm(qa, layer.weight.t()), 10, 3, stream, flush))
             res["w8a8_int8_cfg2"]["torch_int_mm_ms"] = ti
+            # the same output as torch._int_mm (raw int32 accumulators, no scales): like for like
+            t32 = statistics.median(time_steps(lambda: quant.scaled_mm(qa, layer.weight, None, None,
+                                                                        out_dtype=torch.int32), 10, 3, stream, flush))
+            res["w8a8_int8_cfg2"]["gemm_i32_out_ms"] = t32
         del layer, qa, sa
     res["fp8_int8_peak_tflops"] = fp8_peak
     del x, w
