@@ -762,6 +762,17 @@ def secondary(dev, stream, flush, peaks, quant, pb, d3b):
     res["cfg3b_question_pass"] = {"ms": t, "blocks_per_s": 255 / (t / 1e3), "tflops": fl / t / 1e9,
                                   "frac_bf16_peak": fl / t / 1e9 / bf16_peak}
     del inp
+    # config 3a's blocks and state at the model's own attention shape (24 query heads, 4 KV
+    # heads, head_dim 256: the D = 256 kernel, whose O accumulator alone fills 256 TMEM columns)
+    c256 = dict(CFG3A, H=24, D=256)
+    inp = make_question_inputs(c256, 5, dev)
+    t = statistics.median(time_steps(lambda: pb.prefix_bidir_attention(
+        inp["q"], inp["ks"], inp["vs"], inp["kq"], inp["vq"], [c256["L"]] * c256["B"], scale=256 ** -0.5),
+        10, 3, stream, flush))
+    fl = attn_flops(**c256)
+    res["cfg3a_question_pass_h24_d256"] = {"ms": t, "blocks_per_s": c256["B"] / (t / 1e3), "tflops": fl / t / 1e9,
+                                       "frac_bf16_peak": fl / t / 1e9 / bf16_peak}
+    del inp
     # config 2: W8A8 [4096, 5120] x [13824, 5120]^T
     M, K, N = 4096, 5120, 13824
     x = torch.randn(M, K, generator=g)
