@@ -111,7 +111,10 @@ struct Params {
   const int32_t* lengths;
   void* out;
   int64_t out_sb, out_sh, out_sl;  // element strides
-  int H, Hkv, G, T, S, L;
+  // A Q tile holds G query heads (of one KV head's group) x T tokens. When the
+  // group is split (hsplit > 1) into hsplit head groups of G heads each, Hkv
+  // counts the head groups and K/V head = group / hsplit.
+  int H, Hkv, G, T, S, L, hsplit;
   float scale_log2;
   int* err;
   // Launch plan of the D <= 128 kernel (1-D grid). Unit u = (b * Hkv + g) *
@@ -252,6 +255,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __shared__ Bars bars;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int kvh = g / p.hsplit;  // g: head group
   const int G = p.G, T = p.T;
   const int len_b = block_length(p, b);
   const int rows_used = G * T;
@@ -338,12 +342,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const CUtensorMap* m = is_v ? &mapVs : &mapKs;
 #pragma unroll
           for (int c = 0; c < C::NCH; ++c)
-            d3b::tma_load_3d(dst + c * C::SLOT_CHUNK, m, &bars.slot_full[stage], c * C::CH, j * BN, g);
+            d3b::tma_load_3d(dst + c * C::SLOT_CHUNK, m, &bars.slot_full[stage], c * C::CH, j * BN, kvh);
         } else {
           const CUtensorMap* m = is_v ? &mapVq : &mapKq;
 #pragma unroll
           for (int c = 0; c < C::NCH; ++c)
-            d3b::tma_load_4d(dst + c * C::SLOT_CHUNK, m, &bars.slot_full[stage], c * C::CH, (j - n_s) * BN, g, b);
+            d3b::tma_load_4d(dst + c * C::SLOT_CHUNK, m, &bars.slot_full[stage], c * C::CH, (j - n_s) * BN, kvh, b);
         }
         if (++stage == C::NSLOT) { stage = 0; phase ^= 1; }
       }
@@ -727,7 +731,7 @@ __device__ void merge_unit(const Params& p, int r, int b, int g, int tok0, int l
 // real token (its rows are zero-filled) or, in a split launch, when the piece
 // has no real key tile.
 struct Work {
-  int unit, b, g, tok0, len_b, a, n;
+  int unit, b, g, kvh, tok0, len_b, a, n;  // g: head group, kvh: its K/V head
 };
 
 // Item i of this CTA. Without SPLIT the launch is persistent: CTA c takes units
@@ -749,6 +753,7 @@ __device__ __forceinline__ bool work_item(const Params& p, int i, int n_s, Work&
   }
   const int tile = w.unit % p.tiles;
   w.g = (w.unit / p.tiles) % p.Hkv;
+  w.kvh = w.g / p.hsplit;
   w.b = w.unit / (p.tiles * p.Hkv);
   w.len_b = block_length(p, w.b);
   w.tok0 = tile * p.T;
@@ -912,11 +917,11 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
           if (kt < n_s) {
 #pragma unroll
             for (int c = 0; c < C::NCH; ++c)
-              d3b::tma_load_3d(dst + c * C::SLOT_CHUNK, m_state, full, c * C::CH, kt * BN, w.g);
+              d3b::tma_load_3d(dst + c * C::SLOT_CHUNK, m_state, full, c * C::CH, kt * BN, w.kvh);
           } else {
 #pragma unroll
             for (int c = 0; c < C::NCH; ++c)
-              d3b::tma_load_4d(dst + c * C::SLOT_CHUNK, m_own, full, c * C::CH, (kt - n_s) * BN, w.g, w.b);
+              d3b::tma_load_4d(dst + c * C::SLOT_CHUNK, m_own, full, c * C::CH, (kt - n_s) * BN, w.kvh, w.b);
           }
           if (++slot == nslot) { slot = 0; ph ^= 1; }
         }
@@ -1288,6 +1293,7 @@ __device__ __forceinline__ bool pair_item(const Params& p, int i, int n_s, uint3
   if (pu >= p.whole_units) return false;  // whole_units counts pair units in this launch
   const int tp = pu % half_tiles;
   w.g = (pu / half_tiles) % p.Hkv;
+  w.kvh = w.g / p.hsplit;
   w.b = pu / (half_tiles * p.Hkv);
   w.unit = pu;
   w.len_b = block_length(p, w.b);
@@ -1404,18 +1410,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(DU_THREADS, 1)
           const int kt = w.a + j;  // key tile of the unit
           if (is_v) {  // all 128 keys, this CTA's 64 columns
             if (kt < n_s)
-              d3b::tma_load_3d_pair(dst, &mapVs, leader_full, (int)rank * C::CH, kt * BN, w.g);
+              d3b::tma_load_3d_pair(dst, &mapVs, leader_full, (int)rank * C::CH, kt * BN, w.kvh);
             else
-              d3b::tma_load_4d_pair(dst, &mapVq, leader_full, (int)rank * C::CH, (kt - n_s) * BN, w.g, w.b);
+              d3b::tma_load_4d_pair(dst, &mapVq, leader_full, (int)rank * C::CH, (kt - n_s) * BN, w.kvh, w.b);
           } else {  // this CTA's 64 keys, both column halves
 #pragma unroll
             for (int c = 0; c < C::NCH; ++c) {
               if (kt < n_s)
                 d3b::tma_load_3d_pair(dst + c * C::K_CHUNK, &mapKs, leader_full, c * C::CH,
-                                      kt * BN + (int)rank * C::K_ROWS, w.g);
+                                      kt * BN + (int)rank * C::K_ROWS, w.kvh);
               else
                 d3b::tma_load_4d_pair(dst + c * C::K_CHUNK, &mapKq, leader_full, c * C::CH,
-                                      (kt - n_s) * BN + (int)rank * C::K_ROWS, w.g, w.b);
+                                      (kt - n_s) * BN + (int)rank * C::K_ROWS, w.kvh, w.b);
             }
           }
           if (++slot == nslot) { slot = 0; ph ^= 1; }
@@ -1816,6 +1822,28 @@ bool pair_kernel_enabled() {
 constexpr int kMaxCounts = 256;
 constexpr size_t kCountBytes = kMaxCounts * sizeof(int);
 
+// Q tile shape for G query heads per KV head and L tokens per block: Gs of
+// the G heads by T = BM / Gs tokens, Gs a divisor of G, the one with the fewest
+// tiles per (block, KV head) (G / Gs head groups x ceil(L / T) token tiles),
+// ties to the largest Gs. Token-aligned tiles of the whole group leave rows
+// empty when G does not divide BM: G = 6, L = 64 takes 4 tiles of 21 tokens
+// (384 of 512 rows used), 3 head groups of 2 heads x 64 tokens fill 3 tiles.
+// Every K/V tile is read once per tile, so fewer tiles also means fewer reads.
+struct TileShape {
+  int Gs, T, hsplit;
+  int64_t tiles;  // token tiles per head group
+};
+TileShape tile_shape(int G, int L) {
+  TileShape best{G, BM / G, 1, (L + BM / G - 1) / (BM / G)};
+  for (int gs = G - 1; gs >= 1; --gs) {
+    if (G % gs) continue;
+    const int t = BM / gs;
+    const int64_t tiles = (L + t - 1) / t;
+    if ((int64_t)(G / gs) * tiles < (int64_t)best.hsplit * best.tiles) best = {gs, t, G / gs, tiles};
+  }
+  return best;
+}
+
 size_t plan_bytes(const TailPlan& t, int D, size_t* count_bytes) {
   if (count_bytes) *count_bytes = kCountBytes;
   if (!t.split_units) return 0;
@@ -1855,15 +1883,17 @@ static int prefix_bidir_impl(const void* q, const int64_t* q_strides, const void
   const CUtensorMapSwizzle sw = D >= 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   const CUtensorMapDataType dt = dtype == D3B_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const int BN = D == 256 ? 64 : 128;
-  const int T = BM / G;
+  const TileShape shape = tile_shape(G, L);
+  const int T = shape.T;
+  if ((int64_t)Hkv * shape.hsplit > 65535) return D3B_EINVAL;
 
   // 0 Q, 1/2 state K/V, 3/4 own K/V; the pair kernel's key halves: 5 state K, 6 own K (64-key boxes)
   CUtensorMap maps[7];
   int rc;
-  {  // Q: [B, H, L, D] -> dims {D, H, L, B}, box {CH, G, T, 1}
+  {  // Q: [B, H, L, D] -> dims {D, H, L, B}, box {CH, Gs, T, 1}
     const uint64_t dims[4] = {(uint64_t)D, (uint64_t)H, (uint64_t)L, (uint64_t)B};
     const uint64_t st[3] = {(uint64_t)q_strides[1] * 2, (uint64_t)q_strides[2] * 2, (uint64_t)q_strides[0] * 2};
-    const uint32_t box[4] = {(uint32_t)CH, (uint32_t)G, (uint32_t)T, 1};
+    const uint32_t box[4] = {(uint32_t)CH, (uint32_t)shape.Gs, (uint32_t)T, 1};
     if ((rc = d3b_host::encode_tiled(&maps[0], dt, 4, q, dims, st, box, sw))) return rc;
   }
   {  // own-block K/V: [B, Hkv, L, D] -> dims {D, L, Hkv, B}, box {CH, BN, 1, 1}
@@ -1900,17 +1930,18 @@ static int prefix_bidir_impl(const void* q, const int64_t* q_strides, const void
   prm.out_sh = out_strides[1];
   prm.out_sl = out_strides[2];
   prm.H = H;
-  prm.Hkv = Hkv;
-  prm.G = G;
+  prm.Hkv = Hkv * shape.hsplit;  // head groups
+  prm.G = shape.Gs;
   prm.T = T;
+  prm.hsplit = shape.hsplit;
   prm.S = S;
   prm.L = L;
   prm.scale_log2 = (float)((double)scale * 1.4426950408889634);
   prm.err = d3b_host::device_error_word();
   if (!prm.err) return D3B_ECUDA;
 
-  const int64_t tiles = (L + T - 1) / T;
-  const int64_t units = tiles * Hkv * B;
+  const int64_t tiles = shape.tiles;
+  const int64_t units = tiles * prm.Hkv * B;
   const int64_t n_full = (int64_t)(S + BN - 1) / BN + (L + BN - 1) / BN;
   if (units > 0x7FFFFFFF || n_full > 0x7FFFFFFF) return D3B_EINVAL;
   prm.tiles = (int)tiles;
@@ -1947,7 +1978,7 @@ static int prefix_bidir_impl(const void* q, const int64_t* q_strides, const void
     return dtype == D3B_F16 ? launch_pair<1>(maps, prm, prm.whole_units, s)
                             : launch_pair<0>(maps, prm, prm.whole_units, s);
   }
-  const dim3 grid((unsigned)tiles, Hkv, B);
+  const dim3 grid((unsigned)tiles, (unsigned)prm.Hkv, B);
   // D <= 128: one CTA per unit or piece in a split launch, else a persistent
   // grid of at most one CTA per SM looping over the units
   const dim3 grid_dual = prm.split_units ? dim3((unsigned)ctas)
@@ -1959,8 +1990,8 @@ static int prefix_bidir_impl(const void* q, const int64_t* q_strides, const void
 extern "C" size_t d3b_prefix_bidir_workspace_size(int B, int H, int Hkv, int S, int L, int D) {
   if (B <= 0 || H <= 0 || Hkv <= 0 || S < 0 || L <= 0 || H % Hkv || H / Hkv > BM) return 0;
   if (D != 32 && D != 64 && D != 128) return 0;  // D = 256 runs without one
-  const int T = BM / (H / Hkv);
-  const int64_t units = (int64_t)((L + T - 1) / T) * Hkv * B;
+  const TileShape shape = tile_shape(H / Hkv, L);
+  const int64_t units = shape.tiles * shape.hsplit * Hkv * B;
   const int64_t n_full = (int64_t)(S + 127) / 128 + (L + 127) / 128;
   if (units > 0x7FFFFFFF || n_full > 0x7FFFFFFF) return 0;
   const TailPlan t = cached_plan((int)units, (int)n_full, d3b_host::num_sms(d3b_host::current_device()));

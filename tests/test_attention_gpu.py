@@ -191,6 +191,32 @@ def test_head_dim_256_at_4k_state():
     assert _lib.device_error() == 0
 
 
+@pytest.mark.parametrize("B,H,Hkv,S,L,D,seed", [(16, 24, 4, 1000, 64, 256, 41), (37, 24, 2, 500, 64, 128, 42),
+                                                 (9, 24, 4, 300, 64, 64, 43), (5, 20, 2, 700, 50, 128, 44),
+                                                 (4, 20, 2, 300, 50, 256, 45)])
+def test_head_group_tiles_against_oracle(B, H, Hkv, S, L, D, seed):
+    """GQA groups that do not divide the 128-row tile are split into head
+    groups (G = 6 at 64 tokens: 3 tiles of 2 heads x 64 tokens; G = 12: 3
+    groups of 4 heads x 32 tokens; G = 10 at 50 tokens: 4 tiles of 5 heads x 25
+    tokens, 125 of 128 rows), each head group reading its KV head's keys: the
+    D = 256 kernel, the D <= 128 kernel, ragged and empty blocks, against the
+    oracle, and rows past each block's length zero."""
+    g = torch.Generator().manual_seed(seed)
+    q = _rand((B, L, H, D), g).permute(0, 2, 1, 3)
+    ks, vs = _rand((S, Hkv, D), g).permute(1, 0, 2), _rand((S, Hkv, D), g).permute(1, 0, 2)
+    kq, vq = _rand((B, L, Hkv, D), g).permute(0, 2, 1, 3), _rand((B, L, Hkv, D), g).permute(0, 2, 1, 3)
+    lens = torch.randint(0, L + 1, (B,), generator=g).tolist()
+    lens[0], lens[1], lens[-1] = L, 1, 0
+    out = pb.prefix_bidir_attention(q.to(DEV), ks.to(DEV), vs.to(DEV), kq.to(DEV), vq.to(DEV), lens, scale=D**-0.5)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    ref = oattn.questions(q, ks, vs, kq, vq, lens, D**-0.5, dtype=torch.float32)
+    got = out.float().cpu()
+    assert float((got - ref).abs().max()) <= TOL
+    for b, n in enumerate(lens):
+        assert torch.all(got[b, :, n:] == 0)
+
+
 def test_device_lengths_out_of_range_are_reported():
     """A device lengths table is read by the kernel itself: values outside
     [0, L] are clamped (no access leaves the tensors) and reported through the
@@ -216,7 +242,7 @@ def test_device_lengths_out_of_range_are_reported():
 
 
 @pytest.mark.parametrize("B,H,Hkv,S,L,D,seed", [(40, 8, 2, 8200, 300, 64, 25), (24, 32, 4, 8192, 64, 128, 27),
-                                                 (21, 24, 4, 8192, 48, 128, 29)])
+                                                 (21, 24, 4, 8192, 48, 128, 29), (16, 24, 4, 8192, 64, 128, 31)])
 def test_split_schedule_ragged_against_oracle(B, H, Hkv, S, L, D, seed):
     """Units of the last partial wave cut into pieces and merged through the
     workspace (long units, few waves): ragged and empty blocks, blocks longer

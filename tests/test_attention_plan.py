@@ -63,11 +63,24 @@ def plan(units, n, P=SMS):
     return 0, 0, 0, 0
 
 
+def tile_shape(G, L):
+    """(Gs, T, hsplit, token tiles): a Q tile holds Gs of a KV head's G query
+    heads x T = BM // Gs tokens; Gs divides G and gives the fewest tiles per
+    (block, KV head), ties to the largest Gs."""
+    best = None
+    for gs in range(G, 0, -1):
+        if G % gs:
+            continue
+        T = BM // gs
+        tiles = (L + T - 1) // T
+        if best is None or (G // gs) * tiles < best[2] * best[3]:
+            best = (gs, T, G // gs, tiles)
+    return best
+
+
 def shape(B, H, Hkv, S, L):
-    G = H // Hkv
-    T = BM // G
-    tiles = (L + T - 1) // T
-    return tiles, tiles * Hkv * B, (S + BN - 1) // BN + (L + BN - 1) // BN, T
+    _, T, hsplit, tiles = tile_shape(H // Hkv, L)
+    return tiles, tiles * hsplit * Hkv * B, (S + BN - 1) // BN + (L + BN - 1) // BN, T
 
 
 def ws_bytes(split, pieces, D):
@@ -92,7 +105,26 @@ CASES = [
     ("gpu_split_d64", 40, 8, 2, 8200, 300, 64),
     ("gpu_split_d128", 24, 32, 4, 8192, 64, 128),
     ("gpu_split_g6", 21, 24, 4, 8192, 48, 128),
+    ("gpu_split_g6_L64", 16, 24, 4, 8192, 64, 128),
+    ("model_g6_L64", 16, 24, 4, 4096, 64, 128),
+    ("g12_L64", 37, 24, 2, 2048, 64, 128),
+    ("g10_L50", 5, 20, 2, 700, 50, 128),
 ]
+
+
+def test_tile_shape_fills_rows_when_the_group_does_not_divide_the_tile():
+    # G = 8 (and every power of two): the whole group, 16 tokens per tile
+    assert tile_shape(8, 64) == (8, 16, 1, 4)
+    assert tile_shape(8, 4096) == (8, 16, 1, 256)
+    # G = 6 at 64 tokens: 3 tiles of 2 heads x 64 tokens, not 4 of 6 heads x 21 tokens
+    assert tile_shape(6, 64) == (2, 64, 3, 1)
+    # G = 6 at 48 tokens: a tie (3 tiles either way) keeps the whole group
+    assert tile_shape(6, 48) == (6, 21, 1, 3)
+    # G = 12 at 64 tokens: 3 groups of 4 heads x 32 tokens (6 tiles; 7 for the whole group)
+    assert tile_shape(12, 64) == (4, 32, 3, 2)
+    # G = 10 at 50 tokens: 2 groups of 5 heads x 25 tokens (4 tiles, 125 of 128 rows; 5 for the group)
+    assert tile_shape(10, 50) == (5, 25, 2, 2)
+    assert tile_shape(3, 20) == (3, 42, 1, 1)
 
 
 @pytest.mark.parametrize("name,B,H,Hkv,S,L,D", CASES)
@@ -122,6 +154,7 @@ def test_pieces_cover_every_unit_once(name, B, H, Hkv, S, L, D):
     tiles, units, n_full, T = shape(B, H, Hkv, S, L)
     split, pieces, p0, rest = plan(units, n_full)
     whole = units - split
+    groups = units // (tiles * B)  # head groups: KV heads x hsplit
     n_s = (S + BN - 1) // BN
     slots = split * pieces
     rng = random.Random(hash(name) & 0xFFFF)
@@ -143,7 +176,7 @@ def test_pieces_cover_every_unit_once(name, B, H, Hkv, S, L, D):
                 e = p0 if k == 0 else min(n_full, a + rest)
                 assert 0 <= a < e <= n_full
                 assert 0 <= slot < slots and 0 <= r < split
-            tile, b = u % tiles, u // (tiles * Hkv)
+            tile, b = u % tiles, u // (tiles * groups)
             lb = min(max(lens[b], 0), L)
             counted[u] += e - a
             if tile * T >= lb:  # no real token: rows zeroed by the unit's first piece only
