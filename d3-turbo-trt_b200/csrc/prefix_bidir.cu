@@ -105,6 +105,7 @@ struct __align__(8) Bars {
   uint64_t drain;
   uint32_t tmem_slot;
   int abort_flag;
+  int last_arrival;  // split launch: this CTA's piece completed its unit
 };
 
 struct Params {
@@ -245,7 +246,98 @@ __device__ __forceinline__ float exp_row(const float* s, float sl2, float m, uin
   return ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
 }
 
-template <int D, int BN, int FP16>
+// Partial result of one piece of a split unit (fp32): O as [D/4][128 rows]
+// float4 (a warp's 32 rows form one coalesced 512-byte run), then the row's
+// reference max (log2 units, scale applied) m[128] and row sum l[128].
+template <int D>
+struct PartSlot {
+  static constexpr int FLOATS = BM * D + 2 * BM;
+};
+
+// This CTA's unit and iteration range [a, e) in a launch with split units
+// (1-D grid); slot >= 0 for a piece of a split unit.
+__device__ __forceinline__ void cta_work(const Params& p, int& u, int& a, int& e, int& slot) {
+  const int bid = blockIdx.x;
+  if (bid < p.whole_units) {
+    u = bid;
+    a = 0;
+    e = p.n_full;
+    slot = -1;
+    return;
+  }
+  const int q = bid - p.whole_units, k = q / p.split_units, r = q % p.split_units;
+  u = p.whole_units + r;
+  slot = q;
+  a = k == 0 ? 0 : p.piece0 + (k - 1) * p.piece_rest;
+  e = k == 0 ? p.piece0 : min(p.n_full, a + p.piece_rest);
+}
+
+// Adds this piece's iterations to its unit's count; true for the piece that
+// completes the unit (which then merges every piece and resets the count).
+__device__ __forceinline__ bool count_piece(const Params& p, int r, int add) {
+  __threadfence();  // the CTA's partial rows (ordered before by a CTA barrier) before the count
+  const int before = atomicAdd(&p.count[r], add);
+  const bool last = before + add == p.n_full;
+  if (last) {
+    p.count[r] = 0;  // ready for the next launch
+    __threadfence();
+  }
+  return last;
+}
+
+// Merge the pieces of split unit r for one row half (wg: columns [wg*D/2,
+// (wg+1)*D/2)) and store it: O = sum_k 2^(m_k - m) O_k, l = sum_k 2^(m_k - m) l_k
+// over the pieces with l_k > 0, output O / l (zero for padding rows).
+template <int D, int FP16>
+__device__ void merge_unit(const Params& p, int r, int b, int g, int tok0, int len_b, int wg, int row) {
+  constexpr int OH = D / 2;
+  const int tok = tok0 + row / p.G, h = row % p.G;
+  if (!(row < p.G * p.T && tok < p.L)) return;
+  const bool real = tok < len_b;
+  float mx = -INFINITY;
+  for (int k = 0; k < p.pieces; ++k) {
+    const float* ps = p.part + (int64_t)(k * p.split_units + r) * PartSlot<D>::FLOATS;
+    if (__ldcg(ps + BM * D + BM + row) > 0.f) mx = fmaxf(mx, __ldcg(ps + BM * D + row));
+  }
+  float acc[OH];
+#pragma unroll
+  for (int c = 0; c < OH; ++c) acc[c] = 0.f;
+  float lt = 0.f;
+  for (int k = 0; k < p.pieces; ++k) {
+    const float* ps = p.part + (int64_t)(k * p.split_units + r) * PartSlot<D>::FLOATS;
+    const float ls = __ldcg(ps + BM * D + BM + row);
+    if (!(ls > 0.f)) continue;
+    const float w = d3b::ex2_approx(__ldcg(ps + BM * D + row) - mx);
+    lt += ls * w;
+    const float4* os = reinterpret_cast<const float4*>(ps);
+#pragma unroll
+    for (int c = 0; c < OH; c += 4) {
+      const float4 v = __ldcg(os + (wg * OH + c) / 4 * BM + row);
+      acc[c] += v.x * w;
+      acc[c + 1] += v.y * w;
+      acc[c + 2] += v.z * w;
+      acc[c + 3] += v.w * w;
+    }
+  }
+  const float inv_l = 1.f / lt;
+  uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + (int64_t)b * p.out_sb +
+                                        (int64_t)(g * p.G + h) * p.out_sh + (int64_t)tok * p.out_sl + wg * OH);
+#pragma unroll
+  for (int c = 0; c < OH; c += 8) {
+    uint4 v;
+    v.x = real ? pack2<FP16>(acc[c] * inv_l, acc[c + 1] * inv_l) : 0u;
+    v.y = real ? pack2<FP16>(acc[c + 2] * inv_l, acc[c + 3] * inv_l) : 0u;
+    v.z = real ? pack2<FP16>(acc[c + 4] * inv_l, acc[c + 5] * inv_l) : 0u;
+    v.w = real ? pack2<FP16>(acc[c + 6] * inv_l, acc[c + 7] * inv_l) : 0u;
+    dst[c / 8] = v;
+  }
+}
+
+// SPLIT: a launch with split units (1-D grid, the unit or piece of cta_work;
+// a piece writes its partial to its slot and the piece that completes the
+// unit merges them). Without it the grid is (tile, head group, block), one
+// CTA per unit.
+template <int D, int BN, int FP16, bool SPLIT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     prefix_bidir_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapKs,
                         const __grid_constant__ CUtensorMap mapVs, const __grid_constant__ CUtensorMap mapKq,
@@ -254,16 +346,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   __shared__ Bars bars;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  int tile, g, b, unit = 0, a = 0, e = 0x7FFFFFFF, slot = -1;  // key tiles [a, e) of the unit
+  if constexpr (SPLIT) {
+    cta_work(p, unit, a, e, slot);
+    tile = unit % p.tiles;
+    g = (unit / p.tiles) % p.Hkv;
+    b = unit / (p.tiles * p.Hkv);
+  } else {
+    tile = blockIdx.x;
+    g = blockIdx.y;
+    b = blockIdx.z;
+  }
   const int kvh = g / p.hsplit;  // g: head group
   const int G = p.G, T = p.T;
   const int len_b = block_length(p, b);
   const int rows_used = G * T;
   const int tok0 = tile * T;
 
-  // ---- rows of this tile that need no attention: zero-fill and leave ----
+  // ---- rows of this tile that need no attention: zero-fill (once per unit) and leave ----
   if (tok0 >= len_b) {
-    if (warp >= 2) {
+    if (warp >= 2 && a == 0) {
       const int r = (warp & 3) * 32 + lane;
       const int tok = tok0 + r / G, h = r % G;
       if (r < rows_used && tok < p.L) {
@@ -282,7 +384,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   volatile int* abort_flag = &bars.abort_flag;
   const int n_s = (p.S + BN - 1) / BN;
   const int n_o = (len_b + BN - 1) / BN;
-  const int n = n_s + n_o;
+  const int n = max(0, min(e, n_s + n_o) - a);  // this CTA's key tiles: a, a + 1, ..
+  if constexpr (SPLIT) {
+    if (n == 0) {
+      // A piece of a split unit with no real key tile: an empty partial (l = 0),
+      // counted in like any other piece.
+      if (threadIdx.x < BM) {
+        float* ps = p.part + (int64_t)slot * PartSlot<D>::FLOATS;
+        ps[BM * D + threadIdx.x] = -INFINITY;
+        ps[BM * D + BM + threadIdx.x] = 0.f;
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) bars.last_arrival = count_piece(p, unit - p.whole_units, e - a);
+      __syncthreads();
+      if (bars.last_arrival) {
+        __threadfence();
+        for (int i = threadIdx.x; i < 2 * BM; i += NUM_THREADS)
+          merge_unit<D, FP16>(p, unit - p.whole_units, b, g, tok0, len_b, i / BM, i % BM);
+      }
+      return;
+    }
+  }
 
   if (threadIdx.x == 0) {
     d3b::mbar_init(&bars.q_full, 1);
@@ -338,16 +460,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (!d3b::mbar_wait(&bars.slot_empty[stage], phase ^ 1, abort_flag, p.err, kSiteSlotEmpty)) break;
         d3b::mbar_arrive_expect_tx(&bars.slot_full[stage], C::SLOT_BYTES);
         uint8_t* dst = sKV + stage * C::SLOT_BYTES;
-        if (j < n_s) {
+        const int kt = a + j;  // key tile of the unit
+        if (kt < n_s) {
           const CUtensorMap* m = is_v ? &mapVs : &mapKs;
 #pragma unroll
           for (int c = 0; c < C::NCH; ++c)
-            d3b::tma_load_3d(dst + c * C::SLOT_CHUNK, m, &bars.slot_full[stage], c * C::CH, j * BN, kvh);
+            d3b::tma_load_3d(dst + c * C::SLOT_CHUNK, m, &bars.slot_full[stage], c * C::CH, kt * BN, kvh);
         } else {
           const CUtensorMap* m = is_v ? &mapVq : &mapKq;
 #pragma unroll
           for (int c = 0; c < C::NCH; ++c)
-            d3b::tma_load_4d(dst + c * C::SLOT_CHUNK, m, &bars.slot_full[stage], c * C::CH, (j - n_s) * BN, kvh, b);
+            d3b::tma_load_4d(dst + c * C::SLOT_CHUNK, m, &bars.slot_full[stage], c * C::CH, (kt - n_s) * BN, kvh, b);
         }
         if (++stage == C::NSLOT) { stage = 0; phase ^= 1; }
       }
@@ -438,7 +561,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       d3b::tc_fence_before();
       d3b::mbar_arrive(&bars.s_free[sb]);
 
-      const int valid = j < n_s ? p.S - j * BN : len_b - (j - n_s) * BN;
+      const int kt = a + j;  // key tile of the unit
+      const int valid = kt < n_s ? p.S - kt * BN : len_b - (kt - n_s) * BN;
       if (valid < BN) {
 #pragma unroll
         for (int c = 0; c < BN; ++c)
@@ -495,12 +619,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const float inv_l = 1.f / l_sum;
       uint16_t* dst_row = static_cast<uint16_t*>(p.out) + (int64_t)b * p.out_sb + (int64_t)(g * G + h) * p.out_sh +
                           (int64_t)tok * p.out_sl;
+      // a piece of a split unit writes its raw O, m and l to its slot instead
+      float* ps = nullptr;
+      if constexpr (SPLIT) {
+        if (slot >= 0) ps = p.part + (int64_t)slot * PartSlot<D>::FLOATS;
+      }
+      if (ps) {
+        ps[BM * D + r] = m_ref;
+        ps[BM * D + BM + r] = l_sum;
+      }
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
         d3b::tmem_ld32(lane_addr + C::COL_O + c * 32, o);
         d3b::tmem_wait_ld();
-        if (in_tensor) {
+        if (ps) {
+          uint4* os = reinterpret_cast<uint4*>(ps);
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            os[(c * 32 + 4 * k) / 4 * BM + r] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+        } else if (in_tensor) {
           uint32_t w[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i)
@@ -508,6 +646,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint4* dst = reinterpret_cast<uint4*>(dst_row + c * 32);
 #pragma unroll
           for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        }
+      }
+    }
+    if constexpr (SPLIT) {
+      if (slot >= 0) {
+        // Piece of a split unit: count it in; the piece that completes the unit
+        // merges every piece's partial (both column halves of its row). Every
+        // softmax thread reaches this point exactly once (failed waits only skip
+        // work above), so the named barrier over the 128 softmax threads cannot
+        // be left waiting.
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (threadIdx.x == 64)
+          bars.last_arrival = *abort_flag ? 0 : (int)count_piece(p, unit - p.whole_units, e - a);
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (bars.last_arrival) {
+          __threadfence();
+          merge_unit<D, FP16>(p, unit - p.whole_units, b, g, tok0, len_b, 0, r);
+          merge_unit<D, FP16>(p, unit - p.whole_units, b, g, tok0, len_b, 1, r);
         }
       }
     }
@@ -636,93 +793,6 @@ __device__ __forceinline__ void scale_cols(uint32_t addr, float f) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
     d3b::tmem_st16(addr, o);
-  }
-}
-
-// Partial result of one piece of a split unit (fp32): O as [D/4][128 rows]
-// float4 (a warp's 32 rows form one coalesced 512-byte run), then the row's
-// reference max (log2 units, scale applied) m[128] and row sum l[128].
-template <int D>
-struct PartSlot {
-  static constexpr int FLOATS = BM * D + 2 * BM;
-};
-
-// This CTA's unit and iteration range [a, e) in a launch with split units
-// (1-D grid); slot >= 0 for a piece of a split unit.
-__device__ __forceinline__ void cta_work(const Params& p, int& u, int& a, int& e, int& slot) {
-  const int bid = blockIdx.x;
-  if (bid < p.whole_units) {
-    u = bid;
-    a = 0;
-    e = p.n_full;
-    slot = -1;
-    return;
-  }
-  const int q = bid - p.whole_units, k = q / p.split_units, r = q % p.split_units;
-  u = p.whole_units + r;
-  slot = q;
-  a = k == 0 ? 0 : p.piece0 + (k - 1) * p.piece_rest;
-  e = k == 0 ? p.piece0 : min(p.n_full, a + p.piece_rest);
-}
-
-// Adds this piece's iterations to its unit's count; true for the piece that
-// completes the unit (which then merges every piece and resets the count).
-__device__ __forceinline__ bool count_piece(const Params& p, int r, int add) {
-  __threadfence();  // the CTA's partial rows (ordered before by a CTA barrier) before the count
-  const int before = atomicAdd(&p.count[r], add);
-  const bool last = before + add == p.n_full;
-  if (last) {
-    p.count[r] = 0;  // ready for the next launch
-    __threadfence();
-  }
-  return last;
-}
-
-// Merge the pieces of split unit r for one row half (wg: columns [wg*D/2,
-// (wg+1)*D/2)) and store it: O = sum_k 2^(m_k - m) O_k, l = sum_k 2^(m_k - m) l_k
-// over the pieces with l_k > 0, output O / l (zero for padding rows).
-template <int D, int FP16>
-__device__ void merge_unit(const Params& p, int r, int b, int g, int tok0, int len_b, int wg, int row) {
-  constexpr int OH = D / 2;
-  const int tok = tok0 + row / p.G, h = row % p.G;
-  if (!(row < p.G * p.T && tok < p.L)) return;
-  const bool real = tok < len_b;
-  float mx = -INFINITY;
-  for (int k = 0; k < p.pieces; ++k) {
-    const float* ps = p.part + (int64_t)(k * p.split_units + r) * PartSlot<D>::FLOATS;
-    if (__ldcg(ps + BM * D + BM + row) > 0.f) mx = fmaxf(mx, __ldcg(ps + BM * D + row));
-  }
-  float acc[OH];
-#pragma unroll
-  for (int c = 0; c < OH; ++c) acc[c] = 0.f;
-  float lt = 0.f;
-  for (int k = 0; k < p.pieces; ++k) {
-    const float* ps = p.part + (int64_t)(k * p.split_units + r) * PartSlot<D>::FLOATS;
-    const float ls = __ldcg(ps + BM * D + BM + row);
-    if (!(ls > 0.f)) continue;
-    const float w = d3b::ex2_approx(__ldcg(ps + BM * D + row) - mx);
-    lt += ls * w;
-    const float4* os = reinterpret_cast<const float4*>(ps);
-#pragma unroll
-    for (int c = 0; c < OH; c += 4) {
-      const float4 v = __ldcg(os + (wg * OH + c) / 4 * BM + row);
-      acc[c] += v.x * w;
-      acc[c + 1] += v.y * w;
-      acc[c + 2] += v.z * w;
-      acc[c + 3] += v.w * w;
-    }
-  }
-  const float inv_l = 1.f / lt;
-  uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + (int64_t)b * p.out_sb +
-                                        (int64_t)(g * p.G + h) * p.out_sh + (int64_t)tok * p.out_sl + wg * OH);
-#pragma unroll
-  for (int c = 0; c < OH; c += 8) {
-    uint4 v;
-    v.x = real ? pack2<FP16>(acc[c] * inv_l, acc[c + 1] * inv_l) : 0u;
-    v.y = real ? pack2<FP16>(acc[c + 2] * inv_l, acc[c + 3] * inv_l) : 0u;
-    v.z = real ? pack2<FP16>(acc[c + 4] * inv_l, acc[c + 5] * inv_l) : 0u;
-    v.w = real ? pack2<FP16>(acc[c + 6] * inv_l, acc[c + 7] * inv_l) : 0u;
-    dst[c / 8] = v;
   }
 }
 
@@ -1685,26 +1755,34 @@ int launch_pair(const CUtensorMap* maps, const Params& prm, int pair_units, cuda
   return d3b_host::check_launch();
 }
 
-template <int D, int BN, int FP16>
-int launch(const CUtensorMap* maps, const Params& prm, dim3 grid, cudaStream_t stream) {
+template <int D, int BN, int FP16, bool SPLIT>
+int launch_as(const CUtensorMap* maps, const Params& prm, dim3 grid, cudaStream_t stream) {
   using C = Cfg<D, BN>;
   static int attr_set[64] = {0};
   const int dev = d3b_host::current_device();
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(prefix_bidir_kernel<D, BN, FP16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(prefix_bidir_kernel<D, BN, FP16, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::SMEM_BYTES) != cudaSuccess)
       return D3B_ECUDA;
     attr_set[dev] = 1;
   }
-  prefix_bidir_kernel<D, BN, FP16><<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2], maps[3],
-                                                                                 maps[4], prm);
+  prefix_bidir_kernel<D, BN, FP16, SPLIT><<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(maps[0], maps[1], maps[2],
+                                                                                        maps[3], maps[4], prm);
   return d3b_host::check_launch();
+}
+
+// grid: (tiles, head groups, blocks) one CTA per unit; grid_split: the 1-D
+// grid of a launch with split units
+template <int D, int BN, int FP16>
+int launch(const CUtensorMap* maps, const Params& prm, dim3 grid, dim3 grid_split, cudaStream_t stream) {
+  return prm.split_units ? launch_as<D, BN, FP16, true>(maps, prm, grid_split, stream)
+                         : launch_as<D, BN, FP16, false>(maps, prm, grid, stream);
 }
 
 template <int FP16>
 int dispatch(int D, const CUtensorMap* maps, const Params& prm, dim3 grid, dim3 grid_dual, cudaStream_t s) {
-  // D = 256 (O needs 256 TMEM columns): one tile per CTA, one CTA per SM.
-  if (D == 256) return launch<256, 64, FP16>(maps, prm, grid, s);
+  // D = 256 (O needs 256 TMEM columns): one unit (or piece of a unit) per CTA, one CTA per SM.
+  if (D == 256) return launch<256, 64, FP16>(maps, prm, grid, grid_dual, s);
   // D <= 128: one unit (or piece of a unit) per CTA, one CTA per SM, two MMA-issuing threads.
   switch (D) {
     case 32: return launch_dual<32, FP16>(maps, prm, grid_dual, s);
@@ -1951,7 +2029,7 @@ static int prefix_bidir_impl(const void* q, const int64_t* q_strides, const void
   prm.part = nullptr;
   prm.count = nullptr;
   int64_t ctas = units;
-  if (D <= 128 && workspace) {
+  if (workspace) {
     const TailPlan t = cached_plan((int)units, (int)n_full, d3b_host::num_sms(d3b_host::current_device()));
     if (t.split_units) {
       size_t count_bytes = 0;
@@ -1989,10 +2067,11 @@ static int prefix_bidir_impl(const void* q, const int64_t* q_strides, const void
 
 extern "C" size_t d3b_prefix_bidir_workspace_size(int B, int H, int Hkv, int S, int L, int D) {
   if (B <= 0 || H <= 0 || Hkv <= 0 || S < 0 || L <= 0 || H % Hkv || H / Hkv > BM) return 0;
-  if (D != 32 && D != 64 && D != 128) return 0;  // D = 256 runs without one
+  if (D != 32 && D != 64 && D != 128 && D != 256) return 0;
+  const int BN = D == 256 ? 64 : 128;
   const TileShape shape = tile_shape(H / Hkv, L);
   const int64_t units = shape.tiles * shape.hsplit * Hkv * B;
-  const int64_t n_full = (int64_t)(S + 127) / 128 + (L + 127) / 128;
+  const int64_t n_full = (int64_t)(S + BN - 1) / BN + (L + BN - 1) / BN;
   if (units > 0x7FFFFFFF || n_full > 0x7FFFFFFF) return 0;
   const TailPlan t = cached_plan((int)units, (int)n_full, d3b_host::num_sms(d3b_host::current_device()));
   return t.split_units ? plan_bytes(t, D, nullptr) : 0;

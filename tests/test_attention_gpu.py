@@ -191,6 +191,31 @@ def test_head_dim_256_at_4k_state():
     assert _lib.device_error() == 0
 
 
+def test_split_d256_pieces_without_real_keys():
+    """A D = 256 split launch (64-key tiles) whose tail units hold a few real
+    tokens of a long block: their last piece starts past the block's last real
+    key tile and writes an empty partial (l = 0), the middle piece has a few
+    key tiles. A first launch with full blocks leaves every partial slot
+    filled, so a piece that did not write its slot would merge stale rows."""
+    B, H, Hkv, S, L, D = 3, 2, 1, 64, 4096, 256
+    assert int(_lib.lib().d3b_prefix_bidir_workspace_size(B, H, Hkv, S, L, D)) > 0
+    g = torch.Generator().manual_seed(36)
+    q = _rand((B, H, L, D), g)
+    ks, vs = _rand((Hkv, S, D), g), _rand((Hkv, S, D), g)
+    kq, vq = _rand((B, Hkv, L, D), g), _rand((B, Hkv, L, D), g)
+    args = (q.to(DEV), ks.to(DEV), vs.to(DEV), kq.to(DEV), vq.to(DEV))
+    pb.prefix_bidir_attention(*args, [L] * B, scale=D**-0.5)
+    lens = [L, 1000, 1500]
+    out = pb.prefix_bidir_attention(*args, lens, scale=D**-0.5)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    ref = oattn.questions(q, ks, vs, kq, vq, lens, D**-0.5, dtype=torch.float32)
+    got = out.float().cpu()
+    assert float((got - ref).abs().max()) <= TOL
+    for b, n in enumerate(lens):
+        assert torch.all(got[b, :, n:] == 0)
+
+
 @pytest.mark.parametrize("B,H,Hkv,S,L,D,seed", [(16, 24, 4, 1000, 64, 256, 41), (37, 24, 2, 500, 64, 128, 42),
                                                  (9, 24, 4, 300, 64, 64, 43), (5, 20, 2, 700, 50, 128, 44),
                                                  (4, 20, 2, 300, 50, 256, 45)])
@@ -242,11 +267,13 @@ def test_device_lengths_out_of_range_are_reported():
 
 
 @pytest.mark.parametrize("B,H,Hkv,S,L,D,seed", [(40, 8, 2, 8200, 300, 64, 25), (24, 32, 4, 8192, 64, 128, 27),
-                                                 (21, 24, 4, 8192, 48, 128, 29), (16, 24, 4, 8192, 64, 128, 31)])
+                                                 (21, 24, 4, 8192, 48, 128, 29), (16, 24, 4, 8192, 64, 128, 31),
+                                                 (16, 24, 4, 4096, 64, 256, 35)])
 def test_split_schedule_ragged_against_oracle(B, H, Hkv, S, L, D, seed):
     """Units of the last partial wave cut into pieces and merged through the
     workspace (long units, few waves): ragged and empty blocks, blocks longer
-    than one key tile, head_dim 64, a GQA group of 6. Also checked: the
+    than one key tile, head_dim 64, a GQA group of 6, and the D = 256 kernel at
+    the model's own attention shape (24/4 heads). Also checked: the
     workspace's counters are zero again afterwards, a second launch gives the
     same bits, and the entry point without a workspace (one CTA per unit)
     agrees with the oracle too."""

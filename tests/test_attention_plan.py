@@ -22,7 +22,12 @@ import pytest
 
 from d3_turbo_trt_b200 import _lib
 
-BM = BN = 128
+BM = 128
+
+
+def key_tile(D):
+    """Keys per key tile: 64 for head_dim 256 (O takes 256 TMEM columns), else 128."""
+    return 64 if D == 256 else 128
 SMS = 148
 CTA_COST = 12.0
 MIN_SPLIT_TILES = 64
@@ -78,8 +83,9 @@ def tile_shape(G, L):
     return best
 
 
-def shape(B, H, Hkv, S, L):
+def shape(B, H, Hkv, S, L, D=128):
     _, T, hsplit, tiles = tile_shape(H // Hkv, L)
+    BN = key_tile(D)
     return tiles, tiles * hsplit * Hkv * B, (S + BN - 1) // BN + (L + BN - 1) // BN, T
 
 
@@ -109,6 +115,9 @@ CASES = [
     ("model_g6_L64", 16, 24, 4, 4096, 64, 128),
     ("g12_L64", 37, 24, 2, 2048, 64, 128),
     ("g10_L50", 5, 20, 2, 700, 50, 128),
+    ("model_d256", 16, 24, 4, 4096, 64, 256),
+    ("d256_g1", 40, 4, 4, 3000, 40, 256),
+    ("d256_ragged_L300", 3, 24, 4, 2000, 300, 256),
 ]
 
 
@@ -129,7 +138,7 @@ def test_tile_shape_fills_rows_when_the_group_does_not_divide_the_tile():
 
 @pytest.mark.parametrize("name,B,H,Hkv,S,L,D", CASES)
 def test_workspace_size_matches_plan(name, B, H, Hkv, S, L, D):
-    _, units, n, _ = shape(B, H, Hkv, S, L)
+    _, units, n, _ = shape(B, H, Hkv, S, L, D)
     split, pieces, _, _ = plan(units, n)
     assert int(_lib.lib().d3b_prefix_bidir_workspace_size(B, H, Hkv, S, L, D)) == ws_bytes(split, pieces, D)
 
@@ -151,7 +160,8 @@ def test_long_units_are_cut_short_ones_are_not():
 
 @pytest.mark.parametrize("name,B,H,Hkv,S,L,D", CASES)
 def test_pieces_cover_every_unit_once(name, B, H, Hkv, S, L, D):
-    tiles, units, n_full, T = shape(B, H, Hkv, S, L)
+    tiles, units, n_full, T = shape(B, H, Hkv, S, L, D)
+    BN = key_tile(D)
     split, pieces, p0, rest = plan(units, n_full)
     whole = units - split
     groups = units // (tiles * B)  # head groups: KV heads x hsplit
