@@ -185,8 +185,12 @@ class QuestionPipeline:
         self.count += 1
         lens = block_offsets(lengths, self.device)
         with torch.cuda.stream(self.copy_in):
-            if slot.used:  # this slot's buffers are free once its previous output has left the GPU
-                self.copy_in.wait_event(slot.copied_out)
+            # The slot's input buffers are free once its previous pass has run, its
+            # output buffer once that pass's output has left the GPU: the next
+            # batch's copy in does not queue behind the previous copy out, so
+            # host-to-device and device-to-host copies overlap.
+            if slot.used:
+                self.copy_in.wait_event(slot.computed)
             dq = self._buf(slot, "q", q)
             dkq = self._buf(slot, "kq", k_q)
             dvq = self._buf(slot, "vq", v_q)
@@ -197,6 +201,8 @@ class QuestionPipeline:
             slot.copied_in.record(self.copy_in)
         with torch.cuda.stream(self.compute):
             self.compute.wait_event(slot.copied_in)
+            if slot.used:
+                self.compute.wait_event(slot.copied_out)
             if self.before_compute is not None:
                 self.before_compute()
             prefix_bidir_attention(dq, self.k_state, self.v_state, dkq, dvq, lens, scale=self.scale, out=dout)

@@ -6,7 +6,9 @@ Meant as the target of an ``ncu`` capture (one kernel, a few launches, a small
 device footprint) and as a quick device-time probe: it prints the median
 CUDA-event time per launch and the algorithmic work per launch. Configs follow
 cfg3a (4096-token state + 16 x 64-token blocks), cfg3b (16384 +
-255 x 48), cfg5 (16384 + 255 x 64 on one GPU: the CTA-pair attention kernel), state4k (the state pass of cfg3a), cfg2 (W8A8 4096 x 5120 x 13824),
+255 x 48), cfg5 (16384 + 255 x 64 on one GPU: the CTA-pair attention kernel),
+model_d256 (cfg3a's blocks and state at 24/4 heads, head_dim 256: the D = 256
+kernel's split launch), state4k (the state pass of cfg3a), cfg2 (W8A8 4096 x 5120 x 13824),
 cfg4 (readout 255 x 5120 x 255; snapshot: the 64-layer state snapshot at a
 4096-token state, packed by one copy launch; gdn: one GDN layer's question pass,
 255 blocks x 48 tokens x 48 value heads; gdn_state: one GDN layer's state pass,
@@ -34,6 +36,8 @@ ATTN = {
     "cfg3b": dict(B=255, H=32, Hkv=4, L=48, D=128, S=16384),
     "cfg1": dict(B=8, H=8, Hkv=2, L=32, D=64, S=512),
     "cfg5": dict(B=255, H=32, Hkv=4, L=64, D=128, S=16384),
+    # config 3a's blocks and state at the model's own attention shape (head_dim 256)
+    "model_d256": dict(B=16, H=24, Hkv=4, L=64, D=256, S=4096),
 }
 
 
