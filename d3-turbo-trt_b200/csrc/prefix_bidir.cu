@@ -22,10 +22,11 @@
 //
 // Two kernels share this work unit, the key schedule and the softmax; both run
 // one CTA per SM with S and P double-buffered in TMEM:
-//   D <= 128  prefix_bidir_dual_kernel: QK^T and PV issued by two threads,
-//             two softmax warpgroups on alternating key tiles.
-//   D == 256  prefix_bidir_kernel: one MMA-issuing thread, one softmax
-//             warpgroup, 64-key tiles (O alone takes 256 TMEM columns).
+//   prefix_bidir_dual_kernel (every D): QK^T and PV issued by two threads,
+//             two softmax warpgroups on alternating key tiles; 128-key tiles,
+//             64-key tiles for D = 256 (O alone takes 256 TMEM columns).
+//   prefix_bidir_kernel (D = 256 with D3B_ATTN_D256=single): one
+//             MMA-issuing thread, one softmax warpgroup, 64-key tiles.
 // Both use one thread per Q row for the softmax: tcgen05.ld of the S row,
 // online softmax in the log2 domain, P as bf16/f16 written back to TMEM for
 // the TS-form PV MMA (V read MN-major from shared memory), O rescaled in TMEM
@@ -47,6 +48,7 @@
 #include <map>
 #include <mutex>
 #include <queue>
+#include <string>
 #include <tuple>
 #include <vector>
 
@@ -723,7 +725,7 @@ constexpr int DU_THREADS = 384;  // 8 softmax warps, K producer, QK issuer, PV i
 
 template <int D>
 struct CfgDual {
-  static constexpr int BN = 128;
+  static constexpr int BN = D == 256 ? 64 : 128;  // keys per tile (D = 256: O takes 256 TMEM columns)
   static constexpr int CH = D >= 64 ? 64 : D;
   static constexpr int ROWB = CH * 2;
   static constexpr int NCH = D / CH;
@@ -740,11 +742,11 @@ struct CfgDual {
   static constexpr int NV = NSLOT_RAW - NK > 8 ? 8 : NSLOT_RAW - NK;  // V ring slots
   static constexpr int SMEM_BYTES = Q_BYTES + (NK + NV) * SLOT_BYTES + 1024;
   static constexpr int COL_O = 0;
-  static constexpr int COL_S = 128;  // + b * BN
-  static constexpr int COL_P = 384;  // + b * BN / 2
-  static constexpr int OH = D / 2;   // O columns per softmax half
+  static constexpr int COL_S = D == 256 ? 256 : 128;  // + b * BN
+  static constexpr int COL_P = COL_S + 2 * BN;        // + b * BN / 2 (384 either way)
+  static constexpr int OH = D / 2;                    // O columns per softmax half
   static constexpr uint32_t TMEM_COLS = 512;
-  static_assert(D <= 128, "TMEM budget");
+  static_assert(D <= COL_S && COL_P + BN <= (int)TMEM_COLS, "TMEM budget");
   static_assert(NK >= 2 && NV >= 2, "smem budget");
 };
 
@@ -808,7 +810,7 @@ struct Work {
 // c, c + gridDim.x, ... (all of a launch's units have the same number of key
 // tiles up to the blocks' lengths, so a static round robin balances them).
 // With SPLIT each CTA has one item, the unit or piece of cta_work.
-template <bool SPLIT>
+template <bool SPLIT, int BN>
 __device__ __forceinline__ bool work_item(const Params& p, int i, int n_s, Work& w) {
   int e;
   if constexpr (SPLIT) {
@@ -827,7 +829,7 @@ __device__ __forceinline__ bool work_item(const Params& p, int i, int n_s, Work&
   w.b = w.unit / (p.tiles * p.Hkv);
   w.len_b = block_length(p, w.b);
   w.tok0 = tile * p.T;
-  w.n = w.tok0 >= w.len_b ? 0 : max(0, min(e, n_s + (w.len_b + 127) / 128) - w.a);
+  w.n = w.tok0 >= w.len_b ? 0 : max(0, min(e, n_s + (w.len_b + BN - 1) / BN) - w.a);
   return true;
 }
 
@@ -847,7 +849,6 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
                              const __grid_constant__ CUtensorMap mapVq, const Params p) {
   using C = CfgDual<D>;
   constexpr int BN = C::BN;
-  static_assert(BN == 128, "work_item counts own tiles of 128 keys");
   extern __shared__ uint8_t smem_raw[];
   __shared__ BarsDual bars;
   __shared__ float mref_s[2][BM];   // reference max of the last tile of each group, per row
@@ -967,7 +968,7 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
       uint32_t ph = 0;
       bool ok = true;
       Work w;
-      for (int i = 0; ok && work_item<SPLIT>(p, i, n_s, w); ++i) {
+      for (int i = 0; ok && work_item<SPLIT, BN>(p, i, n_s, w); ++i) {
         if (w.n == 0) continue;
         if (!is_v) {
           // Q of this unit: the previous unit's QK^T MMAs have all completed
@@ -1007,7 +1008,7 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
       bool ok = true;
       int jg = 0, ie = 0;
       Work w;
-      for (int i = 0; ok && work_item<SPLIT>(p, i, n_s, w); ++i) {
+      for (int i = 0; ok && work_item<SPLIT, BN>(p, i, n_s, w); ++i) {
         if (w.n == 0) continue;
         if (!(ok = d3b::mbar_wait(&bars.q_full, (uint32_t)ie & 1, abort_flag, p.err, kSiteDuQ))) break;
         for (int j = 0; j < w.n; ++j, ++jg) {
@@ -1052,7 +1053,7 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
       bool ok = true;
       int jg = 0, ie = 0;
       Work w;
-      for (int i = 0; ok && work_item<SPLIT>(p, i, n_s, w); ++i) {
+      for (int i = 0; ok && work_item<SPLIT, BN>(p, i, n_s, w); ++i) {
         if (w.n == 0) continue;
         for (int j = 0; j < w.n; ++j, ++jg) {
           const int sb = jg & 1;
@@ -1110,7 +1111,7 @@ __global__ void __launch_bounds__(DU_THREADS, 1)
     bool ok = true;
     int jg = 0, ie = 0;
     Work w;
-    for (int i = 0; ok && work_item<SPLIT>(p, i, n_s, w); ++i) {
+    for (int i = 0; ok && work_item<SPLIT, BN>(p, i, n_s, w); ++i) {
       if (w.n == 0) {
         if (wg == 0) zero_tile_rows<D>(p, w.b, w.g, w.tok0, quarter, lane);
         continue;
@@ -1779,12 +1780,22 @@ int launch(const CUtensorMap* maps, const Params& prm, dim3 grid, dim3 grid_spli
                          : launch_as<D, BN, FP16, false>(maps, prm, grid, stream);
 }
 
+// D = 256 runs on the two-issuer kernel (64-key tiles); D3B_ATTN_D256=single in
+// the environment selects the one-issuer kernel instead (read once per process).
+bool d256_single_issuer() {
+  static const bool on = [] {
+    const char* v = std::getenv("D3B_ATTN_D256");
+    return v && std::string(v) == "single";
+  }();
+  return on;
+}
+
 template <int FP16>
 int dispatch(int D, const CUtensorMap* maps, const Params& prm, dim3 grid, dim3 grid_dual, cudaStream_t s) {
-  // D = 256 (O needs 256 TMEM columns): one unit (or piece of a unit) per CTA, one CTA per SM.
-  if (D == 256) return launch<256, 64, FP16>(maps, prm, grid, grid_dual, s);
-  // D <= 128: one unit (or piece of a unit) per CTA, one CTA per SM, two MMA-issuing threads.
+  // one unit (or piece of a unit) per CTA, one CTA per SM
+  if (D == 256 && d256_single_issuer()) return launch<256, 64, FP16>(maps, prm, grid, grid_dual, s);
   switch (D) {
+    case 256: return launch_dual<256, FP16>(maps, prm, grid_dual, s);
     case 32: return launch_dual<32, FP16>(maps, prm, grid_dual, s);
     case 64: return launch_dual<64, FP16>(maps, prm, grid_dual, s);
     case 128: return launch_dual<128, FP16>(maps, prm, grid_dual, s);

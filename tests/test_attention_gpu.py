@@ -191,6 +191,46 @@ def test_head_dim_256_at_4k_state():
     assert _lib.device_error() == 0
 
 
+def test_d256_single_issuer_kernel_in_a_subprocess():
+    """head_dim 256 runs on the two-issuer kernel; D3B_ATTN_D256=single (read
+    once per process) selects the one-issuer kernel. Both, in a fresh process
+    each, against the oracle on a ragged split launch and a whole-unit one."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    code = (
+        "import sys, torch\n"
+        f"sys.path[:0] = [{str(root)!r}, {str(root / 'tests')!r}]\n"
+        "import conftest\n"
+        "from oracle import attention as oattn\n"
+        "from d3_turbo_trt_b200 import _lib\n"
+        "from d3_turbo_trt_b200.kernels import prefix_bidir as pb\n"
+        "worst = 0.0\n"
+        "for B, H, Hkv, S, L, lens in ((16, 24, 4, 4096, 64, None), (5, 20, 2, 300, 50, [50, 1, 0, 33, 49])):\n"
+        "    g = torch.Generator().manual_seed(B)\n"
+        "    q = torch.randn(B, L, H, 256, generator=g).to(torch.bfloat16).permute(0, 2, 1, 3)\n"
+        "    ks = torch.randn(S, Hkv, 256, generator=g).to(torch.bfloat16).permute(1, 0, 2)\n"
+        "    vs = torch.randn(S, Hkv, 256, generator=g).to(torch.bfloat16).permute(1, 0, 2)\n"
+        "    kq = torch.randn(B, L, Hkv, 256, generator=g).to(torch.bfloat16).permute(0, 2, 1, 3)\n"
+        "    vq = torch.randn(B, L, Hkv, 256, generator=g).to(torch.bfloat16).permute(0, 2, 1, 3)\n"
+        "    lens = lens or [L] * B\n"
+        "    out = pb.prefix_bidir_attention(*(t.cuda() for t in (q, ks, vs, kq, vq)), lens, scale=256 ** -0.5)\n"
+        "    torch.cuda.synchronize()\n"
+        "    assert _lib.device_error() == 0\n"
+        "    ref = oattn.questions(q, ks, vs, kq, vq, lens, 256 ** -0.5, dtype=torch.float32)\n"
+        "    worst = max(worst, float((out.float().cpu() - ref).abs().max()))\n"
+        "print(worst)\n"
+    )
+    for mode in ("single", "dual"):
+        env = dict(os.environ, D3B_ATTN_D256=mode)
+        res = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
+        assert res.returncode == 0, res.stderr[-2000:]
+        assert float(res.stdout.strip().splitlines()[-1]) <= TOL, mode
+
+
 def test_split_d256_pieces_without_real_keys():
     """A D = 256 split launch (64-key tiles) whose tail units hold a few real
     tokens of a long block: their last piece starts past the block's last real
