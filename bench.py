@@ -183,6 +183,29 @@ def make_question_inputs(cfg, seed, device, with_state=True):
     return out
 
 
+def act_quant_steady(x, mode, stream, copies=6, launches=24):
+    """Per-launch device time (ms) of config 2's act quant in a steady stream of
+    launches: `copies` inputs of x's shape (together larger than L2) used in
+    turn, so no launch finds its input in L2, timed back to back between two
+    events (no flush kernels in between, the launch cost overlaps the previous
+    launch as it does in the backbone)."""
+    from d3_turbo_trt_b200.model import quant
+    xs = [x.clone() for _ in range(copies)]
+    for i in range(2 * copies):
+        quant.quantize_rows(xs[i % copies], mode)
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int(2e6 * 2))
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(launches):
+        quant.quantize_rows(xs[i % copies], mode)
+    b.record(stream)
+    torch.cuda.synchronize()
+    del xs
+    return a.elapsed_time(b) / launches
+
+
 def time_steps(fn, steps, warmup, stream, flush, host_bound=False):
     """Per-step device time (ms) of fn() with an L2 flush before every step.
 
@@ -789,12 +812,17 @@ def secondary(dev, stream, flush, peaks, quant, pb, d3b):
         tg = statistics.median(time_steps(lambda: quant.scaled_mm(qa, layer.weight, sa, layer.weight_scale,
                                                                    out_dtype=torch.bfloat16), 10, 3, stream, flush))
         tq = statistics.median(time_steps(lambda: quant.quantize_rows(x, mode), 10, 3, stream, flush))
+        tq_run = act_quant_steady(x, mode, stream)
         tl = statistics.median(time_steps(lambda: layer(x), 10, 3, stream, flush))
         qbytes = M * K * 2 + M * K + M * 4
         res[f"w8a8_{mode}_cfg2"] = {
             "gemm_ms": tg, "gemm_tflops": gemm_flops / tg / 1e9, "frac_dense_peak": gemm_flops / tg / 1e9 / fp8_peak,
             "frac_spec_4500": gemm_flops / tg / 1e9 / FP8_SPEC_TFLOPS,
             "act_quant_ms": tq, "act_quant_gbs": qbytes / tq / 1e6, "act_quant_frac_hbm": qbytes / tq / 1e6 / peaks["hbm_gbs"],
+            "act_quant_steady_ms": tq_run, "act_quant_steady_gbs": qbytes / tq_run / 1e6,
+            "act_quant_steady_frac_hbm": qbytes / tq_run / 1e6 / peaks["hbm_gbs"],
+            "act_quant_steady_note": "launches back to back over 6 rotating inputs (252 MB > L2), no flush; "
+                                     "act_quant_ms is one launch after an L2 flush, event-timed alone",
             "quant_linear_ms": tl}
         if mode == "fp8":
             ts = statistics.median(time_steps(lambda: torch._scaled_mm(
