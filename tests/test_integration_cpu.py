@@ -15,7 +15,8 @@ from pathlib import Path
 
 import pytest
 
-REF = Path(os.environ.get("D3_REFERENCE_DIR", "/root/reference"))
+# the reference checkout: D3_REFERENCE_DIR, else a `reference` folder beside this repository
+REF = Path(os.environ.get("D3_REFERENCE_DIR", Path(__file__).resolve().parents[2] / "reference"))
 
 
 @pytest.fixture
