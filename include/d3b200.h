@@ -147,7 +147,10 @@ D3B_API int d3b_w8a8_gemm(const void* qa, const void* qw, const float* sa, const
  * H % Hkv == 0 and H/Hkv <= 128. Strides must be multiples of 8 elements.
  * The kernel reads `lengths` itself: an entry outside [0, L] is clamped and
  * sets the device error word (site 2010, see d3b_device_error).
- * Work unit: one (block, kv head, 128-row Q tile); one CTA per unit.
+ * Work unit: one (block, head group, 128-row Q tile), one CTA per SM at a
+ * time. A head group is the kv head's whole GQA group, or, when the group does
+ * not divide 128 rows and fewer tiles result, a divisor of it (G = 6 at 64
+ * tokens: 3 groups of 2 heads x 64 tokens).
  */
 D3B_API int d3b_prefix_bidir(const void* q, const int64_t* q_strides, const void* k_state, const void* v_state,
                      const int64_t* kv_strides, const void* k_q, const void* v_q, const int64_t* kq_strides,
@@ -157,7 +160,7 @@ D3B_API int d3b_prefix_bidir(const void* q, const int64_t* q_strides, const void
 /*
  * Bytes of workspace d3b_prefix_bidir_ws uses for this shape on the current
  * device; 0 when the shape gains nothing from one (units fill whole waves of
- * the SMs, or D == 256).
+ * the SMs, or are too short to cut).
  */
 D3B_API size_t d3b_prefix_bidir_workspace_size(int B, int H, int Hkv, int S, int L, int D);
 
