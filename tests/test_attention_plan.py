@@ -1,7 +1,9 @@
 """Host logic of the attention kernel's launch plan (no GPU needed).
 
-d3b_prefix_bidir_ws runs one CTA per unit (block, kv head, 128-row Q tile) and
-cuts the units of the last partial wave into pieces along their key tiles. The
+d3b_prefix_bidir_ws runs one CTA per unit (block, head group, 128-row Q tile:
+a kv head's whole GQA group, or a divisor of it when that gives fewer tiles)
+and cuts the units of the last partial wave into pieces along their key tiles
+(128 keys each, 64 for head_dim 256). The
 piece that completes a unit merges the partial results through the workspace.
 This file restates the plan (a greedy-dispatch model of the SMs) and checks
 that the library's workspace size agrees with it. It then simulates the pieces
