@@ -206,3 +206,23 @@ def test_pieces_cover_every_unit_once(name, B, H, Hkv, S, L, D):
         assert counted == [n_full] * units
         assert writes == [1] * units
         assert not any(count)
+
+
+def test_workspace_size_matches_plan_on_random_shapes():
+    """The library's tile shape and split plan against this file's restatement
+    on 300 seeded shapes: GQA groups 1..16 (dividing 128 or not), every head
+    dim, short and long blocks, with and without a state."""
+    rng = random.Random(20261202)
+    for _ in range(300):
+        Hkv = rng.choice([1, 2, 4, 8])
+        G = rng.randint(1, 16)
+        B = rng.randint(1, 300)
+        L = rng.choice([rng.randint(1, 64), rng.randint(65, 600)])
+        S = rng.choice([0, rng.randint(1, 20000)])
+        D = rng.choice([32, 64, 128, 256])
+        _, units, n, _ = shape(B, G * Hkv, Hkv, S, L, D)
+        if units > 0x7FFFFFFF:
+            continue
+        split, pieces, _, _ = plan(units, n)
+        got = int(_lib.lib().d3b_prefix_bidir_workspace_size(B, G * Hkv, Hkv, S, L, D))
+        assert got == ws_bytes(split, pieces, D), (B, G * Hkv, Hkv, S, L, D)
