@@ -2059,7 +2059,9 @@ static int prefix_bidir_impl(const void* q, const int64_t* q_strides, const void
   if (ctas > 0x7FFFFFFF) return D3B_EINVAL;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int64_t sms = d3b_host::num_sms(d3b_host::current_device());
-  if (D == 128 && tiles % 2 == 0 && !prm.split_units && units >= kPairMinWaves * sms && pair_kernel_enabled()) {
+  // (whole GQA groups only: the pair kernel with split head groups has not been measured)
+  if (D == 128 && tiles % 2 == 0 && shape.hsplit == 1 && !prm.split_units && units >= kPairMinWaves * sms &&
+      pair_kernel_enabled()) {
     // CTA pairs: both Q tiles of a pair unit share every key and value tile
     prm.whole_units = (int)(units / 2);
     prm.part = nullptr;
